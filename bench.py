@@ -1,0 +1,442 @@
+"""MSDA forward+backward benchmark on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config decoder]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --impl reference ...   # the reference's CPU implementation
+
+A step is one forward + backward of the multi-scale deformable attention op
+over one batch of the configured operating point (default: the
+Deformable-DETR decoder preset, B=4 Q=300 M=8 D=32 L=4 K=4, bf16). With N
+ranks every rank runs its own batch (weak scaling over the batch axis; the op
+path has no collective) and NCCL only carries the timing reduction.
+
+Reported (one JSON line on rank 0):
+  value      queries/s over all ranks (B*Q*N / device time), inputs resident
+             in HBM; device time = CUDA-event time of CUDA-graph replays of
+             the forward and backward launches, L2 flushed before every step,
+             max over ranks.
+  e2e        the same metric through the public op with pinned HOST buffers:
+             host->device copies of the inputs and device->host copies of the
+             output and the three gradients inside the timed region.
+  roofline   the backward (dominant) launch: algorithmic bytes / event time
+             against the measured HBM copy bandwidth.
+  cpu_baseline  the reference's CPU implementation (grid_sample forward +
+             autograd backward, restated in oracle/msda_oracle.py) on the
+             host cores, rank 0 at N=1.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "msda-triton_b200"))
+
+from msda_triton_b200 import multi_scale_deformable_attention, presets  # noqa: E402
+from msda_triton_b200 import ops as msda_ops  # noqa: E402
+
+L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "MSDA fwd+bwd µs, queries/s & % HBM roofline, bf16 decoder/encoder, 1–8 B200"
+NOMINAL_HBM_GBS = 8000.0
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic byte model (labs/solutions/lab06.py:121-129 for the forward,
+# extended to the backward): every gathered corner row counts.
+# ---------------------------------------------------------------------------
+def algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass):
+    ns = B * Q * M * L * K
+    fwd = ns * 4 * D * e + ns * 3 * e + B * Q * M * D * e
+    bwd = (ns * 4 * D * e + ns * 4 * D * e_acc + ns * 6 * e + B * Q * M * D * e
+           + B * S * M * D * e_acc)
+    if cast_pass:
+        bwd += B * S * M * D * (e_acc + e)
+    return fwd, bwd
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML reads only; no setting is changed)
+# ---------------------------------------------------------------------------
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples: list[tuple[int, int, int]] = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid = None
+            try:
+                props = torch.cuda.get_device_properties(device_index)
+                uuid = "GPU-" + str(props.uuid)
+            except Exception:  # noqa: BLE001
+                pass
+            self._h = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid
+                       else pynvml.nvmlDeviceGetHandleByIndex(device_index))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # noqa: BLE001
+            self._nvml = None
+            self.error = f"nvml unavailable: {exc}"
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter_ns(), sm, reasons))
+            except Exception as exc:  # noqa: BLE001
+                self.error = str(exc)
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+        if self._nvml is not None:
+            self.samples.append((time.perf_counter_ns(),
+                                 self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM),
+                                 self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)))
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0, "note": self.error}
+        mask = 0
+        for _, _, r in self.samples:
+            mask |= r
+        reasons = sorted(name for bit, name in _REASONS.items() if mask & bit and name != "gpu_idle")
+        return {"sm_mhz": statistics.median(s for _, s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch with torchrun for N>1")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# Legs
+# ---------------------------------------------------------------------------
+def device_leg(x, steps, warmup, fp32_acc):
+    """CUDA-graph replays of forward and backward, L2 flushed before every step.
+    Returns per-step (fwd_ms, bwd_ms) lists."""
+    args = (x["value"], x["spatial_shapes"], x["level_start_index"], x["sampling_locations"],
+            x["attention_weights"])
+    g = x["grad_output"].reshape(x["value"].shape[0], -1, x["value"].shape[2], x["value"].shape[3])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # warm-up outside capture (allocator, lazy loading)
+        for _ in range(2):
+            msda_ops._forward(*args)
+            msda_ops._backward(*args, g, fp32_acc)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gf):
+        msda_ops._forward(*args)
+    with torch.cuda.graph(gb):
+        msda_ops._backward(*args, g, fp32_acc)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+
+    def one(e):
+        flush.fill_(1)
+        e[0].record()
+        gf.replay()
+        e[1].record()
+        gb.replay()
+        e[2].record()
+
+    tmp = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(warmup):
+        one(tmp)
+    return gf, gb, one, evs
+
+
+def e2e_leg(x, steps, warmup, fp32_acc):
+    """Public op with pinned host buffers: H2D inputs, forward, backward, D2H
+    output and gradients, all inside each timed step."""
+    host = {k: x[k].cpu().pin_memory() for k in ("value", "sampling_locations", "attention_weights",
+                                                 "grad_output")}
+    shapes, starts = x["spatial_shapes"], x["level_start_index"]
+    B, S, M, D = x["value"].shape
+    Q = x["sampling_locations"].shape[1]
+    out_h = torch.empty(B, Q, M * D, dtype=x["value"].dtype).pin_memory()
+    gv_h = torch.empty_like(host["value"]).pin_memory()
+    gl_h = torch.empty_like(host["sampling_locations"]).pin_memory()
+    ga_h = torch.empty_like(host["attention_weights"]).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in (out_h, gv_h, gl_h, ga_h))
+
+    def step():
+        v = host["value"].to("cuda", non_blocking=True).requires_grad_(True)
+        l = host["sampling_locations"].to("cuda", non_blocking=True).requires_grad_(True)
+        a = host["attention_weights"].to("cuda", non_blocking=True).requires_grad_(True)
+        g = host["grad_output"].to("cuda", non_blocking=True)
+        out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc)
+        out.backward(g)
+        out_h.copy_(out.detach(), non_blocking=True)
+        gv_h.copy_(v.grad, non_blocking=True)
+        gl_h.copy_(l.grad, non_blocking=True)
+        ga_h.copy_(a.grad, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    return step, h2d, d2h
+
+
+def cpu_reference_time(preset, dtype, steps, seed=0):
+    """The reference's CPU implementation (grid_sample forward + autograd
+    backward, oracle/msda_oracle.py) on all host cores; seconds per step."""
+    sys.path.insert(0, str(REPO))
+    from oracle import msda_oracle as orc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    x = presets.make_inputs(preset, dtype=dtype, device="cpu", seed=seed)
+
+    def step():
+        v = x["value"].clone().requires_grad_(True)
+        l = x["sampling_locations"].clone().requires_grad_(True)
+        a = x["attention_weights"].clone().requires_grad_(True)
+        out = orc.msda_grid_sample(v, x["spatial_shapes"], l, a)
+        out.backward(x["grad_output"])
+
+    step()  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    return (time.perf_counter() - t0) / steps, threads
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic(config_name):
+    p = REPO / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(config_name)
+
+
+def run_reference_arm(args, preset, dtype):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps = max(1, args.steps)
+    # Bound the CPU run to a few minutes whatever --steps asks for.
+    per_step, threads = cpu_reference_time(preset, dtype, 1)
+    steps = max(1, min(steps, int(120.0 / max(per_step, 1e-3))))
+    for _ in range(min(args.warmup, 2)):
+        cpu_reference_time(preset, dtype, 1)
+    sec, threads = cpu_reference_time(preset, dtype, steps)
+    qps = preset.B * preset.num_queries / sec
+    sample = f"{steps} full fwd+bwd steps of the {preset.name} workload ({dtype}) on {threads} threads"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": str(dtype).replace("torch.", ""), "data": "synthetic",
+        "config": config_dict(preset, dtype, args.gpus),
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(preset, dtype, n):
+    return {"workload": f"{preset.name} preset: {preset.note}", "batch_per_gpu": preset.B,
+            "global_batch": preset.B * n, "queries": preset.num_queries, "heads": preset.M,
+            "head_dim": preset.D, "levels": preset.L, "points": preset.K,
+            "spatial_shapes": [list(s) for s in preset.shapes], "S": preset.S,
+            "dtype": str(dtype).replace("torch.", ""), "parallelism": f"batch-sharded x{n}",
+            "l2": "flushed (512 MiB write) before every timed step"}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default="decoder", choices=sorted(presets.PRESETS))
+    ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    preset = presets.get(args.config)
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32,
+             None: preset.dtype}[args.dtype]
+    if args.impl == "reference":
+        return run_reference_arm(args, preset, dtype)
+
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    x = presets.make_inputs(preset, dtype=dtype, device="cuda", seed=rank)
+    fp32_acc = {"auto": msda_ops._use_fp32_grad_accum(x["value"]), "on": True,
+                "off": False}[args.fp32_grad_accum]
+
+    # ---- device leg -------------------------------------------------------
+    gf, gb, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc)
+    barrier(world)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for e in evs:
+            one(e)
+        barrier(world)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    dev_total_ms = max_over_ranks(sum(f + b for f, b in zip(fwd_ms, bwd_ms)), world)
+    fwd_mean = max_over_ranks(statistics.fmean(fwd_ms), world)
+    bwd_mean = max_over_ranks(statistics.fmean(bwd_ms), world)
+    del gf, gb
+
+    B, S, M, D = x["value"].shape
+    Q = x["sampling_locations"].shape[1]
+    L, K = preset.L, preset.K
+    queries_per_step = B * Q * world
+    value = queries_per_step * args.steps / (dev_total_ms / 1e3)
+
+    # ---- e2e leg ----------------------------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        step, h2d, d2h = e2e_leg(x, args.steps, args.warmup, fp32_acc)
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        barrier(world)
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1), world)
+        e2e = {"value": queries_per_step * args.steps / (e2e_ms / 1e3), "unit": "queries/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": e2e_ms / args.steps}
+
+    # ---- roofline of the backward launch (dominant) -------------------------
+    e = x["value"].element_size()
+    ws = msda_ops._lib.load().msda_backward_workspace_size(
+        B, S, M, D, msda_ops._DTYPE_CODE[x["value"].dtype],
+        msda_ops._lib.MSDA_BWD_FP32_ACCUM if fp32_acc else 0)
+    cast_pass = ws > 0
+    e_acc = 4 if cast_pass else e
+    fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass)
+    peak, peak_kind = load_peaks()
+    achieved = bwd_b / (bwd_mean / 1e3) / 1e9
+    traffic = load_traffic(f"{preset.name}-{str(dtype).replace('torch.', '')}")
+    roofline = {"kernel": "msda_backward (zero-fill + msda_bwd_kernel" + (" + cast" if cast_pass else "") + ")",
+                "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "frac_of_nominal_8TBs": achieved / NOMINAL_HBM_GBS,
+                "traffic": traffic, "algorithmic_bytes": bwd_b, "e_acc": e_acc,
+                "fwd": {"achieved": fwd_b / (fwd_mean / 1e3) / 1e9, "algorithmic_bytes": fwd_b,
+                        "us": fwd_mean * 1e3}}
+
+    # ---- CPU baseline (rank 0, N=1) ----------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, threads = cpu_reference_time(preset, dtype, 3)
+        cpu = {"value": preset.B * preset.num_queries / sec, "unit": "queries/s", "cores": threads,
+               "kind": "port", "sample": f"3 full fwd+bwd steps of the {preset.name} workload, "
+                                         f"grid_sample oracle in {str(dtype).replace('torch.', '')}"}
+
+    launches_per_step = 2 + (1 if cast_pass else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": str(dtype).replace("torch.", ""), "data": "synthetic",
+            "config": config_dict(preset, dtype, world),
+            "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,
+            "fwd_bwd_us": (fwd_mean + bwd_mean) * 1e3,
+            "fp32_grad_accum": fp32_acc,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

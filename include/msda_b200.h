@@ -1,0 +1,113 @@
+/*
+ * msda_b200 -- C ABI of the B200 (sm_100a) multi-scale deformable attention
+ * (MSDA) kernels.
+ *
+ * The library is the native replacement for the CUDA half of the reference
+ * operator roulbac/msda-triton: the Triton kernels in src/msda_triton/kernels.py
+ * and the launches in src/msda_triton/ops.py. Every entry point takes plain
+ * device pointers, sizes and a cudaStream_t passed as void*; no C++ exception
+ * and no framework type crosses this boundary.
+ *
+ * Tensor layouts (all contiguous, row-major; identical to the reference):
+ *   value              (B, S, M, D)          dtype
+ *   spatial_shapes     (L, 2)  int64         (H_l, W_l), on the device
+ *   level_start_index  (L,)    int64         on the device
+ *   sampling_locations (B, Q, M, L, K, 2)    dtype, normalised (x, y)
+ *   attention_weights  (B, Q, M, L, K)       dtype
+ *   output / grad_out  (B, Q, M, D)          dtype (the host views it as (B, Q, M*D))
+ *
+ * Ownership: the caller allocates every buffer, including the optional
+ * backward workspace; the library never allocates device memory.
+ * Threading: the library is stateless apart from a thread-local error string;
+ * all work is enqueued on the given stream with no host synchronisation, so
+ * the calls may be captured in a CUDA graph.
+ * Errors: every entry point returns an msda_status (0 = success); the message
+ * of the last failure on the calling thread is available from
+ * msda_last_error(). A CUDA launch error is reported as MSDA_ERR_CUDA.
+ */
+#ifndef MSDA_B200_H_
+#define MSDA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MSDA_API __attribute__((visibility("default")))
+#else
+#define MSDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of value / sampling_locations / attention_weights / outputs.
+ * Mirrors the dtype set accepted by src/msda_triton/ops.py:17 (_FLOAT_DTYPES). */
+typedef enum msda_dtype {
+  MSDA_DTYPE_F32 = 0,
+  MSDA_DTYPE_F16 = 1,
+  MSDA_DTYPE_BF16 = 2
+} msda_dtype;
+
+typedef enum msda_status {
+  MSDA_OK = 0,
+  MSDA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, misaligned buffer */
+  MSDA_ERR_UNSUPPORTED = 2,      /* dtype / head dim / level count outside what is built */
+  MSDA_ERR_CUDA = 3              /* a CUDA call or kernel launch failed */
+} msda_status;
+
+/* Backward flags. */
+/* Accumulate grad_value in fp32 and downcast once (the fp32_grad_accum=True
+ * path of src/msda_triton/ops.py:76-92). Needs a workspace of
+ * msda_backward_workspace_size() bytes for fp16/bf16; fp32 ignores it. */
+#define MSDA_BWD_FP32_ACCUM 1u
+
+/* Library version string, e.g. "msda_b200 0.1.0 sm_100a". */
+MSDA_API const char* msda_version(void);
+
+/* Message of the last failed call on this thread ("" after a success). */
+MSDA_API const char* msda_last_error(void);
+
+/*
+ * Forward: output[b,q,m,:] = sum_{l,k} attn[b,q,m,l,k] *
+ *                            bilinear(value[b, level l, m, :], loc[b,q,m,l,k,:])
+ * Replaces the launch of _msda_forward_kernel in _MSDAFunction.forward
+ * (src/msda_triton/ops.py:46-52; kernel src/msda_triton/kernels.py:58-163).
+ * B == 0 or Q == 0 is a successful no-op (src/msda_triton/ops.py:186-187).
+ */
+MSDA_API int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                 const void* sampling_locations, const void* attention_weights, void* output,
+                 int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                 int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                 void* stream);
+
+/*
+ * Bytes of fp32 workspace msda_backward needs for these sizes and flags
+ * (0 when no workspace is used). Replaces the allocation of the fp32
+ * grad_value buffer at src/msda_triton/ops.py:76-77.
+ */
+MSDA_API size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int32_t num_heads,
+                                    int32_t head_dim, int32_t dtype, uint32_t flags);
+
+/*
+ * Backward: writes grad_value (B,S,M,D), grad_sampling_locations
+ * (B,Q,M,L,K,2) and grad_attention_weights (B,Q,M,L,K), all in `dtype`.
+ * grad_value need not be zeroed by the caller: the call initialises it.
+ * Replaces _MSDAFunction.backward's zero-fill, kernel launch and downcast
+ * (src/msda_triton/ops.py:76-92; kernel src/msda_triton/kernels.py:166-291).
+ * grad_value is accumulated with atomics: results are not bitwise
+ * deterministic from run to run (as in the reference, ops.py:135-138).
+ */
+MSDA_API int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                  const void* sampling_locations, const void* attention_weights,
+                  const void* grad_output, void* grad_value, void* grad_sampling_locations,
+                  void* grad_attention_weights, void* workspace, size_t workspace_bytes,
+                  int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                  int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                  uint32_t flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSDA_B200_H_ */

@@ -1,0 +1,230 @@
+// C ABI entry points (declared in include/msda_b200.h): argument checks,
+// kernel-shape selection, zero-fill / downcast orchestration.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "msda_b200.h"
+#include "msda_launch.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int succeed() {
+  g_last_error.clear();
+  return MSDA_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MSDA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int elem_size(int32_t dtype) {
+  switch (dtype) {
+    case MSDA_DTYPE_F32: return 4;
+    case MSDA_DTYPE_F16: return 2;
+    case MSDA_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// Largest pixel-index range the kernels address with 32-bit level arithmetic.
+constexpr int64_t kMaxS = int64_t(1) << 30;
+
+struct Shape {
+  int64_t B, S, Q;
+  int32_t M, D, L, K;
+};
+
+int check_shape(const Shape& s, int32_t dtype) {
+  if (elem_size(dtype) == 0) return fail(MSDA_ERR_UNSUPPORTED, "unsupported dtype code %d (0=f32, 1=f16, 2=bf16)", dtype);
+  if (s.B < 0 || s.Q < 0) return fail(MSDA_ERR_INVALID_ARGUMENT, "batch (%lld) and num_queries (%lld) must be >= 0", (long long)s.B, (long long)s.Q);
+  if (s.S < 1 || s.S > kMaxS) return fail(MSDA_ERR_INVALID_ARGUMENT, "num_values S=%lld must be in [1, 2^30]", (long long)s.S);
+  if (s.M < 1 || s.D < 1 || s.K < 1) return fail(MSDA_ERR_INVALID_ARGUMENT, "num_heads (%d), head_dim (%d) and num_points (%d) must be >= 1", s.M, s.D, s.K);
+  if (s.L < 1 || s.L > msda::kMaxLevels) return fail(MSDA_ERR_UNSUPPORTED, "num_levels=%d outside [1, %d]", s.L, msda::kMaxLevels);
+  if ((int64_t)s.L * s.K > 4096) return fail(MSDA_ERR_UNSUPPORTED, "num_levels*num_points=%lld exceeds 4096", (long long)s.L * s.K);
+  return MSDA_OK;
+}
+
+// Picks the lane layout for a head dim. `vec_ptrs_aligned` says whether every
+// buffer read or written in D-chunks is 16-byte aligned.
+int choose_cfg(int32_t D, int es, bool vec_ptrs_aligned, msda::Cfg* c) {
+  const int v16 = 16 / es;
+  if ((D % v16) == 0 && vec_ptrs_aligned) {
+    c->vec = v16;
+  } else {
+    c->vec = 1;
+  }
+  const int nc = D / c->vec;
+  c->lpr = next_pow2(nc < 32 ? nc : 32);
+  c->cpl = (nc + c->lpr - 1) / c->lpr;
+  if (c->cpl == 3) c->cpl = 4;
+  if (c->cpl > 4)
+    return fail(MSDA_ERR_UNSUPPORTED, "head_dim=%d too large for the %s path (max %d)", D,
+                c->vec > 1 ? "vector" : "scalar", 128 * c->vec);
+  return MSDA_OK;
+}
+
+int kshift_of(int32_t K) {
+  if ((K & (K - 1)) != 0) return -1;
+  int s = 0;
+  while ((1 << s) < K) ++s;
+  return s;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* msda_version(void) { return "msda_b200 0.1.0 sm_100a"; }
+
+const char* msda_last_error(void) { return g_last_error.c_str(); }
+
+int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                 const void* sampling_locations, const void* attention_weights, void* output,
+                 int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                 int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                 void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  if (int rc = check_shape(s, dtype)) return rc;
+  if (s.B == 0 || s.Q == 0) return succeed();
+  if (!value || !spatial_shapes || !level_start_index || !sampling_locations || !attention_weights || !output)
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_forward: null pointer argument");
+  const int es = elem_size(dtype);
+  if (!aligned(sampling_locations, 2 * es) || !aligned(value, es) || !aligned(output, es) ||
+      !aligned(attention_weights, es) || !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_forward: misaligned buffer (sampling_locations needs %d-byte alignment)", 2 * es);
+  msda::Cfg cfg;
+  if (int rc = choose_cfg(s.D, es, aligned(value, 16) && aligned(output, 16), &cfg)) return rc;
+
+  msda::OpParams p{};
+  p.value = value;
+  p.shapes = spatial_shapes;
+  p.starts = level_start_index;
+  p.loc = sampling_locations;
+  p.attn = attention_weights;
+  p.out = output;
+  p.B = s.B; p.S = s.S; p.Q = s.Q;
+  p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
+  p.kshift = kshift_of(s.K);
+  p.BQM = s.B * s.Q * s.M;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (dtype) {
+    case MSDA_DTYPE_F32: e = msda::launch_forward<float>(p, cfg, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_forward<__half>(p, cfg, st); break;
+    default: e = msda::launch_forward<__nv_bfloat16>(p, cfg, st); break;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "msda_forward launch");
+  return succeed();
+}
+
+size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int32_t num_heads,
+                                    int32_t head_dim, int32_t dtype, uint32_t flags) {
+  if (!(flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32 || elem_size(dtype) == 0) return 0;
+  if (batch <= 0 || num_values <= 0 || num_heads <= 0 || head_dim <= 0) return 0;
+  return (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim * sizeof(float);
+}
+
+int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                  const void* sampling_locations, const void* attention_weights,
+                  const void* grad_output, void* grad_value, void* grad_sampling_locations,
+                  void* grad_attention_weights, void* workspace, size_t workspace_bytes,
+                  int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                  int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                  uint32_t flags, void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  if (int rc = check_shape(s, dtype)) return rc;
+  if (s.B == 0) return succeed();
+  const int es = elem_size(dtype);
+  const size_t gv_bytes = (size_t)s.B * s.S * s.M * s.D * es;
+  if (!grad_value) return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: null grad_value");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (s.Q == 0) {
+    cudaError_t e = cudaMemsetAsync(grad_value, 0, gv_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
+    return succeed();
+  }
+  if (!value || !spatial_shapes || !level_start_index || !sampling_locations || !attention_weights ||
+      !grad_output || !grad_sampling_locations || !grad_attention_weights)
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: null pointer argument");
+  if (!aligned(sampling_locations, 2 * es) || !aligned(grad_sampling_locations, 2 * es) ||
+      !aligned(value, es) || !aligned(grad_value, es) || !aligned(grad_output, es) ||
+      !aligned(attention_weights, es) || !aligned(grad_attention_weights, es) ||
+      !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: misaligned buffer (locations need %d-byte alignment)", 2 * es);
+
+  const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
+  const size_t ws_need = msda_backward_workspace_size(batch, num_values, num_heads, head_dim, dtype, flags);
+  if (fp32_ws) {
+    if (!workspace || workspace_bytes < ws_need)
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: fp32 accumulation needs a workspace of %zu bytes (got %zu)", ws_need, workspace_bytes);
+    if (!aligned(workspace, 16))
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: workspace must be 16-byte aligned");
+  }
+  void* target = fp32_ws ? workspace : grad_value;
+  msda::Cfg cfg;
+  const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) && aligned(target, 16);
+  if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
+
+  cudaError_t e = cudaMemsetAsync(target, 0, fp32_ws ? ws_need : gv_bytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
+
+  msda::OpParams p{};
+  p.value = value;
+  p.shapes = spatial_shapes;
+  p.starts = level_start_index;
+  p.loc = sampling_locations;
+  p.attn = attention_weights;
+  p.grad_out = grad_output;
+  p.grad_value = target;
+  p.grad_loc = grad_sampling_locations;
+  p.grad_attn = grad_attention_weights;
+  p.B = s.B; p.S = s.S; p.Q = s.Q;
+  p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
+  p.kshift = kshift_of(s.K);
+  p.BQM = s.B * s.Q * s.M;
+  switch (dtype) {
+    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, true, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, fp32_ws, st); break;
+    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, fp32_ws, st); break;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
+  if (fp32_ws) {
+    const int64_t n = s.B * s.S * s.M * s.D;
+    const bool cast_vec = aligned(grad_value, 16);
+    if (dtype == MSDA_DTYPE_F16)
+      e = msda::launch_cast<__half>(static_cast<const float*>(workspace), static_cast<__half*>(grad_value), n, cast_vec, sm_count(), st);
+    else
+      e = msda::launch_cast<__nv_bfloat16>(static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(grad_value), n, cast_vec, sm_count(), st);
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward downcast launch");
+  }
+  return succeed();
+}
+
+}  // extern "C"

@@ -1,0 +1,265 @@
+// Device helpers shared by the MSDA forward and backward kernels (sm_100a).
+//
+// Layouts (all contiguous, row-major, as in the reference operator
+// src/msda_triton/ops.py:96-199 and src/msda_triton/kernels.py:67-82):
+//   value              (B, S, M, D)          one "pixel row" = M*D elements
+//   spatial_shapes     (L, 2)  int64         (H_l, W_l)
+//   level_start_index  (L,)    int64         offset of level l along S
+//   sampling_locations (B, Q, M, L, K, 2)    normalised (x, y)
+//   attention_weights  (B, Q, M, L, K)
+//   output             (B, Q, M, D)          viewed as (B, Q, M*D) by the host
+//
+// Bilinear convention (src/msda_triton/kernels.py:29-35, tests/reference_impls.py:29-31):
+//   x_im = x * W_l - 0.5, y_im = y * H_l - 0.5, zero padding outside the level,
+// i.e. grid_sample(align_corners=False, padding_mode="zeros").
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace msda {
+
+constexpr int kMaxLevels = 16;
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Scalar conversions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// ---------------------------------------------------------------------------
+// Vector loads / stores of VEC elements (VEC * sizeof(T) in {2, 4, 8, 16} bytes,
+// pointer aligned to that size), widened to / narrowed from fp32.
+// ---------------------------------------------------------------------------
+template <int BYTES> struct RawVec;
+template <> struct RawVec<16> { using type = uint4; };
+template <> struct RawVec<8> { using type = uint2; };
+template <> struct RawVec<4> { using type = unsigned int; };
+template <> struct RawVec<2> { using type = unsigned short; };
+
+template <typename T, int VEC>
+struct Pack {
+  using Raw = typename RawVec<VEC * (int)sizeof(T)>::type;
+  union {
+    Raw raw;
+    T e[VEC];
+  };
+};
+
+// Read-only (non-coherent) load; the tensors read this way are never written
+// by the same kernel.
+template <typename T, int VEC>
+__device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&v)[VEC]) {
+  Pack<T, VEC> pk;
+  pk.raw = __ldg(reinterpret_cast<const typename Pack<T, VEC>::Raw*>(p));
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) v[i] = to_f32(pk.e[i]);
+}
+
+// Raw load kept packed (to issue many loads before converting).
+template <typename T, int VEC>
+__device__ __forceinline__ typename Pack<T, VEC>::Raw load_raw(const T* __restrict__ p) {
+  return __ldg(reinterpret_cast<const typename Pack<T, VEC>::Raw*>(p));
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void unpack_raw(typename Pack<T, VEC>::Raw r, float (&v)[VEC]) {
+  Pack<T, VEC> pk;
+  pk.raw = r;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) v[i] = to_f32(pk.e[i]);
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
+  Pack<T, VEC> pk;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) pk.e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<typename Pack<T, VEC>::Raw*>(p) = pk.raw;
+}
+
+// Two consecutive elements (a sampling location's (x, y) pair).
+__device__ __forceinline__ float2 load_pair(const float* p) {
+  return __ldg(reinterpret_cast<const float2*>(p));
+}
+__device__ __forceinline__ float2 load_pair(const __half* p) {
+  return __half22float2(__ldg(reinterpret_cast<const __half2*>(p)));
+}
+__device__ __forceinline__ float2 load_pair(const __nv_bfloat16* p) {
+  return __bfloat1622float2(__ldg(reinterpret_cast<const __nv_bfloat162*>(p)));
+}
+
+__device__ __forceinline__ void store_pair(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+__device__ __forceinline__ void store_pair(__half* p, float a, float b) {
+  *reinterpret_cast<__half2*>(p) = __floats2half2_rn(a, b);
+}
+__device__ __forceinline__ void store_pair(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+
+// ---------------------------------------------------------------------------
+// Vector reductions into global memory (relaxed, gpu scope). sm_90+ supports
+// the 16-byte vector forms of `red.global.add` for f32 and packed f16x2/bf16x2.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void red_add_f32x4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ unsigned pack2(__half lo, __half hi) {
+  return (unsigned)__half_as_ushort(lo) | ((unsigned)__half_as_ushort(hi) << 16);
+}
+__device__ __forceinline__ unsigned pack2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (unsigned)__bfloat16_as_ushort(lo) | ((unsigned)__bfloat16_as_ushort(hi) << 16);
+}
+
+__device__ __forceinline__ void red_add_x8(__half* p, const float (&v)[8]) {
+  unsigned w0 = pack2(__float2half_rn(v[0]), __float2half_rn(v[1]));
+  unsigned w1 = pack2(__float2half_rn(v[2]), __float2half_rn(v[3]));
+  unsigned w2 = pack2(__float2half_rn(v[4]), __float2half_rn(v[5]));
+  unsigned w3 = pack2(__float2half_rn(v[6]), __float2half_rn(v[7]));
+  asm volatile("red.global.add.noftz.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w0), "r"(w1),
+               "r"(w2), "r"(w3)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_x8(__nv_bfloat16* p, const float (&v)[8]) {
+  unsigned w0 = pack2(__float2bfloat16_rn(v[0]), __float2bfloat16_rn(v[1]));
+  unsigned w1 = pack2(__float2bfloat16_rn(v[2]), __float2bfloat16_rn(v[3]));
+  unsigned w2 = pack2(__float2bfloat16_rn(v[4]), __float2bfloat16_rn(v[5]));
+  unsigned w3 = pack2(__float2bfloat16_rn(v[6]), __float2bfloat16_rn(v[7]));
+  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w0),
+               "r"(w1), "r"(w2), "r"(w3)
+               : "memory");
+}
+
+__device__ __forceinline__ void red_add_scalar(float* p, float v) { atomicAdd(p, v); }
+__device__ __forceinline__ void red_add_scalar(__half* p, float v) {
+  atomicAdd(p, __float2half_rn(v));
+}
+__device__ __forceinline__ void red_add_scalar(__nv_bfloat16* p, float v) {
+  atomicAdd(p, __float2bfloat16_rn(v));
+}
+
+// Adds VEC values (one lane's channel chunk) into an accumulator row of type A.
+// A = float with VEC % 4 == 0 uses v4.f32; A = half type with VEC == 8 uses the
+// packed 16-byte form; everything else falls back to scalar atomics.
+template <typename A, int VEC>
+__device__ __forceinline__ void red_add_vec(A* p, const float (&v)[VEC]) {
+  if constexpr (sizeof(A) == 4 && VEC % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 4) red_add_f32x4(reinterpret_cast<float*>(p) + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else if constexpr (sizeof(A) == 2 && VEC == 8) {
+    red_add_x8(p, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) red_add_scalar(p + i, v[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Level table, staged in shared memory at CTA start (the spatial_shapes and
+// level_start_index tensors live on the device; reading them in-kernel avoids
+// a device->host sync and keeps the launch graph-capturable).
+//
+// A level whose (H, W, start) is inconsistent with S (non-positive size, or
+// start + H*W outside [0, S]) is marked empty: every corner on it is treated as
+// out of bounds, so a malformed shapes tensor can never index outside value.
+// ---------------------------------------------------------------------------
+struct LevelInfo {
+  int H;
+  int W;
+  int start;
+  float fH;
+  float fW;
+};
+
+__device__ __forceinline__ void load_levels(const int64_t* __restrict__ shapes,
+                                            const int64_t* __restrict__ starts, int L, int64_t S,
+                                            LevelInfo* lv) {
+  if ((int)threadIdx.x < L) {
+    const int l = threadIdx.x;
+    int64_t H = shapes[2 * l], W = shapes[2 * l + 1], st = starts[l];
+    bool ok = H > 0 && W > 0 && st >= 0 && H <= S && W <= S && st <= S && H * W <= S - st;
+    LevelInfo info;
+    info.H = ok ? (int)H : 0;
+    info.W = ok ? (int)W : 0;
+    info.start = ok ? (int)st : 0;
+    info.fH = (float)info.H;
+    info.fW = (float)info.W;
+    lv[l] = info;
+  }
+  __syncthreads();
+}
+
+// One sampling point resolved to its four bilinear corners:
+//   corner 0 = (y0, x0), 1 = (y0, x0+1), 2 = (y0+1, x0), 3 = (y0+1, x0+1)
+// (the v00, v01, v10, v11 order of src/msda_triton/kernels.py:130-149).
+struct Bilinear {
+  int pix[4];    // pixel index along S (only meaningful where valid)
+  float w[4];    // bilinear weights (1-lx)(1-ly), lx(1-ly), (1-lx)ly, lx*ly
+  float lx, ly;  // fractional offsets inside the cell
+  unsigned valid;  // bit c set iff corner c lies inside the level
+};
+
+// An empty sampling slot (past the last point of the warp's triple): no
+// corner is valid and every weight is zero, so it contributes nothing.
+__device__ __forceinline__ Bilinear empty_slot() {
+  Bilinear r;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    r.pix[c] = 0;
+    r.w[c] = 0.f;
+  }
+  r.lx = r.ly = 0.f;
+  r.valid = 0u;
+  return r;
+}
+
+// x is clamped to [-2, W+1] before the integer conversion (a NaN or huge
+// location then lands fully outside the level instead of overflowing the
+// int cast); inside that range the clamp is the identity, so every in-bounds
+// result equals the unclamped formula of src/msda_triton/kernels.py:112-128.
+__device__ __forceinline__ Bilinear resolve(float locx, float locy, const LevelInfo& L) {
+  Bilinear r;
+  float x = fmaf(locx, L.fW, -0.5f);
+  float y = fmaf(locy, L.fH, -0.5f);
+  x = fminf(fmaxf(x, -2.0f), L.fW + 1.0f);
+  y = fminf(fmaxf(y, -2.0f), L.fH + 1.0f);
+  const float x0f = floorf(x), y0f = floorf(y);
+  const float lx = x - x0f, ly = y - y0f;
+  const int x0 = (int)x0f, y0 = (int)y0f;
+  const bool vx0 = (unsigned)x0 < (unsigned)L.W;
+  const bool vx1 = (unsigned)(x0 + 1) < (unsigned)L.W;
+  const bool vy0 = (unsigned)y0 < (unsigned)L.H;
+  const bool vy1 = (unsigned)(y0 + 1) < (unsigned)L.H;
+  r.valid = (unsigned)(vy0 && vx0) | ((unsigned)(vy0 && vx1) << 1) | ((unsigned)(vy1 && vx0) << 2) |
+            ((unsigned)(vy1 && vx1) << 3);
+  const int p00 = L.start + y0 * L.W + x0;
+  r.pix[0] = p00;
+  r.pix[1] = p00 + 1;
+  r.pix[2] = p00 + L.W;
+  r.pix[3] = p00 + L.W + 1;
+  r.lx = lx;
+  r.ly = ly;
+  r.w[0] = (1.0f - lx) * (1.0f - ly);
+  r.w[1] = lx * (1.0f - ly);
+  r.w[2] = (1.0f - lx) * ly;
+  r.w[3] = lx * ly;
+  return r;
+}
+
+}  // namespace msda

@@ -1,0 +1,112 @@
+// Host-side launch helpers: pick a (VEC, LPR, CPL) instantiation for the
+// head dim and dtype, and launch it on the caller's stream.
+#pragma once
+
+#include "msda_kernels.cuh"
+
+namespace msda {
+
+// VEC: elements per lane load (16 bytes, or 1 for the scalar path).
+// LPR: lanes per corner row (power of two <= 32); CPL: chunks per lane.
+struct Cfg {
+  int vec;
+  int lpr;
+  int cpl;
+};
+
+constexpr int kWarpsPerCta = 8;
+
+template <typename T>
+cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
+template <typename T>
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool fp32_scatter, cudaStream_t st);
+template <typename T>
+cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Template dispatch (included by the per-dtype translation units only).
+// ---------------------------------------------------------------------------
+#ifdef MSDA_LAUNCH_IMPL
+
+#define MSDA_FOR_EACH_SHAPE(X) \
+  X(1, 1, 2)                   \
+  X(2, 1, 2)                   \
+  X(4, 1, 2)                   \
+  X(8, 1, 2)                   \
+  X(16, 1, 2)                  \
+  X(32, 1, 2)                  \
+  X(32, 2, 1)                  \
+  X(32, 4, 1)
+
+template <typename T, int VEC>
+static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
+  const dim3 block(kWarpsPerCta * 32);
+  const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
+#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                             \
+  if (c.lpr == LPR_ && c.cpl == CPL_) {                                            \
+    msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_><<<grid, block, 0, st>>>(p); \
+    return cudaGetLastError();                                                     \
+  }
+  MSDA_FOR_EACH_SHAPE(MSDA_FWD_CASE)
+#undef MSDA_FWD_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T, typename A, int VEC>
+static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
+  const dim3 block(kWarpsPerCta * 32);
+  const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
+#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                         \
+  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                        \
+    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, NB_, true><<<grid, block, 0, st>>>(p); \
+    return cudaGetLastError();                                                                 \
+  }
+  MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
+#undef MSDA_BWD_CASE
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T>
+cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  if (c.vec == V16) return fwd_by_shape<T, V16>(p, c, st);
+  if (c.vec == 1) return fwd_by_shape<T, 1>(p, c, st);
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T>
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool fp32_scatter, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  if (fp32_scatter || sizeof(T) == 4) {
+    if (c.vec == V16) return bwd_by_shape<T, float, V16>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, float, 1>(p, c, st);
+  } else {
+    if (c.vec == V16) return bwd_by_shape<T, T, V16>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1>(p, c, st);
+  }
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T>
+cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  const int64_t max_blocks = (int64_t)num_sms * 8;
+  if (vec_ok && n % V16 == 0) {
+    const int64_t nvec = n / V16;
+    const int64_t blocks = std::min<int64_t>(max_blocks, (nvec + 255) / 256);
+    msda_cast_kernel<T, V16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(src, dst, nvec);
+  } else {
+    const int64_t blocks = std::min<int64_t>(max_blocks, (n + 255) / 256);
+    msda_cast_kernel<T, 1><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(src, dst, n);
+  }
+  return cudaGetLastError();
+}
+
+#define MSDA_INSTANTIATE(T)                                                                 \
+  template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);        \
+  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, bool, cudaStream_t); \
+  template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);
+
+#endif  // MSDA_LAUNCH_IMPL
+
+}  // namespace msda

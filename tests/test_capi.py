@@ -1,0 +1,136 @@
+"""Host-side checks that need no GPU: the C ABI library loads and exports
+every symbol include/msda_b200.h declares, its argument checks reject bad
+calls before touching the device, and the Python op validates like the
+reference (src/msda_triton/ops.py:140-171; tests/test_msda.py:254-271)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import cases
+from msda_triton_b200 import MultiScaleDeformableAttnFunction, _lib, multi_scale_deformable_attention
+from msda_triton_b200.ops import _use_fp32_grad_accum
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "msda_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"MSDA_API\s+[\w\s\*]+?\b(msda_\w+)\s*\(", text)
+
+
+def test_header_declares_the_abi():
+    assert set(_declared()) == {"msda_version", "msda_last_error", "msda_forward",
+                                "msda_backward_workspace_size", "msda_backward"}
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, name
+    assert _lib.version().startswith("msda_b200 ")
+    assert "sm_100a" in _lib.version()
+
+
+def _fwd(lib, **over):
+    args = dict(value=1, shapes=8, starts=8, loc=8, attn=8, out=8, B=1, S=4, Q=1, M=1, D=4, L=1,
+                K=1, dtype=0)
+    args.update(over)
+    vp = ctypes.c_void_p
+    return lib.msda_forward(vp(args["value"]), vp(args["shapes"]), vp(args["starts"]),
+                            vp(args["loc"]), vp(args["attn"]), vp(args["out"]), args["B"],
+                            args["S"], args["Q"], args["M"], args["D"], args["L"], args["K"],
+                            args["dtype"], vp(0))
+
+
+def test_abi_rejects_bad_arguments_before_any_device_work():
+    lib = _lib.load()
+    assert _fwd(lib, dtype=7) == _lib.MSDA_ERR_UNSUPPORTED
+    assert b"dtype" in lib.msda_last_error()
+    assert _fwd(lib, L=0) == _lib.MSDA_ERR_UNSUPPORTED
+    assert _fwd(lib, L=17) == _lib.MSDA_ERR_UNSUPPORTED
+    assert _fwd(lib, S=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert _fwd(lib, S=(1 << 30) + 1) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert _fwd(lib, D=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert _fwd(lib, B=-1) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    # Null pointers and misaligned sampling locations are caught on the host.
+    assert _fwd(lib, value=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.msda_last_error()
+    assert _fwd(lib, loc=6) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert b"misaligned" in lib.msda_last_error()
+    # Empty work (B == 0 or Q == 0) succeeds without launching anything.
+    assert _fwd(lib, B=0, value=0, out=0) == _lib.MSDA_OK
+    assert _fwd(lib, Q=0) == _lib.MSDA_OK
+    assert lib.msda_last_error() == b""
+
+
+def test_abi_workspace_size():
+    lib = _lib.load()
+    f = _lib.MSDA_BWD_FP32_ACCUM
+    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_BF16, f) == 2 * 10 * 3 * 8 * 4
+    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_F16, f) == 2 * 10 * 3 * 8 * 4
+    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_F32, f) == 0
+    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_BF16, 0) == 0
+
+
+def test_abi_backward_needs_workspace_for_fp32_accumulation():
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    rc = lib.msda_backward(vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16),
+                           vp(0), 0, 1, 4, 1, 1, 8, 1, 1, _lib.MSDA_DTYPE_BF16,
+                           _lib.MSDA_BWD_FP32_ACCUM, vp(0))
+    assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert b"workspace" in lib.msda_last_error()
+
+
+def _small(dtype=torch.float32, device="cpu"):
+    return cases.make_inputs(B=1, Q=8, M=2, D=16, shapes=[(6, 6)], K=2, dtype=dtype, device=device)
+
+
+def test_op_validation_messages_match_reference():
+    value, shapes, starts, loc, attn = _small()
+    with pytest.raises(ValueError, match="attention_weights"):
+        multi_scale_deformable_attention(value, shapes, starts, loc, attn[:, :, :, :, :1])
+    with pytest.raises(ValueError, match="dtypes"):
+        multi_scale_deformable_attention(value, shapes, starts, loc.half(), attn)
+    with pytest.raises(ValueError, match="CUDA"):
+        multi_scale_deformable_attention(value, shapes, starts, loc, attn)
+    with pytest.raises(ValueError, match="CUDA .*MPS"):
+        multi_scale_deformable_attention(torch.zeros(1, 1, 1, 1), torch.tensor([[1, 1]]), None,
+                                         torch.zeros(1, 1, 1, 1, 1, 2), torch.zeros(1, 1, 1, 1, 1))
+    with pytest.raises(ValueError, match="value must be"):
+        multi_scale_deformable_attention(value[0], shapes, starts, loc, attn)
+    with pytest.raises(ValueError, match="sampling_locations must be"):
+        multi_scale_deformable_attention(value, shapes, starts, loc[..., :1], attn)
+    with pytest.raises(ValueError, match="inconsistent"):
+        multi_scale_deformable_attention(value, shapes, starts, loc[:, :, :1], attn)
+    with pytest.raises(ValueError, match="spatial_shapes"):
+        multi_scale_deformable_attention(value, shapes[:, :1], starts, loc, attn)
+    with pytest.raises(ValueError, match="unsupported dtype"):
+        multi_scale_deformable_attention(value.double(), shapes, starts, loc.double(), attn.double())
+
+
+def test_default_accumulator_policy():
+    assert _use_fp32_grad_accum(torch.zeros(1, dtype=torch.bfloat16)) is True
+    assert _use_fp32_grad_accum(torch.zeros(1, dtype=torch.float16)) is True
+    assert _use_fp32_grad_accum(torch.zeros(1, dtype=torch.float32)) is False
+
+
+def test_package_surface():
+    import msda_triton_b200 as pkg
+
+    assert pkg.__all__ == ["multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction"]
+    assert callable(MultiScaleDeformableAttnFunction.apply)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libmsda_b200.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.load()

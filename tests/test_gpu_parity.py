@@ -1,0 +1,406 @@
+"""Parity of the sm_100a kernels with the reference, through the public op and
+the C ABI (GPU only). Mirrors tests/test_msda.py of roulbac/msda-triton
+(forward :128-150, backward :179-227, options :153-170 and :230-246,
+validation :254-271) and adds the BASELINE operating points at full size,
+the reference Triton kernels' own outputs (golden vectors), and edge cases.
+
+Tolerances: the reference suite's (tests/cases.py REF_*_TOL) and the
+stricter bar of this build (STRICT_TOL: fp32 rtol 1e-4 / atol 1e-5; fp16 and
+bf16 within 1e-2 relative of the fp32 reference, on the forward output and
+all three gradients).
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from cases import CASES, REF_BWD_TOL, REF_FWD_TOL, STRICT_TOL
+from msda_triton_b200 import MultiScaleDeformableAttnFunction, multi_scale_deformable_attention, presets
+from oracle import msda_oracle as orc
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+DTYPES = [torch.float32, torch.float16, torch.bfloat16]
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(autouse=True)
+def _lib_loaded(cuda_lib):
+    yield
+
+
+def run_op(value, shapes, starts, loc, attn, grad_out=None, **kw):
+    v = value.detach().clone().requires_grad_(grad_out is not None)
+    l = loc.detach().clone().requires_grad_(grad_out is not None)
+    a = attn.detach().clone().requires_grad_(grad_out is not None)
+    out = multi_scale_deformable_attention(v, shapes, starts, l, a, **kw)
+    if grad_out is None:
+        return out.detach(), None
+    out.backward(grad_out)
+    return out.detach(), (v.grad, l.grad, a.grad)
+
+
+def close(actual, expected, tol, what=""):
+    torch.testing.assert_close(actual.double().cpu(), expected.double().cpu(), **tol,
+                               msg=lambda m: f"{what}: {m}")
+
+
+def oracle64(value, shapes, starts, loc, attn, g):
+    """float64 oracle on the same (possibly half-precision) inputs: the
+    grid_sample forward and the analytic backward, in float64. For fp32
+    locations the backward uses the reference's fp32-rounded pixel
+    coordinates (x = fma(loc, W, -0.5) in fp32, src/msda_triton/kernels.py:112-113):
+    at W ~ 167 that rounding alone moves grad_attn by ~1e-4, more than the
+    strict fp32 atol, for every fp32 implementation of the reference's maths.
+    fp16/bf16 locations give exact coordinates either way."""
+    cpu = lambda t: t.detach().cpu().double()  # noqa: E731
+    out = orc.msda_grid_sample(cpu(value), shapes.cpu(), cpu(loc), cpu(attn))
+    coord = torch.float32 if loc.dtype == torch.float32 else None
+    grads = orc.msda_backward_analytic(cpu(value), shapes.cpu(), starts.cpu(), cpu(loc), cpu(attn),
+                                       cpu(g), coord_dtype=coord)
+    return out, grads
+
+
+# ---------------------------------------------------------------------------
+# The reference suite's cases
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("case", CASES, ids=[c["id"] for c in CASES])
+def test_forward_matches_reference(case, dtype):
+    value, shapes, starts, loc, attn = cases.make_inputs(**cases.case_kwargs(case), dtype=dtype,
+                                                         device=DEV)
+    out, _ = run_op(value, shapes, starts, loc, attn)
+    ref, _ = orc.reference_fp32(value, shapes, loc, attn)
+    assert out.dtype == dtype and out.shape == ref.shape
+    close(out, ref, STRICT_TOL[dtype], "out")
+
+
+@pytest.mark.parametrize("fp32_grad_accum", [False, True], ids=["native_acc", "fp32_acc"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("case", [CASES[0], CASES[2]], ids=[CASES[0]["id"], CASES[2]["id"]])
+def test_backward_matches_reference(case, dtype, fp32_grad_accum):
+    value, shapes, starts, loc, attn = cases.make_inputs(**cases.case_kwargs(case), dtype=dtype,
+                                                         device=DEV)
+    B, Q, M, D = value.shape[0], loc.shape[1], value.shape[2], value.shape[3]
+    g = cases.grad_output_like(torch.empty(B, Q, M * D, device=DEV, dtype=dtype))
+    _, got = run_op(value, shapes, starts, loc, attn, g, fp32_grad_accum=fp32_grad_accum)
+    assert all(t.dtype == dtype for t in got)
+    _, ref = oracle64(value, shapes, starts, loc, attn, g)
+    # Native half-precision atomics round at every add: held to the
+    # reference suite's tolerance; every fp32-accumulated path to the strict bar.
+    gv_tol = STRICT_TOL[dtype] if (fp32_grad_accum or dtype == torch.float32) else REF_BWD_TOL[dtype]
+    cases.assert_grads_close(got, ref, loc, shapes, STRICT_TOL[dtype], gv_tol=gv_tol)
+    # ... and the reference suite's own comparison, against its fp32 grid_sample path.
+    _, ref32 = orc.reference_fp32(value, shapes, loc, attn, g)
+    cases.assert_grads_close(got, ref32, loc, shapes, REF_BWD_TOL[dtype])
+
+
+def test_forward_out_of_bounds_locations():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=64, M=4, D=32, shapes=[(14, 20), (7, 10)], K=4, dtype=torch.float32, device=DEV,
+        loc_lo=-0.5, loc_hi=1.5)
+    out, _ = run_op(value, shapes, starts, loc, attn)
+    ref, _ = orc.reference_fp32(value, shapes, loc, attn)
+    close(out, ref, REF_FWD_TOL[torch.float32], "out")
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_backward_out_of_bounds_locations(dtype):
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=64, M=4, D=32, shapes=[(14, 20), (7, 10)], K=4, dtype=dtype, device=DEV,
+        loc_lo=-0.5, loc_hi=1.5)
+    g = cases.grad_output_like(torch.empty(2, 64, 128, device=DEV, dtype=dtype))
+    out, got = run_op(value, shapes, starts, loc, attn, g)
+    ref, grads = oracle64(value, shapes, starts, loc, attn, g)
+    close(out, ref, STRICT_TOL[dtype], "out")
+    cases.assert_grads_close(got, grads, loc, shapes, STRICT_TOL[dtype])
+
+
+def test_forward_level_start_index_optional_and_noncontiguous():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=50, M=4, D=32, shapes=[(12, 16), (6, 8)], K=4, dtype=torch.float32, device=DEV)
+    out, _ = run_op(value, shapes, starts, loc, attn)
+    out_nostarts, _ = run_op(value, shapes, None, loc, attn)
+    torch.testing.assert_close(out, out_nostarts)
+    value_nc = value.transpose(1, 2).contiguous().transpose(1, 2)
+    assert not value_nc.is_contiguous()
+    out_nc = multi_scale_deformable_attention(value_nc, shapes, starts, loc, attn)
+    torch.testing.assert_close(out, out_nc)
+    # Host-side spatial_shapes / level_start_index are accepted too.
+    out_host = multi_scale_deformable_attention(value, shapes.cpu(), starts.cpu(), loc, attn)
+    torch.testing.assert_close(out, out_host)
+
+
+def test_fp32_accum_paths_agree_at_fp32():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=100, M=4, D=32, shapes=[(24, 32), (12, 16)], K=4, dtype=torch.float32, device=DEV)
+    grads = []
+    for acc in (False, True):
+        v = value.clone().requires_grad_(True)
+        out = multi_scale_deformable_attention(v, shapes, starts, loc, attn, fp32_grad_accum=acc)
+        out.backward(torch.ones_like(out))
+        grads.append(v.grad)
+    torch.testing.assert_close(grads[0], grads[1], rtol=1e-5, atol=1e-5)
+
+
+def test_rejects_mismatched_shapes_and_dtypes():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=1, Q=8, M=2, D=16, shapes=[(6, 6)], K=2, dtype=torch.float32, device=DEV)
+    with pytest.raises(ValueError, match="attention_weights"):
+        multi_scale_deformable_attention(value, shapes, starts, loc, attn[:, :, :, :, :1])
+    with pytest.raises(ValueError, match="dtypes"):
+        multi_scale_deformable_attention(value, shapes, starts, loc.half(), attn)
+    with pytest.raises(ValueError, match="CUDA"):
+        multi_scale_deformable_attention(value.cpu(), shapes.cpu(), starts.cpu(), loc.cpu(),
+                                         attn.cpu())
+    with pytest.raises(ValueError, match="level_start_index"):
+        multi_scale_deformable_attention(value, shapes, starts[:0], loc, attn)
+    with pytest.raises(ValueError, match="same CUDA device"):
+        multi_scale_deformable_attention(value, shapes, starts, loc.cpu(), attn)
+    # Host-side shapes that address more rows than value holds are rejected.
+    with pytest.raises(ValueError, match="value has S"):
+        multi_scale_deformable_attention(value, torch.tensor([[7, 6]]), None, loc, attn)
+
+
+# ---------------------------------------------------------------------------
+# The reference's own Triton kernels (golden vectors from the interpreter)
+# ---------------------------------------------------------------------------
+
+GOLDEN_TRITON = sorted(p.stem for p in GOLDEN.glob("*.npz") if p.stem.startswith(("case_", "preset_")))
+
+
+@pytest.mark.parametrize("name", GOLDEN_TRITON)
+def test_matches_reference_triton_kernels(name):
+    npz = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(npz["meta"]))
+    if meta["kind"] == "preset":
+        x = presets.make_inputs(presets.get(meta["preset"]), seed=meta["seed"])
+        value, shapes, starts = x["value"], x["spatial_shapes"], x["level_start_index"]
+        loc, attn, g = x["sampling_locations"], x["attention_weights"], x["grad_output"]
+    else:
+        kw = dict(meta["kwargs"])
+        kw["shapes"] = [tuple(s) for s in kw["shapes"]]
+        value, shapes, starts, loc, attn = cases.make_inputs(
+            **kw, dtype=torch.float32, device="cpu", loc_lo=meta["loc_lo"], loc_hi=meta["loc_hi"])
+        g = cases.grad_output_like(torch.empty(loc.shape[0], loc.shape[1], loc.shape[2] * kw["D"]))
+    assert cases.digest(value) == str(npz["digest_value"])
+    assert cases.digest(loc) == str(npz["digest_loc"])
+    dev = [t.to(DEV) for t in (value, shapes, starts, loc, attn, g)]
+    out, (gv, gl, ga) = run_op(*dev[:5], dev[5])
+    cases.assert_matches_golden(out, npz, "triton_out", rtol=1e-5, atol=1e-5)
+    # The reference suite's fp32 backward tolerance (tests/test_msda.py:52).
+    cases.assert_matches_golden(gv, npz, "triton_grad_value", rtol=1e-4, atol=1e-4)
+    cases.assert_matches_golden(gl, npz, "triton_grad_loc", rtol=1e-4, atol=1e-4)
+    cases.assert_matches_golden(ga, npz, "triton_grad_attn", rtol=1e-4, atol=1e-4)
+
+
+# ---------------------------------------------------------------------------
+# BASELINE operating points at full size
+# ---------------------------------------------------------------------------
+
+BASELINE_POINTS = [("small", None), ("decoder", None), ("encoder", None), ("m2f", torch.float16),
+                   ("m2f", torch.float32), ("decoder", torch.float16), ("decoder", torch.float32)]
+
+
+@pytest.mark.parametrize("name,dtype", BASELINE_POINTS,
+                         ids=[f"{n}-{d if d else 'default'}" for n, d in BASELINE_POINTS])
+def test_baseline_operating_point_full_parity(name, dtype):
+    """Full-size parity. small/decoder: against the float64 oracle at the
+    strict bar. encoder/m2f (CPU float64 would take minutes): against the
+    fp32 grid_sample reference -- strict for fp16/bf16, the reference suite's
+    fp32 backward tolerance for fp32 (whose error there is the reference's own
+    fp32 coordinate rounding, amplified by W ~ 128-167)."""
+    p = presets.get(name)
+    x = presets.make_inputs(p, dtype=dtype, device=DEV, seed=0)
+    v, s, st = x["value"], x["spatial_shapes"], x["level_start_index"]
+    l, a, g = x["sampling_locations"], x["attention_weights"], x["grad_output"]
+    dt = v.dtype
+    out, got = run_op(v, s, st, l, a, g)
+    if name in ("small", "decoder"):
+        ref, grads = oracle64(v, s, st, l, a, g)
+        close(out, ref, STRICT_TOL[dt], "out")
+        cases.assert_grads_close(got, grads, l, s, STRICT_TOL[dt], what=name)
+    else:
+        ref, grads = orc.reference_fp32(v, s, l, a, g)
+        close(out, ref, STRICT_TOL[dt], "out")
+        tol = STRICT_TOL[dt] if dt != torch.float32 else REF_BWD_TOL[dt]
+        cases.assert_grads_close(got, grads, l, s, tol, what=name)
+
+
+def test_scale_d64_variant_parity():
+    p = presets.get("scale_d64")
+    x = presets.make_inputs(p, device=DEV, seed=3, batch=2)
+    v, s, st = x["value"], x["spatial_shapes"], x["level_start_index"]
+    l, a, g = x["sampling_locations"], x["attention_weights"], x["grad_output"]
+    out, got = run_op(v, s, st, l, a, g)
+    ref, grads = orc.reference_fp32(v, s, l, a, g)
+    tol = STRICT_TOL[torch.bfloat16]
+    close(out, ref, tol, "out")
+    cases.assert_grads_close(got, grads, l, s, tol, what="scale_d64")
+
+
+def test_encoder_properties_at_full_size():
+    """Size-independent properties at the encoder point (fp32): the forward
+    is linear in value and in attention_weights, grad_value is linear in
+    grad_output, and sum(grad_attn * attn) == <grad_output, output>."""
+    p = presets.get("encoder")
+    x = presets.make_inputs(p, dtype=torch.float32, device=DEV, seed=1)
+    v, s, st, l, a, g = (x["value"], x["spatial_shapes"], x["level_start_index"],
+                         x["sampling_locations"], x["attention_weights"], x["grad_output"])
+    f = lambda vv, aa: multi_scale_deformable_attention(vv, s, st, l, aa)  # noqa: E731
+    v2 = torch.randn_like(v)
+    torch.testing.assert_close(f(2.5 * v + v2, a), 2.5 * f(v, a) + f(v2, a), rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(f(v, 3.0 * a), 3.0 * f(v, a), rtol=1e-5, atol=1e-5)
+    _, (gv1, _, ga1) = run_op(v, s, st, l, a, g)
+    _, (gv2, _, _) = run_op(v, s, st, l, a, -2.0 * g)
+    torch.testing.assert_close(gv2, -2.0 * gv1, rtol=1e-5, atol=1e-5)
+    out = f(v, a)
+    lhs = (ga1.double() * a.double()).sum()
+    rhs = (g.double() * out.double()).sum()
+    torch.testing.assert_close(lhs, rhs, rtol=1e-5, atol=1e-3)
+
+
+# ---------------------------------------------------------------------------
+# Edge cases
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("D,dtype", [(3, torch.float32), (5, torch.float16), (24, torch.bfloat16),
+                                     (8, torch.bfloat16), (4, torch.float32), (128, torch.bfloat16),
+                                     (256, torch.float32), (96, torch.float16), (40, torch.float32)])
+def test_head_dims(D, dtype):
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=19, M=3, D=D, shapes=[(7, 9), (4, 5)], K=3, dtype=dtype, device=DEV,
+        loc_lo=-0.2, loc_hi=1.2)
+    g = cases.grad_output_like(torch.empty(2, 19, 3 * D, device=DEV, dtype=dtype))
+    out, got = run_op(value, shapes, starts, loc, attn, g)
+    ref, grads = oracle64(value, shapes, starts, loc, attn, g)
+    close(out, ref, STRICT_TOL[dtype], "out")
+    cases.assert_grads_close(got, grads, loc, shapes, STRICT_TOL[dtype], what=f"D={D}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_misaligned_buffers_take_the_scalar_path(dtype):
+    """A value tensor whose data pointer is not 16-byte aligned (a view with a
+    storage offset) is served by the scalar-load kernels, with equal results."""
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=1, Q=21, M=2, D=32, shapes=[(9, 8), (5, 4)], K=4, dtype=dtype, device=DEV)
+    base = torch.empty(value.numel() + 1, device=DEV, dtype=dtype)
+    shifted = base[1:].view_as(value)
+    shifted.copy_(value)
+    assert shifted.data_ptr() % 16 != 0
+    g = cases.grad_output_like(torch.empty(1, 21, 64, device=DEV, dtype=dtype))
+    out_a, (gv_a, gl_a, ga_a) = run_op(value, shapes, starts, loc, attn, g)
+    v = shifted.requires_grad_(True)
+    out_b = multi_scale_deformable_attention(v, shapes, starts, loc, attn)
+    out_b.backward(g)
+    tol = dict(rtol=1e-6, atol=1e-6) if dtype == torch.float32 else STRICT_TOL[dtype]
+    close(out_b.detach(), out_a, tol, "out")
+    close(v.grad, gv_a, tol, "grad_value")
+
+
+def test_exact_corner_locations():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=1, Q=4, M=1, D=3, shapes=[(4, 6)], K=2, dtype=torch.float32, device=DEV)
+    loc = cases.exact_corner_locations(loc.shape, torch.float32).to(DEV)
+    g = cases.grad_output_like(torch.empty(1, 4, 3, device=DEV))
+    out, got = run_op(value, shapes, starts, loc, attn, g)
+    ref, grads = oracle64(value, shapes, starts, loc, attn, g)
+    close(out, ref, STRICT_TOL[torch.float32], "out")
+    cases.assert_grads_close(got, grads, loc, shapes, STRICT_TOL[torch.float32], what="corners")
+
+
+def test_zero_sized_batch_and_queries():
+    for B, Q in ((0, 5), (2, 0)):
+        value = torch.randn(B, 20, 2, 8, device=DEV)
+        loc = torch.rand(B, Q, 2, 1, 2, 2, device=DEV)
+        attn = torch.rand(B, Q, 2, 1, 2, device=DEV)
+        out = multi_scale_deformable_attention(value, torch.tensor([[4, 5]], device=DEV), None,
+                                               loc, attn)
+        assert out.shape == (B, Q, 16) and out.abs().sum() == 0
+
+
+def test_non_finite_and_huge_locations_stay_in_bounds():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=1, Q=8, M=2, D=16, shapes=[(6, 7), (3, 4)], K=2, dtype=torch.float32, device=DEV)
+    bad = torch.tensor([float("nan"), float("inf"), -float("inf"), 1e30, -1e30, 3e9],
+                       device=DEV)
+    flat = loc.view(-1)
+    flat[: bad.numel() * 4] = bad.repeat(4)
+    g = torch.ones(1, 8, 32, device=DEV)
+    out, (gv, gl, ga) = run_op(value, shapes, starts, loc, attn, g)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and torch.isfinite(gv).all()
+    assert torch.isfinite(ga).all() and torch.isfinite(gl).all()
+    # Queries whose locations are all finite and in range still match the oracle.
+    ok = torch.isfinite(loc).all(-1).all(-1).all(-1).all(-1)[0]
+    ref, _ = orc.reference_fp32(value, shapes, loc.nan_to_num(0.0, 5.0, -5.0), attn)
+    close(out[0, ok], ref[0, ok.cpu()], STRICT_TOL[torch.float32], "out")
+
+
+def test_device_shapes_beyond_value_rows_are_treated_as_empty():
+    """Device-side spatial_shapes that claim more rows than value holds cannot
+    be checked without a sync; the kernels treat such a level as empty instead
+    of reading out of bounds."""
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=1, Q=16, M=2, D=16, shapes=[(6, 7), (3, 4)], K=2, dtype=torch.float32, device=DEV)
+    bad_shapes = torch.tensor([[6, 7], [30, 40]], device=DEV)
+    out = multi_scale_deformable_attention(value, bad_shapes, starts, loc, attn)
+    attn0 = attn.clone()
+    attn0[:, :, :, 1] = 0
+    ref, _ = orc.reference_fp32(value, shapes, loc, attn0)
+    close(out, ref, STRICT_TOL[torch.float32], "out")
+
+
+def test_mmcv_style_function():
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=30, M=4, D=32, shapes=[(12, 16), (6, 8)], K=4, dtype=torch.float32, device=DEV)
+    v = value.clone().requires_grad_(True)
+    out = MultiScaleDeformableAttnFunction.apply(v, shapes, starts, loc, attn, 64)
+    out.backward(torch.ones_like(out))
+    ref, (gv_r, _, _) = oracle64(value, shapes, starts, loc, attn, torch.ones(2, 30, 128))
+    close(out.detach(), ref, STRICT_TOL[torch.float32], "out")
+    close(v.grad, gv_r, STRICT_TOL[torch.float32], "grad_value")
+
+
+def test_side_stream_and_graph_capture():
+    """Calls enqueue on the caller's current stream and can be captured in a
+    CUDA graph (no host synchronisation inside the op)."""
+    x = presets.make_inputs(presets.get("decoder"), device=DEV, seed=5)
+    args = (x["value"], x["spatial_shapes"], x["level_start_index"], x["sampling_locations"],
+            x["attention_weights"])
+    ref_out = multi_scale_deformable_attention(*args)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        out_side = multi_scale_deformable_attention(*args)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.testing.assert_close(out_side, ref_out)
+
+    static_g = x["grad_output"].clone()
+    warm = torch.cuda.Stream()
+    warm.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(warm):  # warm up on a side stream, as torch's graph recipe asks
+        for _ in range(2):
+            vw = x["value"].clone().requires_grad_(True)
+            multi_scale_deformable_attention(vw, *args[1:]).backward(static_g)
+    torch.cuda.current_stream().wait_stream(warm)
+    torch.cuda.synchronize()
+    v = x["value"].clone().requires_grad_(True)  # fresh leaf: its AccumulateGrad is captured
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = multi_scale_deformable_attention(v, *args[1:])
+        static_out.backward(static_g)
+    graph.replay()
+    torch.cuda.synchronize()
+    _, (gv_ref, _, _) = run_op(*args, static_g)
+    torch.testing.assert_close(static_out.detach(), ref_out)
+    close(v.grad, gv_ref, STRICT_TOL[torch.bfloat16], "grad_value (graph)")
