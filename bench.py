@@ -180,9 +180,10 @@ def barrier(world: int):
 # ---------------------------------------------------------------------------
 # Legs
 # ---------------------------------------------------------------------------
-def device_leg(x, steps, warmup, fp32_acc):
-    """CUDA-graph replays of forward and backward, L2 flushed before every step.
-    Returns per-step (fwd_ms, bwd_ms) lists."""
+def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
+    """Forward and backward launches (CUDA-graph replays, or direct launches
+    with use_graph=False), L2 flushed before every step, each step bracketed
+    by CUDA events. Returns (graphs, step function, per-step events)."""
     args = (x["value"], x["spatial_shapes"], x["level_start_index"], x["sampling_locations"],
             x["attention_weights"])
     g = x["grad_output"].reshape(x["value"].shape[0], -1, x["value"].shape[2], x["value"].shape[3])
@@ -192,22 +193,30 @@ def device_leg(x, steps, warmup, fp32_acc):
     with torch.cuda.stream(s):  # warm-up outside capture (allocator, lazy loading)
         for _ in range(2):
             msda_ops._forward(*args)
-            msda_ops._backward(*args, g, fp32_acc)
+            msda_ops._backward(*args, g, fp32_acc, algo_flags)
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gf):
-        msda_ops._forward(*args)
-    with torch.cuda.graph(gb):
-        msda_ops._backward(*args, g, fp32_acc)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    if use_graph:
+        gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gf):
+            msda_ops._forward(*args)
+        with torch.cuda.graph(gb):
+            msda_ops._backward(*args, g, fp32_acc, algo_flags)
+        run_f, run_b = gf.replay, gb.replay
+    else:
+        gf = gb = None
+        # Outputs are allocated outside the timed events by the caching
+        # allocator (no device work); the flush keeps the GPU ahead of the host.
+        run_f = lambda: msda_ops._forward(*args)  # noqa: E731
+        run_b = lambda: msda_ops._backward(*args, g, fp32_acc, algo_flags)  # noqa: E731
 
     def one(e):
         flush.fill_(1)
         e[0].record()
-        gf.replay()
+        run_f()
         e[1].record()
-        gb.replay()
+        run_b()
         e[2].record()
 
     tmp = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
@@ -334,6 +343,10 @@ def main(argv=None) -> int:
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner"],
+                    help="force the grad_value algorithm of the device leg (default: automatic)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time direct launches instead of CUDA-graph replays")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
@@ -352,8 +365,13 @@ def main(argv=None) -> int:
     fp32_acc = {"auto": msda_ops._use_fp32_grad_accum(x["value"]), "on": True,
                 "off": False}[args.fp32_grad_accum]
 
+    lib = msda_ops._lib
+    algo_flags = {"auto": 0, "scatter": lib.MSDA_BWD_FORCE_SCATTER,
+                  "owner": lib.MSDA_BWD_FORCE_OWNER}[args.bwd_algo]
+
     # ---- device leg -------------------------------------------------------
-    gf, gb, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc)
+    gf, gb, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
+                                  use_graph=not args.no_graph)
     barrier(world)
     with ClockSampler(torch.cuda.current_device()) as clk:
         for e in evs:
@@ -391,15 +409,21 @@ def main(argv=None) -> int:
     # ---- roofline of the backward launch (dominant) -------------------------
     e = x["value"].element_size()
     ws = msda_ops._lib.load().msda_backward_workspace_size(
-        B, S, M, D, msda_ops._DTYPE_CODE[x["value"].dtype],
-        msda_ops._lib.MSDA_BWD_FP32_ACCUM if fp32_acc else 0)
+        B, S, Q, M, D, L, K, msda_ops._DTYPE_CODE[x["value"].dtype],
+        (msda_ops._lib.MSDA_BWD_FP32_ACCUM if fp32_acc else 0) | algo_flags)
     cast_pass = ws > 0
+    owner = (args.bwd_algo == "owner" or
+             (args.bwd_algo == "auto" and Q * L * K / S <= 1.0 and D <= 256))
     e_acc = 4 if cast_pass else e
     fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass)
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (bwd_mean / 1e3) / 1e9
     traffic = load_traffic(f"{preset.name}-{str(dtype).replace('torch.', '')}")
-    roofline = {"kernel": "msda_backward (zero-fill + msda_bwd_kernel" + (" + cast" if cast_pass else "") + ")",
+    if owner:
+        kdesc = "msda_backward (msda_bwd_kernel grad_loc/grad_attn + msda_bwd_value_owner_kernel)"
+    else:
+        kdesc = "msda_backward (zero-fill + msda_bwd_kernel" + (" + cast" if cast_pass else "") + ")"
+    roofline = {"kernel": kdesc,
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                 "frac_of_nominal_8TBs": achieved / NOMINAL_HBM_GBS,
@@ -415,7 +439,7 @@ def main(argv=None) -> int:
                "kind": "port", "sample": f"3 full fwd+bwd steps of the {preset.name} workload, "
                                          f"grid_sample oracle in {str(dtype).replace('torch.', '')}"}
 
-    launches_per_step = 2 + (1 if cast_pass else 0)
+    launches_per_step = 3 if (owner or cast_pass) else 2
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
@@ -425,7 +449,7 @@ def main(argv=None) -> int:
             "config": config_dict(preset, dtype, world),
             "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,
             "fwd_bwd_us": (fwd_mean + bwd_mean) * 1e3,
-            "fp32_grad_accum": fp32_acc,
+            "fp32_grad_accum": fp32_acc, "bwd_algo": "owner" if owner else "scatter",
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),

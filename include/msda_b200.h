@@ -57,10 +57,21 @@ typedef enum msda_status {
 } msda_status;
 
 /* Backward flags. */
-/* Accumulate grad_value in fp32 and downcast once (the fp32_grad_accum=True
- * path of src/msda_triton/ops.py:76-92). Needs a workspace of
- * msda_backward_workspace_size() bytes for fp16/bf16; fp32 ignores it. */
+/* Accumulate grad_value in fp32 and round to the value dtype once (the
+ * fp32_grad_accum=True path of src/msda_triton/ops.py:76-92). Without it the
+ * library may use native fp16/bf16 atomics; it still accumulates in fp32
+ * whenever the fp32 kernel is the faster one (see MSDA_BWD_FORCE_*). */
 #define MSDA_BWD_FP32_ACCUM 1u
+/* Force the grad_value algorithm (tests and benchmarks; default: automatic).
+ * SCATTER: one pass over sampling points with vector `red.global` adds
+ *   (fp32 workspace + downcast when MSDA_BWD_FP32_ACCUM is set for fp16/bf16,
+ *   native packed fp16x2/bf16x2 adds otherwise).
+ * OWNER: pixel-chunk ownership -- each CTA accumulates one chunk of
+ *   grad_value rows in fp32 shared memory and writes it once; no workspace,
+ *   no zero-fill, no global atomics. Falls back to SCATTER when the head dim
+ *   does not fit its tiling (D > 256). */
+#define MSDA_BWD_FORCE_SCATTER 2u
+#define MSDA_BWD_FORCE_OWNER 4u
 
 /* Library version string, e.g. "msda_b200 0.1.0 sm_100a". */
 MSDA_API const char* msda_version(void);
@@ -83,11 +94,12 @@ MSDA_API int msda_forward(const void* value, const int64_t* spatial_shapes, cons
 
 /*
  * Bytes of fp32 workspace msda_backward needs for these sizes and flags
- * (0 when no workspace is used). Replaces the allocation of the fp32
- * grad_value buffer at src/msda_triton/ops.py:76-77.
+ * (0 when the chosen algorithm uses none). Replaces the allocation of the
+ * fp32 grad_value buffer at src/msda_triton/ops.py:76-77.
  */
-MSDA_API size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int32_t num_heads,
-                                    int32_t head_dim, int32_t dtype, uint32_t flags);
+MSDA_API size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t num_queries,
+                                             int32_t num_heads, int32_t head_dim, int32_t num_levels,
+                                             int32_t num_points, int32_t dtype, uint32_t flags);
 
 /*
  * Backward: writes grad_value (B,S,M,D), grad_sampling_locations

@@ -91,6 +91,24 @@ int kshift_of(int32_t K) {
   return s;
 }
 
+// Sampling points per value row (per head) above which the pixel-chunk owner
+// kernel's rescans cost more than the scatter's atomics: each owner CTA scans
+// all points of its level, so owner work grows with (S / P) * Q * K while the
+// scatter's grows with Q * L * K.
+constexpr double kOwnerMaxPointsPerRow = 1.0;
+
+enum class Algo { kScatterNative, kScatterF32, kOwner };
+
+Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
+  const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
+  const Algo scatter = fp32_ws ? Algo::kScatterF32 : Algo::kScatterNative;
+  if (flags & MSDA_BWD_FORCE_SCATTER) return scatter;
+  if (!owner_ok) return scatter;
+  if (flags & MSDA_BWD_FORCE_OWNER) return Algo::kOwner;
+  const double density = (double)s.Q * s.L * s.K / (double)s.S;
+  return density <= kOwnerMaxPointsPerRow ? Algo::kOwner : scatter;
+}
+
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -98,6 +116,29 @@ int sm_count() {
 }
 
 }  // namespace
+
+namespace msda {
+
+bool plan_owner(int64_t S, int64_t Q, int D, int es, bool out_aligned16, OwnerPlan* plan) {
+  if (D > 256) return false;
+  plan->ch = D <= 32 ? 1 : D <= 64 ? 2 : D <= 128 ? 4 : 8;
+  // fp32 tile of ~32 KB per CTA.
+  int P = 8192 / D;
+  if (P < 16) P = 16;
+  plan->P = P;
+  const int64_t nchunks = (S + P - 1) / P;
+  if (nchunks > 0x7fffffff) return false;
+  plan->nchunks = (int)nchunks;
+  const int v16 = 16 / es;
+  plan->ovec = (D % v16 == 0 && out_aligned16) ? v16 : 1;
+  const size_t base = (size_t)P * D * sizeof(float) + (size_t)kOwnerQueue * sizeof(OwnerHit);
+  const size_t stage_bytes = (size_t)Q * D * es;
+  plan->stage = stage_bytes <= 32 * 1024;
+  plan->smem = base + (plan->stage ? stage_bytes : 0);
+  return true;
+}
+
+}  // namespace msda
 
 extern "C" {
 
@@ -144,10 +185,23 @@ int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t
   return succeed();
 }
 
-size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int32_t num_heads,
-                                    int32_t head_dim, int32_t dtype, uint32_t flags) {
-  if (!(flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32 || elem_size(dtype) == 0) return 0;
-  if (batch <= 0 || num_values <= 0 || num_heads <= 0 || head_dim <= 0) return 0;
+static bool owner_possible(const Shape& s, int es, msda::OwnerPlan* plan) {
+  // The owner grid is (chunks, B*M); gridDim.y is limited to 65535.
+  if (s.B * s.M > 65535) return false;
+  return msda::plan_owner(s.S, s.Q, s.D, es, true, plan);
+}
+
+size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t num_queries,
+                                    int32_t num_heads, int32_t head_dim, int32_t num_levels,
+                                    int32_t num_points, int32_t dtype, uint32_t flags) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  const int es = elem_size(dtype);
+  if (es == 0 || batch <= 0 || num_queries <= 0 || num_values <= 0 || num_heads <= 0 ||
+      head_dim <= 0 || num_levels <= 0 || num_points <= 0)
+    return 0;
+  msda::OwnerPlan plan;
+  const Algo a = choose_algo(s, dtype, flags, owner_possible(s, es, &plan));
+  if (a != Algo::kScatterF32) return 0;
   return (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim * sizeof(float);
 }
 
@@ -179,8 +233,12 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
       !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8))
     return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: misaligned buffer (locations need %d-byte alignment)", 2 * es);
 
-  const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
-  const size_t ws_need = msda_backward_workspace_size(batch, num_values, num_heads, head_dim, dtype, flags);
+  msda::OwnerPlan plan;
+  const bool owner_ok = owner_possible(s, es, &plan);
+  const Algo algo = choose_algo(s, dtype, flags, owner_ok);
+  const bool fp32_ws = algo == Algo::kScatterF32;
+  const size_t ws_need = msda_backward_workspace_size(batch, num_values, num_queries, num_heads,
+                                                      head_dim, num_levels, num_points, dtype, flags);
   if (fp32_ws) {
     if (!workspace || workspace_bytes < ws_need)
       return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: fp32 accumulation needs a workspace of %zu bytes (got %zu)", ws_need, workspace_bytes);
@@ -189,11 +247,15 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   }
   void* target = fp32_ws ? workspace : grad_value;
   msda::Cfg cfg;
-  const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) && aligned(target, 16);
+  const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) &&
+                      (algo == Algo::kOwner || aligned(target, 16));
   if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
 
-  cudaError_t e = cudaMemsetAsync(target, 0, fp32_ws ? ws_need : gv_bytes, st);
-  if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
+  cudaError_t e;
+  if (algo != Algo::kOwner) {
+    e = cudaMemsetAsync(target, 0, fp32_ws ? ws_need : gv_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
+  }
 
   msda::OpParams p{};
   p.value = value;
@@ -202,19 +264,29 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   p.loc = sampling_locations;
   p.attn = attention_weights;
   p.grad_out = grad_output;
-  p.grad_value = target;
+  p.grad_value = algo == Algo::kOwner ? grad_value : target;
   p.grad_loc = grad_sampling_locations;
   p.grad_attn = grad_attention_weights;
   p.B = s.B; p.S = s.S; p.Q = s.Q;
   p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
   p.kshift = kshift_of(s.K);
   p.BQM = s.B * s.Q * s.M;
+  const bool scatter = algo != Algo::kOwner;
   switch (dtype) {
-    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, true, st); break;
-    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, fp32_ws, st); break;
-    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, fp32_ws, st); break;
+    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, scatter, true, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, scatter, fp32_ws, st); break;
+    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, scatter, fp32_ws, st); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
+  if (algo == Algo::kOwner) {
+    plan.ovec = (aligned(grad_value, 16) && s.D % (16 / es) == 0) ? 16 / es : 1;
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = msda::launch_owner<float>(p, plan, st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_owner<__half>(p, plan, st); break;
+      default: e = msda::launch_owner<__nv_bfloat16>(p, plan, st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward grad_value launch");
+  }
   if (fp32_ws) {
     const int64_t n = s.B * s.S * s.M * s.D;
     const bool cast_vec = aligned(grad_value, 16);

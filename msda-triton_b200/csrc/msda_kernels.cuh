@@ -271,6 +271,174 @@ __global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// grad_value by pixel-chunk ownership (no atomics in global memory, no
+// workspace, no zero-fill, no downcast pass).
+//
+// CTA (chunk c, head-slice bm = b*M + m) owns grad_value[b, p0:p1, m, :]
+// (p0 = c*P) as an fp32 tile in shared memory. For every level overlapping
+// [p0, p1) it scans that head's Q*K sampling points of the level, keeps the
+// points with at least one bilinear corner inside the chunk in a shared queue,
+// then adds a * w_c * grad_out[b, q, m, :] into the tile with shared-memory
+// atomics (lanes over D: one warp instruction per corner row, conflict-free).
+// Finally the tile is written out once, densely, in the value dtype -- every
+// grad_value element is written exactly once by exactly one CTA.
+//
+// When a chunk collects many points per query, the (b, :, m, :) slice of
+// grad_out is staged in shared memory once instead of being gathered from L2
+// per point.
+// ---------------------------------------------------------------------------
+struct OwnerHit {
+  int q;
+  int rel00;     // pixel of corner 0 minus p0
+  unsigned mask; // bit c: corner c lies inside [p0, p1)
+  int W;
+  float coef[4]; // a * w_c
+};
+
+constexpr int kOwnerThreads = 256;
+constexpr int kOwnerQueue = 512;   // hits per scan batch (one per thread slot, two slots per thread)
+constexpr int kOwnerBatch = 512;   // sampling points scanned per batch
+constexpr int kOwnerHitsPerWarp = 4;
+
+template <typename T, int CH, int OVEC>
+__global__ void __launch_bounds__(kOwnerThreads) msda_bwd_value_owner_kernel(const OpParams p, int P,
+                                                                           int stage_limit) {
+  extern __shared__ float4 owner_smem[];
+  float* acc = reinterpret_cast<float*>(owner_smem);                 // P * D floats
+  OwnerHit* queue = reinterpret_cast<OwnerHit*>(acc + (size_t)P * p.D);  // kOwnerQueue
+  T* gstage = reinterpret_cast<T*>(queue + kOwnerQueue);             // Q * D (optional)
+  __shared__ LevelInfo lv[kMaxLevels];
+  __shared__ int qcount;
+  __shared__ int staged;
+  load_levels(p.shapes, p.starts, p.L, p.S, lv);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kOwnerThreads / 32;
+  const int D = p.D;
+  const int64_t p0 = (int64_t)blockIdx.x * P;
+  const int64_t p1 = min(p0 + P, p.S);
+  const int npix = (int)(p1 - p0);
+  const int bm = blockIdx.y;
+  const int64_t b = bm / p.M;
+  const int m = bm % p.M;
+  const int LK = p.L * p.K;
+  const int64_t QK = p.Q * (int64_t)p.K;
+
+  for (int i = tid; i < npix * D; i += kOwnerThreads) acc[i] = 0.f;
+  if (tid == 0) {
+    qcount = 0;
+    staged = 0;
+  }
+  __syncthreads();
+
+  const T* gout = reinterpret_cast<const T*>(p.grad_out);
+  const T* locp = reinterpret_cast<const T*>(p.loc);
+  const T* attp = reinterpret_cast<const T*>(p.attn);
+
+  for (int l = 0; l < p.L; ++l) {
+    const LevelInfo L = lv[l];
+    if (L.W == 0 || L.start >= p1 || (int64_t)L.start + (int64_t)L.H * L.W <= p0) continue;
+    for (int64_t base = 0; base < QK; base += kOwnerBatch) {
+      // ---- scan: queue the points with a corner inside the chunk ----------
+      for (int j = tid; j < kOwnerBatch; j += kOwnerThreads) {
+        const int64_t i = base + j;
+        if (i >= QK) break;
+        const int64_t q = p.kshift >= 0 ? (i >> p.kshift) : (i / p.K);
+        const int k = (int)(i - q * p.K);
+        const int64_t qm = (b * p.Q + q) * p.M + m;
+        const int64_t sidx = qm * LK + l * p.K + k;
+        const float2 xy = load_pair(locp + 2 * sidx);
+        const Bilinear bl = resolve(xy.x, xy.y, L);
+        unsigned mask = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (((bl.valid >> c) & 1u) && bl.pix[c] >= p0 && bl.pix[c] < p1) mask |= 1u << c;
+        if (mask) {
+          const float a = to_f32(attp[sidx]);
+          const int slot = atomicAdd(&qcount, 1);
+          OwnerHit h;
+          h.q = (int)q;
+          h.rel00 = (int)(bl.pix[0] - p0);
+          h.mask = mask;
+          h.W = L.W;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) h.coef[c] = a * bl.w[c];
+          queue[slot] = h;
+        }
+      }
+      __syncthreads();
+      const int n = qcount;
+      // ---- stage grad_out[b, :, m, :] once if this chunk is busy ----------
+      if (!staged && stage_limit > 0 && n * 4 >= p.Q) {
+        const int64_t rows = p.Q;
+        for (int64_t e = tid; e < rows * D; e += kOwnerThreads) {
+          const int64_t q = e / D;
+          const int d = (int)(e - q * D);
+          gstage[e] = gout[((b * p.Q + q) * p.M + m) * D + d];
+        }
+        __syncthreads();
+        if (tid == 0) staged = 1;
+      }
+      const bool use_stage = staged || (stage_limit > 0 && n * 4 >= p.Q);
+      // ---- accumulate: lanes over D, kOwnerHitsPerWarp points in flight ---
+      for (int h0 = warp * kOwnerHitsPerWarp; h0 < n; h0 += NW * kOwnerHitsPerWarp) {
+        float gv[kOwnerHitsPerWarp][CH];
+#pragma unroll
+        for (int u = 0; u < kOwnerHitsPerWarp; ++u) {
+          const int h = h0 + u;
+          const int q = h < n ? queue[h].q : 0;
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const int d = lane + 32 * c;
+            float v = 0.f;
+            if (h < n && d < D) {
+              v = use_stage ? to_f32(gstage[(int64_t)q * D + d])
+                            : to_f32(__ldg(gout + ((b * p.Q + q) * p.M + m) * D + d));
+            }
+            gv[u][c] = v;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kOwnerHitsPerWarp; ++u) {
+          const int h = h0 + u;
+          if (h >= n) break;
+          const OwnerHit hit = queue[h];
+          const int rel[4] = {hit.rel00, hit.rel00 + 1, hit.rel00 + hit.W, hit.rel00 + hit.W + 1};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (!((hit.mask >> c) & 1u)) continue;
+            float* row = acc + (size_t)rel[c] * D;
+#pragma unroll
+            for (int cc = 0; cc < CH; ++cc) {
+              const int d = lane + 32 * cc;
+              if (d < D) atomicAdd(row + d, hit.coef[c] * gv[u][cc]);
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (tid == 0) qcount = 0;
+      __syncthreads();
+    }
+  }
+
+  // ---- write the tile once (dense, value dtype) ---------------------------
+  T* gvout = reinterpret_cast<T*>(p.grad_value);
+  const int64_t rs = (int64_t)p.M * D;
+  const int64_t head0 = ((b * p.S + p0) * p.M + m) * D;
+  const int nvec = npix * D / OVEC;
+  for (int e = tid; e < nvec; e += kOwnerThreads) {
+    const int flat = e * OVEC;
+    const int r = flat / D;
+    const int d = flat - r * D;
+    float v[OVEC];
+#pragma unroll
+    for (int k = 0; k < OVEC; ++k) v[k] = acc[flat + k];
+    store_vec<T, OVEC>(gvout + head0 + r * rs + d, v);
+  }
+}
+
 // fp32 accumulation buffer -> value dtype (the downcast of src/msda_triton/ops.py:91-92).
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict__ src, T* __restrict__ dst,

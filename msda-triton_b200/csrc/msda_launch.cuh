@@ -18,8 +18,25 @@ constexpr int kWarpsPerCta = 8;
 
 template <typename T>
 cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
+// Backward over sampling points: grad_loc / grad_attn, plus (scatter=true) the
+// grad_value scatter with vector `red` adds into p.grad_value (fp32 when
+// fp32_scatter, else the value dtype).
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool fp32_scatter, cudaStream_t st);
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool fp32_scatter,
+                            cudaStream_t st);
+
+// grad_value by pixel-chunk ownership (see msda_bwd_value_owner_kernel).
+struct OwnerPlan {
+  int P;          // pixels per chunk
+  int nchunks;
+  int ch;         // channels per lane (D <= 32 * ch)
+  int ovec;       // output vector width (elements)
+  bool stage;     // grad_out slice staged in shared memory
+  size_t smem;    // dynamic shared memory bytes
+};
+bool plan_owner(int64_t S, int64_t Q, int D, int es, bool out_aligned16, OwnerPlan* plan);
+template <typename T>
+cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st);
 template <typename T>
 cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st);
 
@@ -52,14 +69,14 @@ static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st
   return cudaErrorInvalidConfiguration;
 }
 
-template <typename T, typename A, int VEC>
+template <typename T, typename A, int VEC, bool SCATTER>
 static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
-#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                         \
-  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                        \
-    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, NB_, true><<<grid, block, 0, st>>>(p); \
-    return cudaGetLastError();                                                                 \
+#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                            \
+  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                           \
+    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, NB_, SCATTER><<<grid, block, 0, st>>>(p); \
+    return cudaGetLastError();                                                                    \
   }
   MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
 #undef MSDA_BWD_CASE
@@ -75,15 +92,49 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool fp32_scatter, cudaStream_t st) {
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool fp32_scatter,
+                            cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
-  if (fp32_scatter || sizeof(T) == 4) {
-    if (c.vec == V16) return bwd_by_shape<T, float, V16>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, float, 1>(p, c, st);
+  if (!scatter) {
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, false>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, false>(p, c, st);
+  } else if (fp32_scatter || sizeof(T) == 4) {
+    if (c.vec == V16) return bwd_by_shape<T, float, V16, true>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, float, 1, true>(p, c, st);
   } else {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, true>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, true>(p, c, st);
   }
+  return cudaErrorInvalidConfiguration;
+}
+
+template <typename T, int CH, int OVEC>
+static cudaError_t owner_launch(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
+  auto kern = msda_bwd_value_owner_kernel<T, CH, OVEC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)plan.smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)plan.nchunks, (unsigned)(p.B * p.M));
+  kern<<<grid, kOwnerThreads, plan.smem, st>>>(p, plan.P, plan.stage ? 1 : 0);
+  return cudaGetLastError();
+}
+
+template <typename T, int OVEC>
+static cudaError_t owner_by_ch(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
+  switch (plan.ch) {
+    case 1: return owner_launch<T, 1, OVEC>(p, plan, st);
+    case 2: return owner_launch<T, 2, OVEC>(p, plan, st);
+    case 4: return owner_launch<T, 4, OVEC>(p, plan, st);
+    case 8: return owner_launch<T, 8, OVEC>(p, plan, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
+template <typename T>
+cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  if (plan.ovec == V16) return owner_by_ch<T, V16>(p, plan, st);
+  if (plan.ovec == 1) return owner_by_ch<T, 1>(p, plan, st);
   return cudaErrorInvalidConfiguration;
 }
 
@@ -102,9 +153,10 @@ cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int nu
   return cudaGetLastError();
 }
 
-#define MSDA_INSTANTIATE(T)                                                                 \
-  template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);        \
-  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, bool, cudaStream_t); \
+#define MSDA_INSTANTIATE(T)                                                                       \
+  template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
+  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, bool, bool, cudaStream_t); \
+  template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);
 
 #endif  // MSDA_LAUNCH_IMPL

@@ -23,6 +23,8 @@ MSDA_DTYPE_F16 = 1
 MSDA_DTYPE_BF16 = 2
 
 MSDA_BWD_FP32_ACCUM = 1
+MSDA_BWD_FORCE_SCATTER = 2
+MSDA_BWD_FORCE_OWNER = 4
 
 # Every symbol include/msda_b200.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p
@@ -35,7 +37,8 @@ SIGNATURES = {
         ctypes.c_int,
         [_VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _VP],
     ),
-    "msda_backward_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I32, _I32, _I32, ctypes.c_uint32]),
+    "msda_backward_workspace_size": (
+        ctypes.c_size_t, [_I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, ctypes.c_uint32]),
     "msda_backward": (
         ctypes.c_int,
         [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t,

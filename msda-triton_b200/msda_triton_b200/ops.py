@@ -34,8 +34,11 @@ def _use_fp32_grad_accum(value: torch.Tensor) -> bool:
     default: a native bf16/fp16 add rounds the running sum at every hit, and
     at encoder density (about 1300 hits per coarse-level element) that error
     exceeds 1e-2 relative. fp32 inputs always accumulate in fp32, so the flag
-    only matters for fp16/bf16; ``fp32_grad_accum=False`` still selects the
-    native packed f16x2/bf16x2 `red` path explicitly.
+    only matters for fp16/bf16. ``fp32_grad_accum=False`` permits the native
+    packed f16x2/bf16x2 `red` path; where sampling is sparse (fewer sampling
+    points than value rows per head, e.g. a DETR decoder) the library uses
+    its pixel-chunk owner kernel either way, which accumulates in fp32 and is
+    the faster of the two there.
     """
     return value.dtype != torch.float32
 
@@ -70,7 +73,7 @@ def _forward(value, spatial_shapes, level_start_index, sampling_locations, atten
 
 
 def _backward(value, spatial_shapes, level_start_index, sampling_locations, attention_weights,
-              grad_out, fp32_grad_accum):
+              grad_out, fp32_grad_accum, algo_flags=0):
     B, S, M, D = value.shape
     _, Q, _, L, K, _ = sampling_locations.shape
     grad_value = torch.empty_like(value)
@@ -78,8 +81,8 @@ def _backward(value, spatial_shapes, level_start_index, sampling_locations, atte
     grad_attn = torch.empty_like(attention_weights)
     lib = _lib.load()
     code = _DTYPE_CODE[value.dtype]
-    flags = _lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0
-    ws_bytes = lib.msda_backward_workspace_size(B, S, M, D, code, flags)
+    flags = (_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0) | algo_flags
+    ws_bytes = lib.msda_backward_workspace_size(B, S, Q, M, D, L, K, code, flags)
     workspace = (
         torch.empty(ws_bytes, dtype=torch.uint8, device=value.device) if ws_bytes else None
     )

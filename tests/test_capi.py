@@ -73,10 +73,22 @@ def test_abi_rejects_bad_arguments_before_any_device_work():
 def test_abi_workspace_size():
     lib = _lib.load()
     f = _lib.MSDA_BWD_FP32_ACCUM
-    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_BF16, f) == 2 * 10 * 3 * 8 * 4
-    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_F16, f) == 2 * 10 * 3 * 8 * 4
-    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_F32, f) == 0
-    assert lib.msda_backward_workspace_size(2, 10, 3, 8, _lib.MSDA_DTYPE_BF16, 0) == 0
+    ws = lambda B, S, Q, M, D, L, K, dt, fl: lib.msda_backward_workspace_size(  # noqa: E731
+        B, S, Q, M, D, L, K, dt, fl)
+    full = 2 * 10 * 3 * 8 * 4
+    # Dense sampling (Q*L*K per value row > 1) takes the scatter path: fp32
+    # accumulation of fp16/bf16 needs the workspace, fp32 and native do not.
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == full
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F16, f) == full
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F32, f) == 0
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, 0) == 0
+    # Sparse sampling takes the owner path, which needs no workspace ...
+    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == 0
+    # ... unless the scatter path is forced; forcing the owner path drops it.
+    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_SCATTER) == full
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 0
+    # Head dims beyond the owner tiling always scatter.
+    assert ws(1, 10, 2, 1, 512, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 10 * 512 * 4
 
 
 def test_abi_backward_needs_workspace_for_fp32_accumulation():
@@ -84,7 +96,7 @@ def test_abi_backward_needs_workspace_for_fp32_accumulation():
     vp = ctypes.c_void_p
     rc = lib.msda_backward(vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16),
                            vp(0), 0, 1, 4, 1, 1, 8, 1, 1, _lib.MSDA_DTYPE_BF16,
-                           _lib.MSDA_BWD_FP32_ACCUM, vp(0))
+                           _lib.MSDA_BWD_FP32_ACCUM | _lib.MSDA_BWD_FORCE_SCATTER, vp(0))
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert b"workspace" in lib.msda_last_error()
 

@@ -404,3 +404,71 @@ def test_side_stream_and_graph_capture():
     _, (gv_ref, _, _) = run_op(*args, static_g)
     torch.testing.assert_close(static_out.detach(), ref_out)
     close(v.grad, gv_ref, STRICT_TOL[torch.bfloat16], "grad_value (graph)")
+
+
+# ---------------------------------------------------------------------------
+# Every grad_value algorithm, forced through the C ABI flags
+# ---------------------------------------------------------------------------
+from msda_triton_b200 import _lib as _clib  # noqa: E402
+from msda_triton_b200 import ops as _ops  # noqa: E402
+
+ALGOS = {
+    "owner": (_clib.MSDA_BWD_FORCE_OWNER, True),
+    "scatter_fp32": (_clib.MSDA_BWD_FORCE_SCATTER, True),
+    "scatter_native": (_clib.MSDA_BWD_FORCE_SCATTER, False),
+}
+ALGO_CASES = [
+    ("decoder_case", dict(B=2, Q=100, M=4, D=32, K=4, shapes=[(24, 32), (12, 16), (6, 8)]), 0.0, 1.0),
+    ("nonpow2", dict(B=2, Q=33, M=2, D=24, K=3, shapes=[(10, 14), (5, 7)]), 0.0, 1.0),
+    ("wide_oob", dict(B=1, Q=64, M=8, D=64, K=4, shapes=[(16, 16), (8, 8)]), -0.5, 1.5),
+    ("odd_d", dict(B=2, Q=9, M=3, D=5, K=2, shapes=[(7, 9), (4, 5)]), -0.2, 1.2),
+    ("d128", dict(B=1, Q=40, M=2, D=128, K=4, shapes=[(20, 30), (10, 15)]), 0.0, 1.0),
+    ("one_pixel_levels", dict(B=2, Q=50, M=2, D=32, K=4, shapes=[(1, 1), (2, 1), (1, 3)]), -0.3, 1.3),
+]
+
+
+@pytest.mark.parametrize("algo", list(ALGOS))
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,kw,lo,hi", ALGO_CASES, ids=[c[0] for c in ALGO_CASES])
+def test_backward_algorithms(name, kw, lo, hi, dtype, algo):
+    flags, fp32 = ALGOS[algo]
+    value, shapes, starts, loc, attn = cases.make_inputs(**kw, dtype=dtype, device=DEV, loc_lo=lo,
+                                                         loc_hi=hi)
+    B, Q, M, D = value.shape[0], loc.shape[1], value.shape[2], value.shape[3]
+    g = cases.grad_output_like(torch.empty(B, Q, M, D, device=DEV, dtype=dtype))
+    got = _ops._backward(value, shapes, starts, loc, attn, g, fp32, flags)
+    _, ref = oracle64(value, shapes, starts, loc, attn, g)
+    gv_tol = REF_BWD_TOL[dtype] if (algo == "scatter_native" and dtype != torch.float32) else None
+    cases.assert_grads_close(got, ref, loc, shapes, STRICT_TOL[dtype], gv_tol=gv_tol, what=algo)
+
+
+@pytest.mark.parametrize("algo", ["owner", "scatter_fp32"])
+@pytest.mark.parametrize("name", ["decoder", "small"])
+def test_backward_algorithms_at_baseline_points(name, algo):
+    flags, fp32 = ALGOS[algo]
+    x = presets.make_inputs(presets.get(name), device=DEV, seed=2)
+    v, s, st = x["value"], x["spatial_shapes"], x["level_start_index"]
+    l, a = x["sampling_locations"], x["attention_weights"]
+    g = x["grad_output"].view(v.shape[0], l.shape[1], v.shape[2], v.shape[3])
+    got = _ops._backward(v, s, st, l, a, g, fp32, flags)
+    _, ref = oracle64(v, s, st, l, a, g)
+    cases.assert_grads_close(got, ref, l, s, STRICT_TOL[v.dtype], what=f"{name}/{algo}")
+
+
+def test_owner_writes_every_grad_value_element():
+    """The owner path writes grad_value without a zero-fill: rows no sampling
+    point touches (padding rows past the last level included) must come back
+    as exact zeros even when the output buffer starts as garbage."""
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=3, M=2, D=32, shapes=[(9, 11), (4, 5)], K=2, dtype=torch.bfloat16, device=DEV)
+    pad = torch.randn(2, 17, 2, 32, device=DEV, dtype=torch.bfloat16)
+    value = torch.cat([value, pad], 1)  # S = 119 + 17 rows, the last 17 unused
+    g = cases.grad_output_like(torch.empty(2, 3, 2, 32, device=DEV, dtype=torch.bfloat16))
+    torch.cuda.empty_cache()
+    junk = torch.full((value.numel() * 4,), float("nan"), device=DEV)
+    del junk  # leave NaN garbage in the caching allocator's blocks
+    gv, _, _ = _ops._backward(value, shapes, starts, loc, attn, g, True, _clib.MSDA_BWD_FORCE_OWNER)
+    assert torch.isfinite(gv).all()
+    assert (gv[:, 119:] == 0).all()
+    _, ref = oracle64(value, shapes, starts, loc, attn, g)
+    close(gv, ref[0], STRICT_TOL[torch.bfloat16], "grad_value")
