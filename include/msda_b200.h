@@ -118,6 +118,45 @@ MSDA_API int msda_backward(const void* value, const int64_t* spatial_shapes, con
                   int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
                   uint32_t flags, void* stream);
 
+/*
+ * Backward for callers that cannot allocate device memory (no counterpart in
+ * the reference, which always allocates its fp32 buffer with torch).
+ *
+ * A caller that plans all device memory ahead of time and may not call
+ * cudaMalloc while it runs (a TensorRT-style plugin's enqueue, code running
+ * under CUDA graph capture in a mode that makes allocation an error, an
+ * embedder without a device allocator) cannot hand msda_backward the fp32
+ * workspace it needs for fp32 accumulation of fp16/bf16 gradients. This entry
+ * point computes the same three gradients as msda_backward with
+ * MSDA_BWD_FP32_ACCUM | MSDA_BWD_FORCE_SCATTER, taking that workspace from a
+ * static device array of MSDA_NOALLOC_SCRATCH_BYTES inside the library. It
+ * calls no cudaMalloc/cudaFree and no allocating library routine; the caller
+ * still passes every input and output buffer.
+ *
+ * Limits and caveats:
+ * - B*S*M*D*4 bytes (the fp32 accumulation buffer) must fit in
+ *   MSDA_NOALLOC_SCRATCH_BYTES (16 MiB, i.e. 4M grad_value elements) for
+ *   fp16/bf16; larger sizes fail with MSDA_ERR_INVALID_ARGUMENT. fp32 inputs
+ *   accumulate directly in grad_value and use no scratch.
+ * - Every GPU that loads the library holds the 16 MiB array until exit.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress, with that device current); make that first call
+ *   before any stream capture. The stream must belong to the current device.
+ * - All calls on a device share the one array (each call zeroes what it
+ *   uses): calls that overlap on the GPU -- on different streams, or from
+ *   different threads -- race and corrupt each other's gradients. Serialise
+ *   them on one stream.
+ */
+#define MSDA_NOALLOC_SCRATCH_BYTES (16u << 20)
+MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_shapes,
+                                   const int64_t* level_start_index, const void* sampling_locations,
+                                   const void* attention_weights, const void* grad_output,
+                                   void* grad_value, void* grad_sampling_locations,
+                                   void* grad_attention_weights, int64_t batch, int64_t num_values,
+                                   int64_t num_queries, int32_t num_heads, int32_t head_dim,
+                                   int32_t num_levels, int32_t num_points, int32_t dtype,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,6 +119,10 @@ int sm_count() {
 
 namespace msda {
 
+// Lets other translation units of the library (msda_noalloc.cu) report a
+// failure through msda_last_error(). Not exported.
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 bool plan_owner(int64_t S, int64_t Q, int D, int es, bool out_aligned16, OwnerPlan* plan) {
   if (D > 256) return false;
   plan->ch = D <= 32 ? 1 : D <= 64 ? 2 : D <= 128 ? 4 : 8;

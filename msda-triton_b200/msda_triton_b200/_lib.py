@@ -44,7 +44,18 @@ SIGNATURES = {
         [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t,
          _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, ctypes.c_uint32, _VP],
     ),
+    # The backward for callers that cannot allocate: same as msda_backward
+    # without the workspace arguments (fp32 scratch from a static device array).
+    "msda_backward_noalloc": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+         _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _VP],
+    ),
 }
+
+# Size of the static scratch behind msda_backward_noalloc
+# (MSDA_NOALLOC_SCRATCH_BYTES in include/msda_b200.h).
+MSDA_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

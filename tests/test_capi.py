@@ -26,7 +26,8 @@ def _declared():
 
 def test_header_declares_the_abi():
     assert set(_declared()) == {"msda_version", "msda_last_error", "msda_forward",
-                                "msda_backward_workspace_size", "msda_backward"}
+                                "msda_backward_workspace_size", "msda_backward",
+                                "msda_backward_noalloc"}
 
 
 def test_library_exports_every_declared_symbol():
