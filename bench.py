@@ -45,6 +45,7 @@ from msda_triton_b200 import multi_scale_deformable_attention, presets  # noqa: 
 from msda_triton_b200 import ops as msda_ops  # noqa: E402
 
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+L2_DRAIN_BYTES = 256 << 20
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "MSDA fwd+bwd µs, queries/s & % HBM roofline, bf16 decoder/encoder, 1–8 B200"
 NOMINAL_HBM_GBS = 8000.0
@@ -188,6 +189,7 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
             x["attention_weights"])
     g = x["grad_output"].reshape(x["value"].shape[0], -1, x["value"].shape[2], x["value"].shape[3])
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    drain = torch.ones(L2_DRAIN_BYTES // 4, dtype=torch.float32, device="cuda")
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):  # warm-up outside capture (allocator, lazy loading)
@@ -212,7 +214,11 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
         run_b = lambda: msda_ops._backward(*args, g, fp32_acc, algo_flags)  # noqa: E731
 
     def one(e):
+        # Flush: write 512 MiB (evicts everything of ours from L2), then read
+        # 256 MiB so the flush's own dirty lines are written back before the
+        # timed region instead of inside it.
         flush.fill_(1)
+        drain.sum()
         e[0].record()
         run_f()
         e[1].record()
@@ -331,7 +337,7 @@ def config_dict(preset, dtype, n):
             "head_dim": preset.D, "levels": preset.L, "points": preset.K,
             "spatial_shapes": [list(s) for s in preset.shapes], "S": preset.S,
             "dtype": str(dtype).replace("torch.", ""), "parallelism": f"batch-sharded x{n}",
-            "l2": "flushed (512 MiB write) before every timed step"}
+            "l2": "flushed before every timed step (512 MiB write, then 256 MiB read to drain dirty lines)"}
 
 
 def main(argv=None) -> int:
@@ -412,8 +418,7 @@ def main(argv=None) -> int:
         B, S, Q, M, D, L, K, msda_ops._DTYPE_CODE[x["value"].dtype],
         (msda_ops._lib.MSDA_BWD_FP32_ACCUM if fp32_acc else 0) | algo_flags)
     cast_pass = ws > 0
-    owner = (args.bwd_algo == "owner" or
-             (args.bwd_algo == "auto" and Q * L * K / S <= 1.0 and D <= 256))
+    owner = args.bwd_algo == "owner"
     e_acc = 4 if cast_pass else e
     fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass)
     peak, peak_kind = load_peaks()

@@ -66,10 +66,11 @@ typedef enum msda_status {
  * SCATTER: one pass over sampling points with vector `red.global` adds
  *   (fp32 workspace + downcast when MSDA_BWD_FP32_ACCUM is set for fp16/bf16,
  *   native packed fp16x2/bf16x2 adds otherwise).
- * OWNER: pixel-chunk ownership -- each CTA accumulates one chunk of
- *   grad_value rows in fp32 shared memory and writes it once; no workspace,
- *   no zero-fill, no global atomics. Falls back to SCATTER when the head dim
- *   does not fit its tiling (D > 256). */
+ * OWNER: pixel-chunk ownership -- each CTA accumulates chunks of grad_value
+ *   rows in fp32 shared memory and writes each once; no workspace, no
+ *   zero-fill, no global atomics. Falls back to SCATTER when a head slice has
+ *   more sampling points (L*Q*K) than its shared-memory point list holds
+ *   (65535) or its shared-memory plan does not fit. */
 #define MSDA_BWD_FORCE_SCATTER 2u
 #define MSDA_BWD_FORCE_OWNER 4u
 

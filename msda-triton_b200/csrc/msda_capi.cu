@@ -91,11 +91,12 @@ int kshift_of(int32_t K) {
   return s;
 }
 
-// Sampling points per value row (per head) above which the pixel-chunk owner
-// kernel's rescans cost more than the scatter's atomics: each owner CTA scans
-// all points of its level, so owner work grows with (S / P) * Q * K while the
-// scatter's grows with Q * L * K.
-constexpr double kOwnerMaxPointsPerRow = 1.0;
+// Sampling points per value row (per head) below which the automatic choice
+// takes the pixel-chunk owner kernel. Disabled (0): on B200 the owner kernel's
+// shared-memory accumulation is slower than the scatter's L2 reductions at
+// every measured operating point; it stays available through
+// MSDA_BWD_FORCE_OWNER (deterministic grad_value).
+constexpr double kOwnerMaxPointsPerRow = 0.0;
 
 enum class Algo { kScatterNative, kScatterF32, kOwner };
 
@@ -106,7 +107,7 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
   if (!owner_ok) return scatter;
   if (flags & MSDA_BWD_FORCE_OWNER) return Algo::kOwner;
   const double density = (double)s.Q * s.L * s.K / (double)s.S;
-  return density <= kOwnerMaxPointsPerRow ? Algo::kOwner : scatter;
+  return density < kOwnerMaxPointsPerRow ? Algo::kOwner : scatter;
 }
 
 int sm_count() {
@@ -123,23 +124,39 @@ namespace msda {
 // failure through msda_last_error(). Not exported.
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
-bool plan_owner(int64_t S, int64_t Q, int D, int es, bool out_aligned16, OwnerPlan* plan) {
-  if (D > 256) return false;
-  plan->ch = D <= 32 ? 1 : D <= 64 ? 2 : D <= 128 ? 4 : 8;
-  // fp32 tile of ~32 KB per CTA.
-  int P = 8192 / D;
+static size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+bool plan_owner(int64_t B, int64_t S, int64_t Q, int M, int D, int L, int K, int es,
+                int num_sms, OwnerPlan* plan) {
+  // Point indices are 16-bit.
+  const int64_t max_points = (int64_t)L * Q * K;
+  if (max_points > 65535) return false;
+  OwnerArgs& a = plan->args;
+  // fp32 tile of ~32 KB per chunk; P a multiple of 4 keeps it float4-aligned.
+  int P = (8192 / D) & ~3;
   if (P < 16) P = 16;
-  plan->P = P;
+  a.P = P;
   const int64_t nchunks = (S + P - 1) / P;
-  if (nchunks > 0x7fffffff) return false;
-  plan->nchunks = (int)nchunks;
-  const int v16 = 16 / es;
-  plan->ovec = (D % v16 == 0 && out_aligned16) ? v16 : 1;
-  const size_t base = (size_t)P * D * sizeof(float) + (size_t)kOwnerQueue * sizeof(OwnerHit);
-  const size_t stage_bytes = (size_t)Q * D * es;
-  plan->stage = stage_bytes <= 32 * 1024;
-  plan->smem = base + (plan->stage ? stage_bytes : 0);
-  return true;
+  if (nchunks > (1 << 30)) return false;
+  a.nchunks = (int)nchunks;
+  // One wave at two CTAs per SM; each CTA bins at most `seg` chunks at a time.
+  const int64_t slices = B * M;
+  int64_t per_slice = (2 * (int64_t)num_sms + slices - 1) / slices;
+  if (per_slice < 1) per_slice = 1;
+  if (per_slice > nchunks) per_slice = nchunks;
+  plan->ctas_per_slice = (int)per_slice;
+  a.seg = (int)((nchunks + per_slice - 1) / per_slice);
+  a.max_points = (int)max_points;
+  a.max_bins = a.seg * P + 2 * L + 1;
+  const size_t tile = (size_t)P * D * sizeof(float);
+  a.off_g = align16(tile);
+  a.off_pts = align16(a.off_g + (size_t)Q * D * es);
+  a.off_sorted = align16(a.off_pts + (size_t)3 * max_points * es);
+  a.off_bins = align16(a.off_sorted + (size_t)2 * max_points);
+  plan->smem = a.off_bins + (size_t)(a.max_bins + 1) * sizeof(unsigned);
+  plan->ovec = 1;
+  a.stage_vec = 0;
+  return plan->smem <= 220 * 1024;
 }
 
 }  // namespace msda
@@ -190,9 +207,9 @@ int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t
 }
 
 static bool owner_possible(const Shape& s, int es, msda::OwnerPlan* plan) {
-  // The owner grid is (chunks, B*M); gridDim.y is limited to 65535.
+  // The owner grid is (CTAs per head slice, B*M); gridDim.y is limited to 65535.
   if (s.B * s.M > 65535) return false;
-  return msda::plan_owner(s.S, s.Q, s.D, es, true, plan);
+  return msda::plan_owner(s.B, s.S, s.Q, s.M, s.D, s.L, s.K, es, sm_count(), plan);
 }
 
 size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t num_queries,
@@ -284,6 +301,7 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
   if (algo == Algo::kOwner) {
     plan.ovec = (aligned(grad_value, 16) && s.D % (16 / es) == 0) ? 16 / es : 1;
+    plan.args.stage_vec = (aligned(grad_output, 16) && (s.D * es) % 16 == 0) ? 1 : 0;
     switch (dtype) {
       case MSDA_DTYPE_F32: e = msda::launch_owner<float>(p, plan, st); break;
       case MSDA_DTYPE_F16: e = msda::launch_owner<__half>(p, plan, st); break;

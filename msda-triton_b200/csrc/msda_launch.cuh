@@ -27,14 +27,15 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool 
 
 // grad_value by pixel-chunk ownership (see msda_bwd_value_owner_kernel).
 struct OwnerPlan {
-  int P;          // pixels per chunk
-  int nchunks;
-  int ch;         // channels per lane (D <= 32 * ch)
-  int ovec;       // output vector width (elements)
-  bool stage;     // grad_out slice staged in shared memory
-  size_t smem;    // dynamic shared memory bytes
+  OwnerArgs args;
+  int ctas_per_slice;  // grid.x
+  int ovec;            // output vector width (elements)
+  size_t smem;         // dynamic shared memory bytes
 };
-bool plan_owner(int64_t S, int64_t Q, int D, int es, bool out_aligned16, OwnerPlan* plan);
+// Returns false when the owner kernel cannot take these sizes (its per-CTA
+// shared-memory arrays must hold all L*Q*K points of a head slice).
+bool plan_owner(int64_t B, int64_t S, int64_t Q, int M, int D, int L, int K, int es,
+                int num_sms, OwnerPlan* plan);
 template <typename T>
 cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st);
 template <typename T>
@@ -108,33 +109,26 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool 
   return cudaErrorInvalidConfiguration;
 }
 
-template <typename T, int CH, int OVEC>
+template <typename T, int OVEC, int DT>
 static cudaError_t owner_launch(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
-  auto kern = msda_bwd_value_owner_kernel<T, CH, OVEC>;
+  auto kern = msda_bwd_value_owner_kernel<T, OVEC, DT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)plan.smem);
   if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)plan.nchunks, (unsigned)(p.B * p.M));
-  kern<<<grid, kOwnerThreads, plan.smem, st>>>(p, plan.P, plan.stage ? 1 : 0);
+  const dim3 grid((unsigned)plan.ctas_per_slice, (unsigned)(p.B * p.M));
+  kern<<<grid, kOwnerThreads, plan.smem, st>>>(p, plan.args);
   return cudaGetLastError();
-}
-
-template <typename T, int OVEC>
-static cudaError_t owner_by_ch(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
-  switch (plan.ch) {
-    case 1: return owner_launch<T, 1, OVEC>(p, plan, st);
-    case 2: return owner_launch<T, 2, OVEC>(p, plan, st);
-    case 4: return owner_launch<T, 4, OVEC>(p, plan, st);
-    case 8: return owner_launch<T, 8, OVEC>(p, plan, st);
-    default: return cudaErrorInvalidConfiguration;
-  }
 }
 
 template <typename T>
 cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
-  if (plan.ovec == V16) return owner_by_ch<T, V16>(p, plan, st);
-  if (plan.ovec == 1) return owner_by_ch<T, 1>(p, plan, st);
+  if (plan.ovec == V16) {
+    if (p.D == 32) return owner_launch<T, V16, 32>(p, plan, st);
+    if (p.D == 64) return owner_launch<T, V16, 64>(p, plan, st);
+    return owner_launch<T, V16, 0>(p, plan, st);
+  }
+  if (plan.ovec == 1) return owner_launch<T, 1, 0>(p, plan, st);
   return cudaErrorInvalidConfiguration;
 }
 

@@ -83,13 +83,14 @@ def test_abi_workspace_size():
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F16, f) == full
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F32, f) == 0
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, 0) == 0
-    # Sparse sampling takes the owner path, which needs no workspace ...
-    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == 0
-    # ... unless the scatter path is forced; forcing the owner path drops it.
+    # The automatic choice is the scatter path; forcing the scatter path keeps
+    # the workspace, forcing the owner path (no workspace) drops it.
+    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == full
     assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_SCATTER) == full
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 0
-    # Head dims beyond the owner tiling always scatter.
-    assert ws(1, 10, 2, 1, 512, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 10 * 512 * 4
+    # More than 65535 sampling points per head slice (L*Q*K) exceed the owner
+    # kernel's shared-memory point list: it always scatters then.
+    assert ws(1, 10, 20000, 1, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 10 * 8 * 4
 
 
 def test_abi_backward_needs_workspace_for_fp32_accumulation():
