@@ -349,7 +349,7 @@ def main(argv=None) -> int:
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
-    ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner"],
+    ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner", "counted"],
                     help="force the grad_value algorithm of the device leg (default: automatic)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time direct launches instead of CUDA-graph replays")
@@ -373,7 +373,8 @@ def main(argv=None) -> int:
 
     lib = msda_ops._lib
     algo_flags = {"auto": 0, "scatter": lib.MSDA_BWD_FORCE_SCATTER,
-                  "owner": lib.MSDA_BWD_FORCE_OWNER}[args.bwd_algo]
+                  "owner": lib.MSDA_BWD_FORCE_OWNER,
+                  "counted": lib.MSDA_BWD_FORCE_COUNTED}[args.bwd_algo]
 
     # ---- device leg -------------------------------------------------------
     gf, gb, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,

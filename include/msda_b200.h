@@ -66,6 +66,12 @@ typedef enum msda_status {
  * SCATTER: one pass over sampling points with vector `red.global` adds
  *   (fp32 workspace + downcast when MSDA_BWD_FP32_ACCUM is set for fp16/bf16,
  *   native packed fp16x2/bf16x2 adds otherwise).
+ * COUNTED: hit-counted scatter -- a first pass counts the bilinear hits of
+ *   every grad_value row; rows hit once get their single contribution stored,
+ *   rows hit more often accumulate in fp32 rows of the workspace; a last pass
+ *   writes zeros / rounds the multi-hit rows. Same result as fp32
+ *   accumulation, with fp32 traffic only for the multi-hit rows (the
+ *   automatic choice for fp32 accumulation when sampling is sparse).
  * OWNER: pixel-chunk ownership -- each CTA accumulates chunks of grad_value
  *   rows in fp32 shared memory and writes each once; no workspace, no
  *   zero-fill, no global atomics. Falls back to SCATTER when a head slice has
@@ -73,6 +79,7 @@ typedef enum msda_status {
  *   (65535) or its shared-memory plan does not fit. */
 #define MSDA_BWD_FORCE_SCATTER 2u
 #define MSDA_BWD_FORCE_OWNER 4u
+#define MSDA_BWD_FORCE_COUNTED 8u
 
 /* Library version string, e.g. "msda_b200 0.1.0 sm_100a". */
 MSDA_API const char* msda_version(void);

@@ -98,16 +98,37 @@ int kshift_of(int32_t K) {
 // MSDA_BWD_FORCE_OWNER (deterministic grad_value).
 constexpr double kOwnerMaxPointsPerRow = 0.0;
 
-enum class Algo { kScatterNative, kScatterF32, kOwner };
+// Sampling points per value row (per head) up to which fp32 accumulation
+// uses the hit-counted scatter; denser sampling hits almost every row more
+// than once, and the plain fp32 scatter is cheaper.
+constexpr double kCountedMaxPointsPerRow = 2.0;
+
+enum class Algo { kScatterNative, kScatterF32, kCounted, kOwner };
 
 Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
   const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
+  const bool fp32_semantics = (flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32;
   const Algo scatter = fp32_ws ? Algo::kScatterF32 : Algo::kScatterNative;
   if (flags & MSDA_BWD_FORCE_SCATTER) return scatter;
-  if (!owner_ok) return scatter;
-  if (flags & MSDA_BWD_FORCE_OWNER) return Algo::kOwner;
+  if ((flags & MSDA_BWD_FORCE_OWNER) && owner_ok) return Algo::kOwner;
+  if (flags & MSDA_BWD_FORCE_COUNTED) return Algo::kCounted;
+  if (!fp32_semantics) return scatter;
   const double density = (double)s.Q * s.L * s.K / (double)s.S;
-  return density < kOwnerMaxPointsPerRow ? Algo::kOwner : scatter;
+  if (density <= kCountedMaxPointsPerRow) return Algo::kCounted;
+  if (owner_ok && density < kOwnerMaxPointsPerRow) return Algo::kOwner;
+  return scatter;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace of the hit-counted scatter: per-row hit counts, then (fp16/bf16
+// only) one fp32 row per grad_value row.
+size_t counted_ws_bytes(const Shape& s, int32_t dtype, size_t* acc_offset) {
+  const size_t rows = (size_t)s.B * s.S * s.M;
+  const size_t counts = align256(rows * sizeof(unsigned));
+  *acc_offset = counts;
+  if (dtype == MSDA_DTYPE_F32) return counts;
+  return counts + rows * (size_t)s.D * sizeof(float);
 }
 
 int sm_count() {
@@ -222,6 +243,10 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
     return 0;
   msda::OwnerPlan plan;
   const Algo a = choose_algo(s, dtype, flags, owner_possible(s, es, &plan));
+  if (a == Algo::kCounted) {
+    size_t off;
+    return counted_ws_bytes(s, dtype, &off);
+  }
   if (a != Algo::kScatterF32) return 0;
   return (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim * sizeof(float);
 }
@@ -258,9 +283,10 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   const bool owner_ok = owner_possible(s, es, &plan);
   const Algo algo = choose_algo(s, dtype, flags, owner_ok);
   const bool fp32_ws = algo == Algo::kScatterF32;
+  const bool counted = algo == Algo::kCounted;
   const size_t ws_need = msda_backward_workspace_size(batch, num_values, num_queries, num_heads,
                                                       head_dim, num_levels, num_points, dtype, flags);
-  if (fp32_ws) {
+  if (fp32_ws || counted) {
     if (!workspace || workspace_bytes < ws_need)
       return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: fp32 accumulation needs a workspace of %zu bytes (got %zu)", ws_need, workspace_bytes);
     if (!aligned(workspace, 16))
@@ -269,12 +295,22 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   void* target = fp32_ws ? workspace : grad_value;
   msda::Cfg cfg;
   const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) &&
-                      (algo == Algo::kOwner || aligned(target, 16));
+                      (algo == Algo::kOwner || aligned(target, 16)) &&
+                      (!counted || aligned(grad_value, 16));
   if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
 
   cudaError_t e;
-  if (algo != Algo::kOwner) {
-    e = cudaMemsetAsync(target, 0, fp32_ws ? ws_need : gv_bytes, st);
+  size_t acc_off = 0;
+  if (counted) {
+    counted_ws_bytes(s, dtype, &acc_off);
+    e = cudaMemsetAsync(workspace, 0, (size_t)s.B * s.S * s.M * sizeof(unsigned), st);
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count zero-fill");
+  } else if (algo != Algo::kOwner) {
+    const size_t zbytes = fp32_ws ? ws_need : gv_bytes;
+    if (zbytes % 16 == 0 && aligned(target, 16))
+      e = msda::launch_zero(target, zbytes, sm_count(), st);
+    else
+      e = cudaMemsetAsync(target, 0, zbytes, st);
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
   }
 
@@ -285,20 +321,42 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   p.loc = sampling_locations;
   p.attn = attention_weights;
   p.grad_out = grad_output;
-  p.grad_value = algo == Algo::kOwner ? grad_value : target;
+  p.grad_value = (algo == Algo::kOwner || counted) ? grad_value : target;
   p.grad_loc = grad_sampling_locations;
   p.grad_attn = grad_attention_weights;
+  if (counted) {
+    p.counts = static_cast<unsigned*>(workspace);
+    p.acc = dtype == MSDA_DTYPE_F32 ? static_cast<float*>(grad_value)
+                                    : reinterpret_cast<float*>(static_cast<char*>(workspace) + acc_off);
+  }
   p.B = s.B; p.S = s.S; p.Q = s.Q;
   p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
   p.kshift = kshift_of(s.K);
   p.BQM = s.B * s.Q * s.M;
-  const bool scatter = algo != Algo::kOwner;
+  if (counted) {
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, st); break;
+      default: e = msda::launch_count<__nv_bfloat16>(p, st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count launch");
+  }
+  const int mode = algo == Algo::kOwner ? msda::kNoScatter : counted ? msda::kCounted : msda::kScatter;
   switch (dtype) {
-    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, scatter, true, st); break;
-    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, scatter, fp32_ws, st); break;
-    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, scatter, fp32_ws, st); break;
+    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, true, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, fp32_ws, st); break;
+    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, mode, fp32_ws, st); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
+  if (counted) {
+    const bool fvec = aligned(grad_value, 16);
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = msda::launch_finalize<float>(p, fvec, sm_count(), st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_finalize<__half>(p, fvec, sm_count(), st); break;
+      default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, sm_count(), st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward finalize launch");
+  }
   if (algo == Algo::kOwner) {
     plan.ovec = (aligned(grad_value, 16) && s.D % (16 / es) == 0) ? 16 / es : 1;
     plan.args.stage_vec = (aligned(grad_output, 16) && (s.D * es) % 16 == 0) ? 1 : 0;

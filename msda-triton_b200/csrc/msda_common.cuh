@@ -146,12 +146,81 @@ __device__ __forceinline__ void red_add_x8(__nv_bfloat16* p, const float (&v)[8]
                : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// L2 cache policies for the scatter backward: the rows it reduces into are
+// zero-filled and reduced with evict_last, the value rows it gathers meanwhile
+// with evict_first, so the gathers do not push the reduction targets out.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void red_add_f32x4_hint(float* p, float a, float b, float c, float d,
+                                                   uint64_t pol) {
+  asm volatile("red.global.add.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(a),
+               "f"(b), "f"(c), "f"(d), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void st_zero16_hint(void* p, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %1, %1, %1}, %2;" ::"l"(p), "r"(0u),
+               "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ void red_add_scalar(float* p, float v) { atomicAdd(p, v); }
 __device__ __forceinline__ void red_add_scalar(__half* p, float v) {
   atomicAdd(p, __float2half_rn(v));
 }
 __device__ __forceinline__ void red_add_scalar(__nv_bfloat16* p, float v) {
   atomicAdd(p, __float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ void red_add_x8_hint(__half* p, const float (&v)[8], uint64_t pol) {
+  unsigned w0 = pack2(__float2half_rn(v[0]), __float2half_rn(v[1]));
+  unsigned w1 = pack2(__float2half_rn(v[2]), __float2half_rn(v[3]));
+  unsigned w2 = pack2(__float2half_rn(v[4]), __float2half_rn(v[5]));
+  unsigned w3 = pack2(__float2half_rn(v[6]), __float2half_rn(v[7]));
+  asm volatile("red.global.add.noftz.L2::cache_hint.v4.f16x2 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p),
+               "r"(w0), "r"(w1), "r"(w2), "r"(w3), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_x8_hint(__nv_bfloat16* p, const float (&v)[8], uint64_t pol) {
+  unsigned w0 = pack2(__float2bfloat16_rn(v[0]), __float2bfloat16_rn(v[1]));
+  unsigned w1 = pack2(__float2bfloat16_rn(v[2]), __float2bfloat16_rn(v[3]));
+  unsigned w2 = pack2(__float2bfloat16_rn(v[4]), __float2bfloat16_rn(v[5]));
+  unsigned w3 = pack2(__float2bfloat16_rn(v[6]), __float2bfloat16_rn(v[7]));
+  asm volatile("red.global.add.noftz.L2::cache_hint.v4.bf16x2 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p),
+               "r"(w0), "r"(w1), "r"(w2), "r"(w3), "l"(pol)
+               : "memory");
+}
+
+// As red_add_vec, with the L2 policy `pol` on the 16-byte forms.
+template <typename A, int VEC>
+__device__ __forceinline__ void red_add_vec_hint(A* p, const float (&v)[VEC], uint64_t pol) {
+  if constexpr (sizeof(A) == 4 && VEC % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < VEC; i += 4)
+      red_add_f32x4_hint(reinterpret_cast<float*>(p) + i, v[i], v[i + 1], v[i + 2], v[i + 3], pol);
+  } else if constexpr (sizeof(A) == 2 && VEC == 8) {
+    red_add_x8_hint(p, v, pol);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) red_add_scalar(p + i, v[i]);
+  }
+}
+
+// Read-only 16-byte load with an L2 policy (value rows in the scatter backward).
+__device__ __forceinline__ uint4 ldg16_hint(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
 }
 
 // Adds VEC values (one lane's channel chunk) into an accumulator row of type A.

@@ -2,6 +2,7 @@
 // dtype so the build compiles them in parallel).
 #include <algorithm>
 #define MSDA_LAUNCH_IMPL
+#define MSDA_LAUNCH_ZERO_IMPL
 #include "msda_launch.cuh"
 
 namespace msda {

@@ -35,6 +35,8 @@ struct OpParams {
   void* grad_value;   // scatter target of the backward (value dtype or fp32)
   void* grad_loc;
   void* grad_attn;
+  unsigned* counts;   // counted scatter: bilinear hits per (b, pixel, m) row
+  float* acc;         // counted scatter: fp32 rows of the multi-hit rows
   int64_t B, S, Q;
   int M, D, L, K;
   int kshift;  // log2(K) when K is a power of two, else -1
@@ -141,8 +143,21 @@ __global__ void __launch_bounds__(WARPS * 32) msda_fwd_kernel(const OpParams p) 
 //   grad_loc[s].y   = a * H * sum_d g_d * ((v10-v00)(1-lx) + (v11-v01) lx)
 //   grad_value[c]  += a * w_c * g          (SCATTER; A = accumulator type)
 // ---------------------------------------------------------------------------
-template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, bool SCATTER>
-__global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) {
+// grad_value handling of msda_bwd_kernel.
+enum ScatterMode : int {
+  kNoScatter = 0,  // grad_value written by another kernel
+  kScatter = 1,    // vector `red` into p.grad_value (type A), zero-filled beforehand
+  kCounted = 2,    // hit-counted: one-hit rows stored, multi-hit rows reduced in fp32
+};
+
+// Minimum resident CTAs per SM the backward is compiled for (register cap).
+#ifndef MSDA_BWD_MIN_BLOCKS
+#define MSDA_BWD_MIN_BLOCKS 4
+#endif
+
+template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE>
+__global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kernel(const OpParams p) {
+  constexpr bool SCATTER = MODE != kNoScatter;
   __shared__ LevelInfo lv[kMaxLevels];
   load_levels(p.shapes, p.starts, p.L, p.S, lv);
 
@@ -159,11 +174,19 @@ __global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) 
   const int64_t head_base = (b * p.S * p.M + m) * D;
   const T* vb = reinterpret_cast<const T*>(p.value) + head_base;
   A* gvb = reinterpret_cast<A*>(p.grad_value) + head_base;
+  float* accb = p.acc + head_base;                     // kCounted only
+  const unsigned* cnb = p.counts + (b * p.S * p.M + m);  // kCounted: row pix at cnb[pix * M]
   const int LK = p.L * p.K;
   const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
   const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
   T* glp = reinterpret_cast<T*>(p.grad_loc) + qm * (2 * LK);
   T* gap = reinterpret_cast<T*>(p.grad_attn) + qm * LK;
+  // Scatter: keep the reduction target in L2, let the gathered value rows go first.
+  uint64_t pol_keep = 0, pol_stream = 0;
+  if constexpr (SCATTER) {
+    pol_keep = policy_evict_last();
+    pol_stream = policy_evict_first();
+  }
 
   float g[CPL][VEC];
   {
@@ -201,6 +224,15 @@ __global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) 
       }
     }
     Raw raw[NB][4][CPL];
+    unsigned hits[NB][4];
+#pragma unroll
+    for (int n = 0; n < NB; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        hits[n][c] = 0u;
+        if constexpr (MODE == kCounted)
+          if ((bl[n].valid >> c) & 1u) hits[n][c] = __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
+      }
 #pragma unroll
     for (int n = 0; n < NB; ++n)
 #pragma unroll
@@ -209,7 +241,14 @@ __global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) 
         for (int j = 0; j < CPL; ++j) {
           const int ch = (j * LPR + sub) * VEC;
           Raw r{};
-          if (((bl[n].valid >> c) & 1u) && ch < D) r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
+          if (((bl[n].valid >> c) & 1u) && ch < D) {
+            if constexpr (SCATTER && VEC * sizeof(T) == 16) {
+              const uint4 u = ldg16_hint(vb + bl[n].pix[c] * rs + ch, pol_stream);
+              r = *reinterpret_cast<const Raw*>(&u);
+            } else {
+              r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
+            }
+          }
           raw[n][c][j] = r;
         }
 
@@ -260,7 +299,17 @@ __global__ void __launch_bounds__(WARPS * 32) msda_bwd_kernel(const OpParams p) 
                   float contrib[VEC];
 #pragma unroll
                   for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
-                  red_add_vec<A, VEC>(gvb + bl[n].pix[c] * rs + ch, contrib);
+                  if constexpr (MODE == kCounted) {
+                    // A row with one hit gets its only contribution stored
+                    // (rounded once, as fp32 accumulation would); rows with
+                    // more hits accumulate in fp32.
+                    if (hits[n][c] == 1u)
+                      store_vec<T, VEC>(reinterpret_cast<T*>(gvb) + bl[n].pix[c] * rs + ch, contrib);
+                    else
+                      red_add_vec_hint<float, VEC>(accb + bl[n].pix[c] * rs + ch, contrib, pol_keep);
+                  } else {
+                    red_add_vec_hint<A, VEC>(gvb + bl[n].pix[c] * rs + ch, contrib, pol_keep);
+                  }
                 }
               }
             }
@@ -730,6 +779,95 @@ __global__ void __launch_bounds__(kOwnerThreads) msda_bwd_value_owner_kernel(con
     }
   }
   OWNER_STAMP(63);
+}
+
+// ---------------------------------------------------------------------------
+// Hit-counted scatter, pass 1: count the bilinear hits of every
+// (b, pixel, m) row of grad_value, one thread per sampling point, with
+// fire-and-forget reductions.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p) {
+  __shared__ LevelInfo lv[kMaxLevels];
+  load_levels(p.shapes, p.starts, p.L, p.S, lv);
+  const int LK = p.L * p.K;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.BQM * LK) return;
+  const int64_t qm = i / LK;
+  const int s = (int)(i - qm * LK);
+  const int64_t b = qm / (p.Q * p.M);
+  const int m = (int)(qm % p.M);
+  const float2 xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);
+  const Bilinear bl = resolve(xy.x, xy.y, lv[level_of(s, p.K, p.kshift)]);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if (!((bl.valid >> c) & 1u)) continue;
+    const int64_t row = (b * p.S + bl.pix[c]) * p.M + m;
+    asm volatile("red.global.add.u32 [%0], 1;" ::"l"(p.counts + row) : "memory");
+  }
+}
+
+// Hit-counted scatter, pass 2: zero the fp32 accumulator rows of the rows hit
+// more than once (one thread per row); no other accumulator row is touched.
+__device__ __forceinline__ void zero_row(float* a, int D) {
+  if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(a + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    for (int d = 0; d < D; ++d) a[d] = 0.f;
+  }
+}
+
+template <int kUnused = 0>
+__global__ void __launch_bounds__(256) msda_zero_multi_kernel(const OpParams p) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= p.B * p.S * p.M) return;
+  if (__ldg(p.counts + row) > 1u) zero_row(p.acc + row * p.D, p.D);
+}
+
+// Hit-counted scatter, pass 4: rows nothing hit become zeros; multi-hit rows
+// are rounded from their fp32 accumulator (skipped when grad_value itself is
+// the fp32 accumulator); one-hit rows were already stored by the backward.
+// One thread per VEC elements of a row.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {
+  const int D = p.D;
+  const int per_row = D / VEC;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.B * p.S * p.M * per_row) return;
+  const int64_t row = t / per_row;
+  const int64_t e = row * D + (t - row * per_row) * VEC;
+  const unsigned cnt = __ldg(p.counts + row);
+  const bool in_place = reinterpret_cast<const void*>(p.acc) == p.grad_value;
+  if (cnt == 1u || (cnt > 1u && in_place)) return;
+  float v[VEC];
+  if (cnt == 0u) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+  } else if constexpr (VEC % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < VEC; k += 4) {
+      const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
+      v[k] = f.x;
+      v[k + 1] = f.y;
+      v[k + 2] = f.z;
+      v[k + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+  }
+  store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
+}
+
+// Zero-fill of the scatter target (grad_value or the fp32 workspace) with
+// evict_last stores, so the lines the reductions hit next are already in L2.
+template <int kUnused = 0>  // a template, so the header can define it in every unit
+__global__ void __launch_bounds__(256) msda_zero_kernel(void* __restrict__ dst, int64_t n16) {
+  const uint64_t pol = policy_evict_last();
+  char* d = reinterpret_cast<char*>(dst);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
+       i += (int64_t)gridDim.x * blockDim.x)
+    st_zero16_hint(d + i * 16, pol);
 }
 
 // fp32 accumulation buffer -> value dtype (the downcast of src/msda_triton/ops.py:91-92).

@@ -18,12 +18,19 @@ constexpr int kWarpsPerCta = 8;
 
 template <typename T>
 cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
-// Backward over sampling points: grad_loc / grad_attn, plus (scatter=true) the
-// grad_value scatter with vector `red` adds into p.grad_value (fp32 when
-// fp32_scatter, else the value dtype).
+// Backward over sampling points: grad_loc / grad_attn, plus the grad_value
+// handling `mode` (ScatterMode): kScatter adds with vector `red` into
+// p.grad_value (fp32 when fp32_scatter, else the value dtype); kCounted stores
+// one-hit rows and reduces multi-hit rows into p.acc (needs the counts).
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool fp32_scatter,
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
                             cudaStream_t st);
+// Hit-counted scatter passes 1 (count hits, zero multi-hit accumulators) and
+// 3 (zeros / downcast). p.counts must be zeroed before launch_count.
+template <typename T>
+cudaError_t launch_count(const OpParams& p, cudaStream_t st);
+template <typename T>
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st);
 
 // grad_value by pixel-chunk ownership (see msda_bwd_value_owner_kernel).
 struct OwnerPlan {
@@ -40,6 +47,8 @@ template <typename T>
 cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st);
 template <typename T>
 cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st);
+// Zero `bytes` (a multiple of 16, 16-byte aligned) with L2 evict_last stores.
+cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Template dispatch (included by the per-dtype translation units only).
@@ -70,13 +79,15 @@ static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st
   return cudaErrorInvalidConfiguration;
 }
 
-template <typename T, typename A, int VEC, bool SCATTER>
+template <typename T, typename A, int VEC, int MODE>
 static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
+// The backward keeps one point per group in flight (NB = 1): its per-point
+// state (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
 #define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                            \
   if (c.lpr == LPR_ && c.cpl == CPL_) {                                                           \
-    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, NB_, SCATTER><<<grid, block, 0, st>>>(p); \
+    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE><<<grid, block, 0, st>>>(p);      \
     return cudaGetLastError();                                                                    \
   }
   MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
@@ -93,20 +104,54 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, bool scatter, bool fp32_scatter,
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
                             cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
-  if (!scatter) {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, false>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, false>(p, c, st);
+  if (mode == kNoScatter) {
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kNoScatter>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kNoScatter>(p, c, st);
+  } else if (mode == kCounted) {
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kCounted>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kCounted>(p, c, st);
   } else if (fp32_scatter || sizeof(T) == 4) {
-    if (c.vec == V16) return bwd_by_shape<T, float, V16, true>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, float, 1, true>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, float, V16, kScatter>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, float, 1, kScatter>(p, c, st);
   } else {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, true>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, true>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kScatter>(p, c, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kScatter>(p, c, st);
   }
   return cudaErrorInvalidConfiguration;
+}
+
+template <typename T>
+cudaError_t launch_count(const OpParams& p, cudaStream_t st) {
+  const int64_t n = p.BQM * p.L * p.K;
+  const int64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  msda_count_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // Zero the fp32 accumulator rows of the multi-hit rows (the workspace rows
+  // for fp16/bf16, grad_value's own rows for fp32).
+  const int64_t rows = p.B * p.S * p.M;
+  msda_zero_multi_kernel<0><<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st) {
+  (void)num_sms;
+  constexpr int V16 = 16 / (int)sizeof(T);
+  const int64_t rows = p.B * p.S * p.M;
+  const int vec = (vec_ok && p.D % V16 == 0 && p.D % 4 == 0) ? V16 : 1;
+  const int64_t n = rows * (p.D / vec);
+  const int64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (vec == V16)
+    msda_finalize_kernel<T, V16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
+  else
+    msda_finalize_kernel<T, 1><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
+  return cudaGetLastError();
 }
 
 template <typename T, int OVEC, int DT>
@@ -147,9 +192,24 @@ cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int nu
   return cudaGetLastError();
 }
 
+#endif  // MSDA_LAUNCH_IMPL
+
+#ifdef MSDA_LAUNCH_ZERO_IMPL
+cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
+  const int64_t n16 = (int64_t)(bytes / 16);
+  if (n16 == 0) return cudaSuccess;
+  const int64_t blocks = std::min<int64_t>((int64_t)num_sms * 8, (n16 + 255) / 256);
+  msda_zero_kernel<0><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(dst, n16);
+  return cudaGetLastError();
+}
+#endif  // MSDA_LAUNCH_ZERO_IMPL
+
+#ifdef MSDA_LAUNCH_IMPL
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
-  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, bool, bool, cudaStream_t); \
+  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, bool, cudaStream_t);  \
+  template cudaError_t launch_count<T>(const OpParams&, cudaStream_t);                            \
+  template cudaError_t launch_finalize<T>(const OpParams&, bool, int, cudaStream_t);              \
   template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);
 

@@ -25,6 +25,7 @@ MSDA_DTYPE_BF16 = 2
 MSDA_BWD_FP32_ACCUM = 1
 MSDA_BWD_FORCE_SCATTER = 2
 MSDA_BWD_FORCE_OWNER = 4
+MSDA_BWD_FORCE_COUNTED = 8
 
 # Every symbol include/msda_b200.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p

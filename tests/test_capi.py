@@ -83,9 +83,13 @@ def test_abi_workspace_size():
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F16, f) == full
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_F32, f) == 0
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, 0) == 0
-    # The automatic choice is the scatter path; forcing the scatter path keeps
-    # the workspace, forcing the owner path (no workspace) drops it.
-    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == full
+    # Sparse sampling takes the hit-counted scatter: per-row counts (padded to
+    # 256 bytes) plus fp32 rows for fp16/bf16, counts only for fp32.
+    counted = 256 + 2 * 10 * 3 * 8 * 4
+    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == counted
+    assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_F32, 0) == 256
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_COUNTED) == counted
+    # Forcing the plain scatter keeps the full fp32 workspace; the owner path has none.
     assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_SCATTER) == full
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 0
     # More than 65535 sampling points per head slice (L*Q*K) exceed the owner

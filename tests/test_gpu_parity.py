@@ -416,6 +416,7 @@ ALGOS = {
     "owner": (_clib.MSDA_BWD_FORCE_OWNER, True),
     "scatter_fp32": (_clib.MSDA_BWD_FORCE_SCATTER, True),
     "scatter_native": (_clib.MSDA_BWD_FORCE_SCATTER, False),
+    "counted": (_clib.MSDA_BWD_FORCE_COUNTED, True),
 }
 ALGO_CASES = [
     ("decoder_case", dict(B=2, Q=100, M=4, D=32, K=4, shapes=[(24, 32), (12, 16), (6, 8)]), 0.0, 1.0),
@@ -442,7 +443,7 @@ def test_backward_algorithms(name, kw, lo, hi, dtype, algo):
     cases.assert_grads_close(got, ref, loc, shapes, STRICT_TOL[dtype], gv_tol=gv_tol, what=algo)
 
 
-@pytest.mark.parametrize("algo", ["owner", "scatter_fp32"])
+@pytest.mark.parametrize("algo", ["owner", "scatter_fp32", "counted"])
 @pytest.mark.parametrize("name", ["decoder", "small"])
 def test_backward_algorithms_at_baseline_points(name, algo):
     flags, fp32 = ALGOS[algo]
@@ -472,3 +473,24 @@ def test_owner_writes_every_grad_value_element():
     assert (gv[:, 119:] == 0).all()
     _, ref = oracle64(value, shapes, starts, loc, attn, g)
     close(gv, ref[0], STRICT_TOL[torch.bfloat16], "grad_value")
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_counted_scatter_matches_fp32_accumulation(dtype):
+    """The hit-counted scatter stores one-hit rows and reduces multi-hit rows in
+    fp32: its grad_value must equal the fp32-workspace scatter's up to fp32
+    summation order, and untouched rows (here: a padding tail) must be zeros
+    even when grad_value starts as garbage."""
+    value, shapes, starts, loc, attn = cases.make_inputs(
+        B=2, Q=40, M=4, D=32, K=4, shapes=[(20, 30), (10, 15), (5, 8)], dtype=dtype, device=DEV,
+        loc_lo=-0.1, loc_hi=1.1, seed=4)
+    value = torch.cat([value, torch.randn(2, 9, 4, 32, device=DEV).to(dtype)], 1)  # 9 unused rows
+    g = cases.grad_output_like(torch.empty(2, 40, 4, 32, device=DEV, dtype=dtype))
+    ref = _ops._backward(value, shapes, starts, loc, attn, g, True, _clib.MSDA_BWD_FORCE_SCATTER)
+    torch.empty(value.numel() * 8, device=DEV).fill_(float("nan"))  # dirty the allocator
+    got = _ops._backward(value, shapes, starts, loc, attn, g, True, _clib.MSDA_BWD_FORCE_COUNTED)
+    assert (got[0][:, -9:] == 0).all()
+    tol = dict(rtol=1e-6, atol=1e-6) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-5)
+    torch.testing.assert_close(got[0].float(), ref[0].float(), **tol)
+    torch.testing.assert_close(got[1], ref[1])
+    torch.testing.assert_close(got[2], ref[2])
