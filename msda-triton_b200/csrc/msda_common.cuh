@@ -89,6 +89,51 @@ __device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
   *reinterpret_cast<typename Pack<T, VEC>::Raw*>(p) = pk.raw;
 }
 
+// ---------------------------------------------------------------------------
+// Packed fp32 pairs for sm_100's f32x2 FMA (two fp32 lanes per 64-bit register).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// A 32-bit word holding two 16-bit values -> packed fp32 pair.
+__device__ __forceinline__ uint64_t word_to_f2(unsigned w, const __nv_bfloat16*) {
+  uint64_t r;  // bf16 is the upper half of fp32: shift / mask, no conversion
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(w << 16), "r"(w & 0xffff0000u));
+  return r;
+}
+__device__ __forceinline__ uint64_t word_to_f2(unsigned w, const __half*) {
+  __half2 h;
+  *reinterpret_cast<unsigned*>(&h) = w;
+  const float2 f = __half22float2(h);
+  return f2_pack(f.x, f.y);
+}
+// VEC elements of a Raw vector -> VEC/2 packed pairs (VEC even).
+template <typename T, int VEC>
+__device__ __forceinline__ void raw_to_f2(typename Pack<T, VEC>::Raw r, uint64_t (&out)[VEC / 2]) {
+  const unsigned* w = reinterpret_cast<const unsigned*>(&r);
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < VEC / 2; ++i) {
+      uint64_t x;
+      asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(w[2 * i]), "r"(w[2 * i + 1]));
+      out[i] = x;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC / 2; ++i) out[i] = word_to_f2(w[i], (const T*)nullptr);
+  }
+}
+
 // Two consecutive elements (a sampling location's (x, y) pair).
 __device__ __forceinline__ float2 load_pair(const float* p) {
   return __ldg(reinterpret_cast<const float2*>(p));

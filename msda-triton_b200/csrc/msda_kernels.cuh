@@ -1,8 +1,9 @@
 // MSDA forward / backward kernels for sm_100a.
 //
 // Work decomposition (one warp per (b, q, m), lanes over D):
-//   * A warp owns one (batch, query, head) triple -- the unit the reference's
-//     Triton programs tile over (src/msda_triton/kernels.py:83-96).
+//   * A CTA owns a block of consecutive queries of one (batch, head) slice --
+//     the reference's query-block tiling (src/msda_triton/kernels.py:83-96) --
+//     and each of its warps one (batch, query, head) triple.
 //   * Its 32 lanes split into G = 32 / LPR groups of LPR lanes. A group owns
 //     one sampling point (l, k) at a time; its LPR lanes cover the D channels
 //     of each bilinear corner row with VEC-element (16-byte) vector loads, so
@@ -47,6 +48,18 @@ __device__ __forceinline__ int level_of(int s, int K, int kshift) {
   return kshift >= 0 ? (s >> kshift) : (s / K);
 }
 
+// Query-block tiling (src/msda_triton/kernels.py:83-96): a CTA owns WARPS
+// consecutive queries of one (batch, head) slice, one warp per query, so the
+// overlapping corner rows of neighbouring queries are re-read from L1. Grid:
+// x = query block, y = head, z = batch (no integer division in the mapping).
+__device__ __forceinline__ bool query_block_of(const OpParams& p, int warps, int64_t& b, int& m,
+                                               int64_t& q) {
+  q = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
+  m = (int)blockIdx.y;
+  b = (int64_t)blockIdx.z;
+  return q < p.Q;
+}
+
 // ---------------------------------------------------------------------------
 // Forward: out[b,q,m,:] = sum_{l,k} a * sum_c w_c * value[b, pix_c, m, :]
 // (src/msda_triton/kernels.py:100-163)
@@ -59,11 +72,11 @@ __global__ void __launch_bounds__(WARPS * 32) msda_fwd_kernel(const OpParams p) 
   constexpr int G = 32 / LPR;
   using Raw = typename Pack<T, VEC>::Raw;
   const int lane = threadIdx.x & 31;
-  const int64_t qm = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
-  if (qm >= p.BQM) return;
+  int64_t b, q;
+  int m;
+  if (!query_block_of(p, WARPS, b, m, q)) return;
+  const int64_t qm = (b * p.Q + q) * p.M + m;
   const int grp = lane / LPR, sub = lane % LPR;
-  const int64_t b = qm / (p.Q * p.M);
-  const int m = (int)(qm % p.M);
   const int D = p.D;
   const int64_t rs = (int64_t)p.M * D;
   const T* vb = reinterpret_cast<const T*>(p.value) + (b * p.S * p.M + m) * D;
@@ -71,11 +84,18 @@ __global__ void __launch_bounds__(WARPS * 32) msda_fwd_kernel(const OpParams p) 
   const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
   const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
 
+  // Packed-pair accumulators (f32x2 FMA) on the vector path, scalars otherwise.
+  constexpr bool kPairs = VEC >= 2 && VEC % 2 == 0;
+  constexpr int NP = kPairs ? VEC / 2 : 1;
+  uint64_t acc2[CPL][NP];
   float acc[CPL][VEC];
 #pragma unroll
-  for (int j = 0; j < CPL; ++j)
+  for (int j = 0; j < CPL; ++j) {
+#pragma unroll
+    for (int v = 0; v < NP; ++v) acc2[j][v] = 0ull;
 #pragma unroll
     for (int v = 0; v < VEC; ++v) acc[j][v] = 0.f;
+  }
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -109,29 +129,83 @@ __global__ void __launch_bounds__(WARPS * 32) msda_fwd_kernel(const OpParams p) 
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const float wc = at[n] * bl[n].w[c];
+        if constexpr (kPairs) {
+          const uint64_t w2 = f2_pack(wc, wc);
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-          float v[VEC];
-          unpack_raw<T, VEC>(raw[n][c][j], v);
+          for (int j = 0; j < CPL; ++j) {
+            uint64_t v2[NP];
+            raw_to_f2<T, VEC>(raw[n][c][j], v2);
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[j][e] = fmaf(wc, v[e], acc[j][e]);
+            for (int e = 0; e < NP; ++e) acc2[j][e] = f2_fma(w2, v2[e], acc2[j][e]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) {
+            float v[VEC];
+            unpack_raw<T, VEC>(raw[n][c][j], v);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[j][e] = fmaf(wc, v[e], acc[j][e]);
+          }
         }
       }
   }
-
-#pragma unroll
-  for (int off = LPR; off < 32; off <<= 1)
+  if constexpr (kPairs) {
 #pragma unroll
     for (int j = 0; j < CPL; ++j)
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], off);
+      for (int e = 0; e < NP; ++e) f2_unpack(acc2[j][e], acc[j][2 * e], acc[j][2 * e + 1]);
+  }
 
-  if (grp == 0) {
-    T* op = reinterpret_cast<T*>(p.out) + qm * D;
+  T* op = reinterpret_cast<T*>(p.out) + qm * D;
+  if constexpr (CPL == 1 && G > 1 && VEC >= 2) {
+    // Reduce-scatter across the G groups: each xor stage halves the values a
+    // lane keeps (it keeps the half its partner sends it the other of), so
+    // log2(VEC) stages cost VEC-1 shuffles instead of VEC*log2(G); once a lane
+    // holds one value the remaining stages are plain xor-sums.
+    constexpr int STAGES = __builtin_ctz(G);
+    int base = 0;
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const int ch = (j * LPR + sub) * VEC;
-      if (ch < D) store_vec<T, VEC>(op + ch, acc[j]);
+    for (int st = 0; st < STAGES; ++st) {
+      const int off = LPR << st;
+      const int n = VEC >> st;  // live values before this stage (compile time after unrolling)
+      if (n > 1) {
+        const bool upper = (lane & off) != 0;
+        const int half = n / 2;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = upper ? acc[0][i] : acc[0][half + i];
+          const float keep = upper ? acc[0][half + i] : acc[0][i];
+          acc[0][i] = keep + __shfl_xor_sync(kFullMask, send, off);
+        }
+        if (upper) base += half;
+      } else {
+        acc[0][0] += __shfl_xor_sync(kFullMask, acc[0][0], off);
+      }
+    }
+    constexpr int NF = (VEC >> STAGES) > 0 ? (VEC >> STAGES) : 1;  // values left per lane
+    constexpr int HALVINGS = __builtin_ctz(VEC) < STAGES ? __builtin_ctz(VEC) : STAGES;
+    // Lanes that only replicated a value in the plain xor stages skip the store.
+    const int rep_mask = ((G - 1) << __builtin_ctz(LPR)) & ~(((1 << HALVINGS) - 1) << __builtin_ctz(LPR));
+    const int ch = sub * VEC + base;
+    if ((lane & rep_mask) == 0 && sub * VEC < D) {
+      float outv[NF];
+#pragma unroll
+      for (int i = 0; i < NF; ++i) outv[i] = acc[0][i];
+      store_vec<T, NF>(op + ch, outv);
+    }
+  } else {
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+      for (int j = 0; j < CPL; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], off);
+    if (grp == 0) {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int ch = (j * LPR + sub) * VEC;
+        if (ch < D) store_vec<T, VEC>(op + ch, acc[j]);
+      }
     }
   }
 }
@@ -164,11 +238,11 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
   constexpr int G = 32 / LPR;
   using Raw = typename Pack<T, VEC>::Raw;
   const int lane = threadIdx.x & 31;
-  const int64_t qm = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
-  if (qm >= p.BQM) return;
+  int64_t b, q;
+  int m;
+  if (!query_block_of(p, WARPS, b, m, q)) return;
+  const int64_t qm = (b * p.Q + q) * p.M + m;
   const int grp = lane / LPR, sub = lane % LPR;
-  const int64_t b = qm / (p.Q * p.M);
-  const int m = (int)(qm % p.M);
   const int D = p.D;
   const int64_t rs = (int64_t)p.M * D;
   const int64_t head_base = (b * p.S * p.M + m) * D;

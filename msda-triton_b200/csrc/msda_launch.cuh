@@ -65,10 +65,15 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st);
   X(32, 2, 1)                  \
   X(32, 4, 1)
 
+// Grid of the query-block kernels: (ceil(Q / kWarpsPerCta), M, B).
+inline dim3 query_block_grid(const OpParams& p) {
+  return dim3((unsigned)((p.Q + kWarpsPerCta - 1) / kWarpsPerCta), (unsigned)p.M, (unsigned)p.B);
+}
+
 template <typename T, int VEC>
 static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
-  const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
+  const dim3 grid = query_block_grid(p);
 #define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                             \
   if (c.lpr == LPR_ && c.cpl == CPL_) {                                            \
     msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_><<<grid, block, 0, st>>>(p); \
@@ -82,7 +87,7 @@ static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st
 template <typename T, typename A, int VEC, int MODE>
 static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
-  const dim3 grid((unsigned)((p.BQM + kWarpsPerCta - 1) / kWarpsPerCta));
+  const dim3 grid = query_block_grid(p);
 // The backward keeps one point per group in flight (NB = 1): its per-point
 // state (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
 #define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                            \
