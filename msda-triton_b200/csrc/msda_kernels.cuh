@@ -857,9 +857,19 @@ __global__ void __launch_bounds__(kOwnerThreads) msda_bwd_value_owner_kernel(con
 
 // ---------------------------------------------------------------------------
 // Hit-counted scatter, pass 1: count the bilinear hits of every
-// (b, pixel, m) row of grad_value, one thread per sampling point, with
-// fire-and-forget reductions.
+// (b, pixel, m) row of grad_value, one thread per sampling point. The hit
+// that raises a row's count from 1 to 2 zero-fills that row's fp32
+// accumulator, so exactly the multi-hit rows are zeroed, once. The four
+// corner atomics are issued before any zeroing waits on their results.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void zero_row(float* a, int D) {
+  if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(a + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    for (int d = 0; d < D; ++d) a[d] = 0.f;
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p) {
   __shared__ LevelInfo lv[kMaxLevels];
@@ -873,64 +883,64 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p) {
   const int m = (int)(qm % p.M);
   const float2 xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);
   const Bilinear bl = resolve(xy.x, xy.y, lv[level_of(s, p.K, p.kshift)]);
+  unsigned old[4];
+  int64_t row[4];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    if (!((bl.valid >> c) & 1u)) continue;
-    const int64_t row = (b * p.S + bl.pix[c]) * p.M + m;
-    asm volatile("red.global.add.u32 [%0], 1;" ::"l"(p.counts + row) : "memory");
+    old[c] = 0u;
+    row[c] = (b * p.S + bl.pix[c]) * p.M + m;
+    if ((bl.valid >> c) & 1u) old[c] = atomicAdd(p.counts + row[c], 1u);
   }
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    if (((bl.valid >> c) & 1u) && old[c] == 1u) zero_row(p.acc + row[c] * p.D, p.D);
 }
 
-// Hit-counted scatter, pass 2: zero the fp32 accumulator rows of the rows hit
-// more than once (one thread per row); no other accumulator row is touched.
-__device__ __forceinline__ void zero_row(float* a, int D) {
-  if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
-    for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(a + d) = make_float4(0.f, 0.f, 0.f, 0.f);
-  } else {
-    for (int d = 0; d < D; ++d) a[d] = 0.f;
-  }
-}
-
-template <int kUnused = 0>
-__global__ void __launch_bounds__(256) msda_zero_multi_kernel(const OpParams p) {
-  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= p.B * p.S * p.M) return;
-  if (__ldg(p.counts + row) > 1u) zero_row(p.acc + row * p.D, p.D);
-}
-
-// Hit-counted scatter, pass 4: rows nothing hit become zeros; multi-hit rows
+// Hit-counted scatter, pass 3: rows nothing hit become zeros; multi-hit rows
 // are rounded from their fp32 accumulator (skipped when grad_value itself is
 // the fp32 accumulator); one-hit rows were already stored by the backward.
-// One thread per VEC elements of a row.
+// One thread per 4 consecutive rows x VEC elements (one 16-byte count load).
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {
   const int D = p.D;
   const int per_row = D / VEC;
+  const int64_t rows = p.B * p.S * p.M;
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= p.B * p.S * p.M * per_row) return;
-  const int64_t row = t / per_row;
-  const int64_t e = row * D + (t - row * per_row) * VEC;
-  const unsigned cnt = __ldg(p.counts + row);
-  const bool in_place = reinterpret_cast<const void*>(p.acc) == p.grad_value;
-  if (cnt == 1u || (cnt > 1u && in_place)) return;
-  float v[VEC];
-  if (cnt == 0u) {
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) v[k] = 0.f;
-  } else if constexpr (VEC % 4 == 0) {
-#pragma unroll
-    for (int k = 0; k < VEC; k += 4) {
-      const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
-      v[k] = f.x;
-      v[k + 1] = f.y;
-      v[k + 2] = f.z;
-      v[k + 3] = f.w;
-    }
+  const int64_t quad = t / per_row;  // rows 4*quad .. 4*quad+3
+  if (quad * 4 >= rows) return;
+  const int chunk = (int)(t - quad * per_row);
+  unsigned cnt[4];
+  if (quad * 4 + 3 < rows && (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0) {
+    const uint4 c4 = __ldg(reinterpret_cast<const uint4*>(p.counts) + quad);
+    cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
   } else {
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+    for (int r = 0; r < 4; ++r) cnt[r] = quad * 4 + r < rows ? __ldg(p.counts + quad * 4 + r) : 1u;
   }
-  store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
+  const bool in_place = reinterpret_cast<const void*>(p.acc) == p.grad_value;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    if (cnt[r] == 1u || (cnt[r] > 1u && in_place)) continue;
+    const int64_t e = (quad * 4 + r) * D + chunk * VEC;
+    float v[VEC];
+    if (cnt[r] == 0u) {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+    } else if constexpr (VEC % 4 == 0) {
+#pragma unroll
+      for (int k = 0; k < VEC; k += 4) {
+        const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
+        v[k] = f.x;
+        v[k + 1] = f.y;
+        v[k + 2] = f.z;
+        v[k + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+    }
+    store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
+  }
 }
 
 // Zero-fill of the scatter target (grad_value or the fp32 workspace) with

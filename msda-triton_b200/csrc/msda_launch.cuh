@@ -134,12 +134,6 @@ cudaError_t launch_count(const OpParams& p, cudaStream_t st) {
   const int64_t blocks = (n + 255) / 256;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   msda_count_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  // Zero the fp32 accumulator rows of the multi-hit rows (the workspace rows
-  // for fp16/bf16, grad_value's own rows for fp32).
-  const int64_t rows = p.B * p.S * p.M;
-  msda_zero_multi_kernel<0><<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -149,7 +143,7 @@ cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStr
   constexpr int V16 = 16 / (int)sizeof(T);
   const int64_t rows = p.B * p.S * p.M;
   const int vec = (vec_ok && p.D % V16 == 0 && p.D % 4 == 0) ? V16 : 1;
-  const int64_t n = rows * (p.D / vec);
+  const int64_t n = (rows + 3) / 4 * (p.D / vec);
   const int64_t blocks = (n + 255) / 256;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if (vec == V16)
