@@ -276,6 +276,12 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
       }
     }
   }
+  // grad_out as packed fp32 pairs (VEC even).
+  uint64_t g2[CPL][VEC / 2 > 0 ? VEC / 2 : 1];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j)
+#pragma unroll
+    for (int e = 0; e < VEC / 2; ++e) g2[j][e] = f2_pack(g[j][2 * e], g[j][2 * e + 1]);
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -328,27 +334,53 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
 
 #pragma unroll
     for (int n = 0; n < NB; ++n) {
-      const float lx = bl[n].lx, ly = bl[n].ly;
-      float ga = 0.f, gx = 0.f, gy = 0.f;
+      // Per-corner dot products over this lane's channels,
+      // P_c = sum_d g_d * v_c,d; the three gradients are linear in them:
+      //   ga = sum_c w_c P_c
+      //   gx = (1 - ly)(P01 - P00) + ly (P11 - P10)
+      //   gy = (1 - lx)(P10 - P00) + lx (P11 - P01)
+      float P[4];
+      if constexpr (VEC % 2 == 0) {
+        uint64_t acc2[4];
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        float v00[VEC], v01[VEC], v10[VEC], v11[VEC];
-        unpack_raw<T, VEC>(raw[n][0][j], v00);
-        unpack_raw<T, VEC>(raw[n][1][j], v01);
-        unpack_raw<T, VEC>(raw[n][2][j], v10);
-        unpack_raw<T, VEC>(raw[n][3][j], v11);
+        for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float gd = g[j][e];
-          const float smp = bl[n].w[0] * v00[e] + bl[n].w[1] * v01[e] + bl[n].w[2] * v10[e] +
-                            bl[n].w[3] * v11[e];
-          const float dx = (v01[e] - v00[e]) * (1.f - ly) + (v11[e] - v10[e]) * ly;
-          const float dy = (v10[e] - v00[e]) * (1.f - lx) + (v11[e] - v01[e]) * lx;
-          ga = fmaf(gd, smp, ga);
-          gx = fmaf(gd, dx, gx);
-          gy = fmaf(gd, dy, gy);
+        for (int j = 0; j < CPL; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint64_t v2[VEC / 2];
+            raw_to_f2<T, VEC>(raw[n][c][j], v2);
+#pragma unroll
+            for (int e = 0; e < VEC / 2; ++e) acc2[c] = f2_fma(g2[j][e], v2[e], acc2[c]);
+          }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float lo, hi;
+          f2_unpack(acc2[c], lo, hi);
+          P[c] = lo + hi;
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) P[c] = 0.f;
+#pragma unroll
+        for (int j = 0; j < CPL; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float v[VEC];
+            unpack_raw<T, VEC>(raw[n][c][j], v);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) P[c] = fmaf(g[j][e], v[e], P[c]);
+          }
       }
+      const float lx = bl[n].lx, ly = bl[n].ly;
+      float ga = bl[n].w[0] * P[0];
+      ga = fmaf(bl[n].w[1], P[1], ga);
+      ga = fmaf(bl[n].w[2], P[2], ga);
+      ga = fmaf(bl[n].w[3], P[3], ga);
+      float gx = (1.f - ly) * (P[1] - P[0]);
+      gx = fmaf(ly, P[3] - P[2], gx);
+      float gy = (1.f - lx) * (P[2] - P[0]);
+      gy = fmaf(lx, P[3] - P[1], gy);
 #pragma unroll
       for (int off = 1; off < LPR; off <<= 1) {
         ga += __shfl_xor_sync(kFullMask, ga, off);
@@ -371,8 +403,15 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
                 const int ch = (j * LPR + sub) * VEC;
                 if (ch < D) {
                   float contrib[VEC];
+                  if constexpr (VEC % 2 == 0) {
+                    const uint64_t wc2 = f2_pack(wc, wc);
 #pragma unroll
-                  for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
+                    for (int e = 0; e < VEC / 2; ++e)
+                      f2_unpack(f2_mul(wc2, g2[j][e]), contrib[2 * e], contrib[2 * e + 1]);
+                  } else {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
+                  }
                   if constexpr (MODE == kCounted) {
                     // A row with one hit gets its only contribution stored
                     // (rounded once, as fp32 accumulation would); rows with
