@@ -12,14 +12,17 @@ path has no collective) and NCCL only carries the timing reduction.
 
 Reported (one JSON line on rank 0):
   value      queries/s over all ranks (B*Q*N / device time), inputs resident
-             in HBM; device time = CUDA-event time of CUDA-graph replays of
-             the forward and backward launches, L2 flushed before every step,
-             max over ranks.
+             in HBM; device time = CUDA-event time of one CUDA-graph replay
+             per step (forward then backward launches), L2 flushed before
+             every step, max over ranks.
   e2e        the same metric through the public op with pinned HOST buffers:
              host->device copies of the inputs and device->host copies of the
              output and the three gradients inside the timed region.
-  roofline   the backward (dominant) launch: algorithmic bytes / event time
-             against the measured HBM copy bandwidth.
+  roofline   the backward call (the dominant launch sequence): algorithmic
+             bytes / its CUDA-event time against the measured HBM copy
+             bandwidth; `step` gives the same for forward + backward.
+  kernels_us per-kernel device times (CUPTI) of a few extra steps after the
+             timed region; `gpu_launches` counts the msda kernels found there.
   cpu_baseline  the reference's CPU implementation (grid_sample forward +
              autograd backward, restated in oracle/msda_oracle.py) on the
              host cores, rank 0 at N=1.
@@ -53,15 +56,16 @@ NOMINAL_HBM_GBS = 8000.0
 
 # ---------------------------------------------------------------------------
 # Algorithmic byte model (labs/solutions/lab06.py:121-129 for the forward,
-# extended to the backward): every gathered corner row counts.
+# extended to the backward): every gathered corner row counts, every
+# grad_value contribution counts once at the op's element size, grad_value is
+# written once. The same numerator serves every accumulator algorithm, so a
+# slower algorithm shows up as a lower fraction, never as more "work".
 # ---------------------------------------------------------------------------
-def algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass):
+def algorithmic_bytes(B, S, Q, M, D, L, K, e):
     ns = B * Q * M * L * K
     fwd = ns * 4 * D * e + ns * 3 * e + B * Q * M * D * e
-    bwd = (ns * 4 * D * e + ns * 4 * D * e_acc + ns * 6 * e + B * Q * M * D * e
-           + B * S * M * D * e_acc)
-    if cast_pass:
-        bwd += B * S * M * D * (e_acc + e)
+    bwd = (ns * 4 * D * e + ns * 4 * D * e + ns * 6 * e + B * Q * M * D * e
+           + B * S * M * D * e)
     return fwd, bwd
 
 
@@ -182,9 +186,10 @@ def barrier(world: int):
 # Legs
 # ---------------------------------------------------------------------------
 def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
-    """Forward and backward launches (CUDA-graph replays, or direct launches
-    with use_graph=False), L2 flushed before every step, each step bracketed
-    by CUDA events. Returns (graphs, step function, per-step events)."""
+    """Forward and backward launches (one CUDA-graph replay per step, or
+    direct launches with use_graph=False), L2 flushed before every step, each
+    step bracketed by CUDA events. Returns (graph, step function, per-step
+    events)."""
     args = (x["value"], x["spatial_shapes"], x["level_start_index"], x["sampling_locations"],
             x["attention_weights"])
     g = x["grad_output"].reshape(x["value"].shape[0], -1, x["value"].shape[2], x["value"].shape[3])
@@ -200,35 +205,81 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
     torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     if use_graph:
-        gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gf):
+        # One graph per step (forward then backward), as a training step
+        # captured whole would run; an event recorded inside the graph
+        # (external: a real event-record node) splits forward from backward.
+        mid = torch.cuda.Event(enable_timing=True, external=True)
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gs):
             msda_ops._forward(*args)
-        with torch.cuda.graph(gb):
+            mid.record()
             msda_ops._backward(*args, g, fp32_acc, algo_flags)
-        run_f, run_b = gf.replay, gb.replay
-    else:
-        gf = gb = None
-        # Outputs are allocated outside the timed events by the caching
-        # allocator (no device work); the flush keeps the GPU ahead of the host.
-        run_f = lambda: msda_ops._forward(*args)  # noqa: E731
-        run_b = lambda: msda_ops._backward(*args, g, fp32_acc, algo_flags)  # noqa: E731
 
-    def one(e):
-        # Flush: write 512 MiB (evicts everything of ours from L2), then read
-        # 256 MiB so the flush's own dirty lines are written back before the
-        # timed region instead of inside it.
-        flush.fill_(1)
-        drain.sum()
-        e[0].record()
-        run_f()
-        e[1].record()
-        run_b()
-        e[2].record()
+        def one(e):
+            # Flush: write 512 MiB (evicts everything of ours from L2), then
+            # read 256 MiB so the flush's own dirty lines are written back
+            # before the timed region instead of inside it.
+            flush.fill_(1)
+            drain.sum()
+            e[0].record()
+            gs.replay()
+            e[2].record()
+            # The in-graph event is overwritten by the next replay: read the
+            # split now (outside the timed region of the next step).
+            e[2].synchronize()
+            e[1] = (e[0].elapsed_time(mid), mid.elapsed_time(e[2]))
+    else:
+        gs = None
+
+        def one(e):
+            flush.fill_(1)
+            drain.sum()
+            e[0].record()
+            msda_ops._forward(*args)
+            e[1].record()
+            msda_ops._backward(*args, g, fp32_acc, algo_flags)
+            e[2].record()
 
     tmp = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for _ in range(warmup):
         one(tmp)
-    return gf, gb, one, evs
+    return gs, one, evs
+
+
+def split_ms(e):
+    """(forward ms, backward ms) of one timed step."""
+    if isinstance(e[1], tuple):
+        return e[1]
+    return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+
+
+def kernel_breakdown(one, steps=5):
+    """Per-kernel device times (CUPTI, through torch.profiler) of a few extra
+    steps after the timed region: {kernel: (mean us, launches per step)}."""
+    from torch.profiler import ProfilerActivity, profile
+
+    tmp = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            one(tmp)
+        torch.cuda.synchronize()
+    agg = {}
+    for ev in prof.events():
+        if ev.device_type != torch.autograd.DeviceType.CUDA or not ev.name.startswith("void msda::"):
+            continue
+        name = ev.name[len("void msda::"):].split("<")[0]
+        agg.setdefault(name, []).append(ev.device_time)
+    return {k: (statistics.fmean(v), len(v) / steps) for k, v in agg.items()}
+
+
+def backward_algorithm(kernels):
+    if "msda_count_kernel" in kernels:
+        return "counted (fp32 rows for multi-hit pixels)"
+    if "msda_bwd_value_owner_kernel" in kernels:
+        return "owner"
+    if "msda_cast_kernel" in kernels:
+        return "scatter into fp32 workspace + cast"
+    return "scatter (native packed reductions)"
 
 
 def e2e_leg(x, steps, warmup, fp32_acc):
@@ -264,9 +315,11 @@ def e2e_leg(x, steps, warmup, fp32_acc):
     return step, h2d, d2h
 
 
-def cpu_reference_time(preset, dtype, steps, seed=0):
+def cpu_reference_time(preset, dtype, steps, seed=0, min_seconds=0.0):
     """The reference's CPU implementation (grid_sample forward + autograd
-    backward, oracle/msda_oracle.py) on all host cores; seconds per step."""
+    backward, oracle/msda_oracle.py) on all host cores: (seconds per step,
+    threads, steps run). Runs at least `steps` steps and at least
+    `min_seconds`."""
     sys.path.insert(0, str(REPO))
     from oracle import msda_oracle as orc
 
@@ -283,9 +336,11 @@ def cpu_reference_time(preset, dtype, steps, seed=0):
 
     step()  # warm-up
     t0 = time.perf_counter()
-    for _ in range(steps):
+    n = 0
+    while n < steps or (min_seconds and time.perf_counter() - t0 < min_seconds):
         step()
-    return (time.perf_counter() - t0) / steps, threads
+        n += 1
+    return (time.perf_counter() - t0) / n, threads, n
 
 
 def load_peaks():
@@ -310,11 +365,11 @@ def run_reference_arm(args, preset, dtype):
         return 0
     steps = max(1, args.steps)
     # Bound the CPU run to a few minutes whatever --steps asks for.
-    per_step, threads = cpu_reference_time(preset, dtype, 1)
+    per_step, threads, _ = cpu_reference_time(preset, dtype, 1)
     steps = max(1, min(steps, int(120.0 / max(per_step, 1e-3))))
     for _ in range(min(args.warmup, 2)):
         cpu_reference_time(preset, dtype, 1)
-    sec, threads = cpu_reference_time(preset, dtype, steps)
+    sec, threads, steps = cpu_reference_time(preset, dtype, steps)
     qps = preset.B * preset.num_queries / sec
     sample = f"{steps} full fwd+bwd steps of the {preset.name} workload ({dtype}) on {threads} threads"
     line = {
@@ -355,6 +410,8 @@ def main(argv=None) -> int:
                     help="time direct launches instead of CUDA-graph replays")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-breakdown", action="store_true",
+                    help="skip the CUPTI per-kernel pass (use under ncu)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -377,19 +434,18 @@ def main(argv=None) -> int:
                   "counted": lib.MSDA_BWD_FORCE_COUNTED}[args.bwd_algo]
 
     # ---- device leg -------------------------------------------------------
-    gf, gb, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
-                                  use_graph=not args.no_graph)
+    gs, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
+                              use_graph=not args.no_graph)
     barrier(world)
     with ClockSampler(torch.cuda.current_device()) as clk:
         for e in evs:
             one(e)
         barrier(world)
-    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
-    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    fwd_ms = [split_ms(e)[0] for e in evs]
+    bwd_ms = [split_ms(e)[1] for e in evs]
     dev_total_ms = max_over_ranks(sum(f + b for f, b in zip(fwd_ms, bwd_ms)), world)
     fwd_mean = max_over_ranks(statistics.fmean(fwd_ms), world)
     bwd_mean = max_over_ranks(statistics.fmean(bwd_ms), world)
-    del gf, gb
 
     B, S, M, D = x["value"].shape
     Q = x["sampling_locations"].shape[1]
@@ -413,39 +469,43 @@ def main(argv=None) -> int:
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": e2e_ms / args.steps}
 
-    # ---- roofline of the backward launch (dominant) -------------------------
+    # ---- per-kernel breakdown (CUPTI, untimed extra steps) -------------------
+    if args.no_kernel_breakdown:
+        kernels = {}
+        launches_per_step = None
+    else:
+        kernels = kernel_breakdown(one)
+        launches_per_step = sum(n for _, n in kernels.values())
+    del gs
+
+    # ---- roofline: the backward call (dominant), and the whole step ----------
     e = x["value"].element_size()
-    ws = msda_ops._lib.load().msda_backward_workspace_size(
-        B, S, Q, M, D, L, K, msda_ops._DTYPE_CODE[x["value"].dtype],
-        (msda_ops._lib.MSDA_BWD_FP32_ACCUM if fp32_acc else 0) | algo_flags)
-    cast_pass = ws > 0
-    owner = args.bwd_algo == "owner"
-    e_acc = 4 if cast_pass else e
-    fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, L, K, e, e_acc, cast_pass)
+    fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, L, K, e)
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (bwd_mean / 1e3) / 1e9
+    step_achieved = (fwd_b + bwd_b) / ((fwd_mean + bwd_mean) / 1e3) / 1e9
     traffic = load_traffic(f"{preset.name}-{str(dtype).replace('torch.', '')}")
-    if owner:
-        kdesc = "msda_backward (msda_bwd_kernel grad_loc/grad_attn + msda_bwd_value_owner_kernel)"
-    else:
-        kdesc = "msda_backward (zero-fill + msda_bwd_kernel" + (" + cast" if cast_pass else "") + ")"
-    roofline = {"kernel": kdesc,
+    algo = backward_algorithm(kernels) if kernels else "automatic (not inspected)"
+    roofline = {"kernel": "msda_backward call (" + " + ".join(
+                    k for k in kernels if k != "msda_fwd_kernel") + "), CUDA-event time",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                 "frac_of_nominal_8TBs": achieved / NOMINAL_HBM_GBS,
-                "traffic": traffic, "algorithmic_bytes": bwd_b, "e_acc": e_acc,
+                "traffic": traffic, "algorithmic_bytes": bwd_b,
                 "fwd": {"achieved": fwd_b / (fwd_mean / 1e3) / 1e9, "algorithmic_bytes": fwd_b,
-                        "us": fwd_mean * 1e3}}
+                        "us": fwd_mean * 1e3, "frac": fwd_b / (fwd_mean / 1e3) / 1e9 / peak},
+                "step": {"achieved": step_achieved, "algorithmic_bytes": fwd_b + bwd_b,
+                         "frac": step_achieved / peak,
+                         "frac_of_nominal_8TBs": step_achieved / NOMINAL_HBM_GBS}}
 
     # ---- CPU baseline (rank 0, N=1) ----------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec, threads = cpu_reference_time(preset, dtype, 3)
+        sec, threads, n = cpu_reference_time(preset, dtype, 3, min_seconds=10.0)
         cpu = {"value": preset.B * preset.num_queries / sec, "unit": "queries/s", "cores": threads,
-               "kind": "port", "sample": f"3 full fwd+bwd steps of the {preset.name} workload, "
+               "kind": "port", "sample": f"{n} full fwd+bwd steps of the {preset.name} workload, "
                                          f"grid_sample oracle in {str(dtype).replace('torch.', '')}"}
 
-    launches_per_step = 3 if (owner or cast_pass) else 2
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
@@ -455,9 +515,11 @@ def main(argv=None) -> int:
             "config": config_dict(preset, dtype, world),
             "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,
             "fwd_bwd_us": (fwd_mean + bwd_mean) * 1e3,
-            "fp32_grad_accum": fp32_acc, "bwd_algo": "owner" if owner else "scatter",
+            "fp32_grad_accum": fp32_acc, "bwd_algo": algo,
+            "kernels_us": {k: round(t, 2) for k, (t, _) in kernels.items()},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": (None if launches_per_step is None
+                             else int(round(launches_per_step * args.steps))),
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

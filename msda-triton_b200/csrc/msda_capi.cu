@@ -72,6 +72,7 @@ int check_shape(const Shape& s, int32_t dtype) {
 // buffer read or written in D-chunks is 16-byte aligned.
 int choose_cfg(int32_t D, int es, bool vec_ptrs_aligned, msda::Cfg* c) {
   const int v16 = 16 / es;
+  c->short_grid = false;
   if ((D % v16) == 0 && vec_ptrs_aligned) {
     c->vec = v16;
   } else {
@@ -207,6 +208,10 @@ int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t
     return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_forward: misaligned buffer (sampling_locations needs %d-byte alignment)", 2 * es);
   msda::Cfg cfg;
   if (int rc = choose_cfg(s.D, es, aligned(value, 16) && aligned(output, 16), &cfg)) return rc;
+  {
+    const int64_t ctas = (s.Q + msda::kWarpsPerCta - 1) / msda::kWarpsPerCta * s.M * s.B;
+    cfg.short_grid = ctas <= (int64_t)msda::kShortGridWaves * 4 * sm_count();
+  }
 
   msda::OpParams p{};
   p.value = value;
@@ -338,9 +343,9 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   p.BQM = s.B * s.Q * s.M;
   if (counted) {
     switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, st); break;
-      default: e = msda::launch_count<__nv_bfloat16>(p, st); break;
+      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, sm_count(), st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, sm_count(), st); break;
+      default: e = msda::launch_count<__nv_bfloat16>(p, sm_count(), st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count launch");
   }

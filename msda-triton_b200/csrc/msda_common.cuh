@@ -304,11 +304,18 @@ struct LevelInfo {
   int start;
   float fH;
   float fW;
+  int dense;  // hit-counted backward: the level's rows are accumulated in fp32 without counting
 };
+
+// A level is "dense" for the hit-counted backward when its Q*K sampling
+// points per head put at least kDenseHitsPerRow bilinear corners on each of
+// its H*W rows on average: most of its rows are then hit more than once, so
+// counting them buys nothing and their same-row counters are the hottest.
+constexpr int kDenseHitsPerRow = 2;
 
 __device__ __forceinline__ void load_levels(const int64_t* __restrict__ shapes,
                                             const int64_t* __restrict__ starts, int L, int64_t S,
-                                            LevelInfo* lv) {
+                                            LevelInfo* lv, int64_t Q = 0, int K = 0) {
   if ((int)threadIdx.x < L) {
     const int l = threadIdx.x;
     int64_t H = shapes[2 * l], W = shapes[2 * l + 1], st = starts[l];
@@ -319,6 +326,7 @@ __device__ __forceinline__ void load_levels(const int64_t* __restrict__ shapes,
     info.start = ok ? (int)st : 0;
     info.fH = (float)info.H;
     info.fW = (float)info.W;
+    info.dense = ok && 4 * Q * K >= (int64_t)kDenseHitsPerRow * H * W;
     lv[l] = info;
   }
   __syncthreads();

@@ -64,8 +64,12 @@ __device__ __forceinline__ bool query_block_of(const OpParams& p, int warps, int
 // Forward: out[b,q,m,:] = sum_{l,k} a * sum_c w_c * value[b, pix_c, m, :]
 // (src/msda_triton/kernels.py:100-163)
 // ---------------------------------------------------------------------------
-template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB>
-__global__ void __launch_bounds__(WARPS * 32) msda_fwd_kernel(const OpParams p) {
+// MINB: minimum resident CTAs per SM the forward is compiled for (0 leaves
+// the register budget to the compiler). A grid of a few waves runs faster
+// with fewer, register-richer warps per SM (MINB = 3); a long grid needs the
+// occupancy of the compiler's default.
+template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB, int MINB>
+__global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpParams p) {
   __shared__ LevelInfo lv[kMaxLevels];
   load_levels(p.shapes, p.starts, p.L, p.S, lv);
 
@@ -224,6 +228,10 @@ enum ScatterMode : int {
   kCounted = 2,    // hit-counted: one-hit rows stored, multi-hit rows reduced in fp32
 };
 
+// Hit-counted scatter: flag in a row's hit count marking a row of a dense
+// level (accumulated in fp32 whatever its count).
+constexpr unsigned kDenseRow = 0x80000000u;
+
 // Minimum resident CTAs per SM the backward is compiled for (register cap).
 #ifndef MSDA_BWD_MIN_BLOCKS
 #define MSDA_BWD_MIN_BLOCKS 4
@@ -233,7 +241,7 @@ template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, 
 __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kernel(const OpParams p) {
   constexpr bool SCATTER = MODE != kNoScatter;
   __shared__ LevelInfo lv[kMaxLevels];
-  load_levels(p.shapes, p.starts, p.L, p.S, lv);
+  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
 
   constexpr int G = 32 / LPR;
   using Raw = typename Pack<T, VEC>::Raw;
@@ -287,6 +295,7 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
     Bilinear bl[NB];
     float at[NB];
     float fw[NB], fh[NB];
+    bool dense[NB];
 #pragma unroll
     for (int n = 0; n < NB; ++n) {
       const int s = s0 + n * G + grp;
@@ -297,10 +306,12 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
         bl[n] = resolve(xy.x, xy.y, L);
         fw[n] = L.fW;
         fh[n] = L.fH;
+        dense[n] = L.dense;
       } else {
         at[n] = 0.f;
         fw[n] = fh[n] = 0.f;
         bl[n] = empty_slot();
+        dense[n] = false;
       }
     }
     Raw raw[NB][4][CPL];
@@ -310,8 +321,10 @@ __global__ void __launch_bounds__(WARPS * 32, MSDA_BWD_MIN_BLOCKS) msda_bwd_kern
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         hits[n][c] = 0u;
+        // Dense-level rows are always reduced in fp32: no count to read.
         if constexpr (MODE == kCounted)
-          if ((bl[n].valid >> c) & 1u) hits[n][c] = __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
+          if ((bl[n].valid >> c) & 1u)
+            hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
       }
 #pragma unroll
     for (int n = 0; n < NB; ++n)
@@ -895,11 +908,18 @@ __global__ void __launch_bounds__(kOwnerThreads) msda_bwd_value_owner_kernel(con
 }
 
 // ---------------------------------------------------------------------------
-// Hit-counted scatter, pass 1: count the bilinear hits of every
-// (b, pixel, m) row of grad_value, one thread per sampling point. The hit
-// that raises a row's count from 1 to 2 zero-fills that row's fp32
-// accumulator, so exactly the multi-hit rows are zeroed, once. The four
-// corner atomics are issued before any zeroing waits on their results.
+// Hit-counted scatter, pass 1 (one kernel, two roles).
+//
+// Point blocks: one thread per sampling point of a sparse level counts the
+// bilinear hits of its corner rows (b, pixel, m); the hit that raises a
+// row's count from 1 to 2 zero-fills that row's fp32 accumulator, so exactly
+// the multi-hit rows are zeroed, once. The four corner atomics are issued
+// before any zeroing waits on their results. Points of dense levels do
+// nothing here.
+//
+// Dense blocks (the last blocks of the grid): flag every row of the dense
+// levels with kDenseRow and zero its fp32 accumulator. The backward reduces
+// into flagged rows without reading their counts, the finalize rounds them.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void zero_row(float* a, int D) {
   if ((D & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
@@ -909,19 +929,75 @@ __device__ __forceinline__ void zero_row(float* a, int D) {
   }
 }
 
+// r-th pixel (0-based) of the concatenated dense levels -> pixel index in S.
+__device__ __forceinline__ int64_t dense_pixel(const LevelInfo* lv, int L, int64_t r) {
+  for (int l = 0; l < L; ++l) {
+    if (!lv[l].dense) continue;
+    const int64_t n = (int64_t)lv[l].H * lv[l].W;
+    if (r < n) return lv[l].start + r;
+    r -= n;
+  }
+  return 0;  // unreachable for r < dense pixels per batch
+}
+
+__device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelInfo* lv, int64_t tid,
+                                                 int64_t nthreads) {
+  int64_t per_batch = 0;
+  for (int l = 0; l < p.L; ++l)
+    if (lv[l].dense) per_batch += (int64_t)lv[l].H * lv[l].W;
+  if (per_batch == 0) return;
+  const int64_t pixels = p.B * per_batch;
+  for (int64_t u = tid; u < pixels * p.M; u += nthreads) {
+    const int64_t px = u / p.M;
+    const int m = (int)(u - px * p.M);
+    const int64_t b = px / per_batch;
+    const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
+    atomicOr(p.counts + (b * p.S + pix) * p.M + m, kDenseRow);
+  }
+  // A pixel's rows of all heads are contiguous: M*D floats.
+  const int64_t row_floats = (int64_t)p.M * p.D;
+  if (row_floats % 4 == 0 && (reinterpret_cast<uintptr_t>(p.acc) & 15) == 0) {
+    const int64_t q4 = row_floats / 4;
+    for (int64_t u = tid; u < pixels * q4; u += nthreads) {
+      const int64_t px = u / q4;
+      const int64_t k = u - px * q4;
+      const int64_t b = px / per_batch;
+      const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
+      reinterpret_cast<float4*>(p.acc + (b * p.S + pix) * row_floats)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+    for (int64_t u = tid; u < pixels * row_floats; u += nthreads) {
+      const int64_t px = u / row_floats;
+      const int64_t k = u - px * row_floats;
+      const int64_t b = px / per_batch;
+      const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
+      p.acc[(b * p.S + pix) * row_floats + k] = 0.f;
+    }
+  }
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p) {
+__global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsigned point_blocks) {
   __shared__ LevelInfo lv[kMaxLevels];
-  load_levels(p.shapes, p.starts, p.L, p.S, lv);
   const int LK = p.L * p.K;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= p.BQM * LK) return;
+  const bool point = blockIdx.x < point_blocks && i < p.BQM * LK;
+  float2 xy = make_float2(0.f, 0.f);
+  if (point) xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);  // in flight across the sync
+  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
+  if (blockIdx.x >= point_blocks) {
+    count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * blockDim.x + threadIdx.x,
+                     (int64_t)(gridDim.x - point_blocks) * blockDim.x);
+    return;
+  }
+  if (!point) return;
   const int64_t qm = i / LK;
   const int s = (int)(i - qm * LK);
+  const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
+  if (L.dense) return;
   const int64_t b = qm / (p.Q * p.M);
   const int m = (int)(qm % p.M);
-  const float2 xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);
-  const Bilinear bl = resolve(xy.x, xy.y, lv[level_of(s, p.K, p.kshift)]);
+  const Bilinear bl = resolve(xy.x, xy.y, L);
   unsigned old[4];
   int64_t row[4];
 #pragma unroll
@@ -930,14 +1006,17 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p) {
     row[c] = (b * p.S + bl.pix[c]) * p.M + m;
     if ((bl.valid >> c) & 1u) old[c] = atomicAdd(p.counts + row[c], 1u);
   }
+  // old == 1 only on unflagged rows: a flagged (dense) row is zeroed by the
+  // dense blocks.
 #pragma unroll
   for (int c = 0; c < 4; ++c)
     if (((bl.valid >> c) & 1u) && old[c] == 1u) zero_row(p.acc + row[c] * p.D, p.D);
 }
 
-// Hit-counted scatter, pass 3: rows nothing hit become zeros; multi-hit rows
-// are rounded from their fp32 accumulator (skipped when grad_value itself is
-// the fp32 accumulator); one-hit rows were already stored by the backward.
+// Hit-counted scatter, pass 3: rows nothing hit become zeros; multi-hit and
+// dense-level rows (count > 1, or the kDenseRow flag) are rounded from their
+// fp32 accumulator (skipped when grad_value itself is the fp32 accumulator);
+// one-hit rows were already stored by the backward.
 // One thread per 4 consecutive rows x VEC elements (one 16-byte count load).
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {

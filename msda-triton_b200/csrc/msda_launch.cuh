@@ -12,7 +12,12 @@ struct Cfg {
   int vec;
   int lpr;
   int cpl;
+  bool short_grid;  // the query-block grid is at most kShortGridWaves waves
 };
+
+// Forward grids of at most this many waves (at 4 CTAs per SM) use the
+// register-richer forward variant.
+constexpr int kShortGridWaves = 4;
 
 constexpr int kWarpsPerCta = 8;
 
@@ -25,10 +30,11 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
 template <typename T>
 cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
                             cudaStream_t st);
-// Hit-counted scatter passes 1 (count hits, zero multi-hit accumulators) and
-// 3 (zeros / downcast). p.counts must be zeroed before launch_count.
+// Hit-counted scatter passes 1 (count hits, zero the accumulators that will
+// be reduced into) and 3 (zeros / downcast). p.counts must be zeroed before
+// launch_count.
 template <typename T>
-cudaError_t launch_count(const OpParams& p, cudaStream_t st);
+cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st);
 template <typename T>
 cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st);
 
@@ -74,10 +80,13 @@ template <typename T, int VEC>
 static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid = query_block_grid(p);
-#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                             \
-  if (c.lpr == LPR_ && c.cpl == CPL_) {                                            \
-    msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_><<<grid, block, 0, st>>>(p); \
-    return cudaGetLastError();                                                     \
+#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                                   \
+  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                  \
+    if (VEC > 1 && c.short_grid)                                                         \
+      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 3><<<grid, block, 0, st>>>(p); \
+    else                                                                                 \
+      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 0><<<grid, block, 0, st>>>(p); \
+    return cudaGetLastError();                                                           \
   }
   MSDA_FOR_EACH_SHAPE(MSDA_FWD_CASE)
 #undef MSDA_FWD_CASE
@@ -129,11 +138,15 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32
 }
 
 template <typename T>
-cudaError_t launch_count(const OpParams& p, cudaStream_t st) {
+cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
   const int64_t n = p.BQM * p.L * p.K;
-  const int64_t blocks = (n + 255) / 256;
-  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  msda_count_kernel<T><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
+  const int64_t point_blocks = (n + 255) / 256;
+  // The dense rows are not known on the host (the level table is on the
+  // device): enough blocks for all of them, capped at two waves' worth.
+  const int64_t acc_vec4 = (p.B * p.S * p.M * p.D + 3) / 4;
+  const int64_t dense_blocks = std::max<int64_t>(1, std::min<int64_t>(2 * num_sms, (acc_vec4 + 255) / 256));
+  if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  msda_count_kernel<T><<<(unsigned)(point_blocks + dense_blocks), 256, 0, st>>>(p, (unsigned)point_blocks);
   return cudaGetLastError();
 }
 
@@ -207,7 +220,7 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
   template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, bool, cudaStream_t);  \
-  template cudaError_t launch_count<T>(const OpParams&, cudaStream_t);                            \
+  template cudaError_t launch_count<T>(const OpParams&, int, cudaStream_t);                         \
   template cudaError_t launch_finalize<T>(const OpParams&, bool, int, cudaStream_t);              \
   template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);

@@ -11,7 +11,7 @@ import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(os.environ.get("MSDA_B200_LIB", Path(__file__).resolve().parent / "libmsda_b200.so"))
+LIB_PATH = Path(os.environ.get("MSDA_B200_LIB") or (Path(__file__).resolve().parent / "libmsda_b200.so"))
 
 MSDA_OK = 0
 MSDA_ERR_INVALID_ARGUMENT = 1
