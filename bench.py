@@ -7,8 +7,10 @@
 A step is one forward + backward of the multi-scale deformable attention op
 over one batch of the configured operating point (default: the
 Deformable-DETR decoder preset, B=4 Q=300 M=8 D=32 L=4 K=4, bf16). With N
-ranks every rank runs its own batch (weak scaling over the batch axis; the op
-path has no collective) and NCCL only carries the timing reduction.
+ranks every rank runs the op on its own batch slice (msda_triton_b200.sharding:
+weak scaling, B items per rank, for the per-GPU presets; strong scaling, the
+global B split N ways, for `scale`/`scale_d64`); the op path has no
+collective and NCCL only carries the timing reduction.
 
 Reported (one JSON line on rank 0):
   value      queries/s over all ranks (B*Q*N / device time), inputs resident
@@ -44,7 +46,7 @@ import torch
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "msda-triton_b200"))
 
-from msda_triton_b200 import multi_scale_deformable_attention, presets  # noqa: E402
+from msda_triton_b200 import multi_scale_deformable_attention, presets, sharding  # noqa: E402
 from msda_triton_b200 import ops as msda_ops  # noqa: E402
 
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
@@ -147,39 +149,41 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Distributed plumbing
 # ---------------------------------------------------------------------------
+class _StdoutToStderr:
+    """Send file descriptor 1 to stderr for a while (NCCL prints its version
+    banner on stdout during communicator setup; stdout carries only the
+    JSON line)."""
+
+    def __enter__(self):
+        import ctypes
+
+        self._libc = ctypes.CDLL(None)
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        self._libc.fflush(None)
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+
+
 def dist_setup(n_gpus: int):
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != n_gpus:
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch with torchrun for N>1")
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    return rank, world, local
-
-
-def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
-        return x
-    import torch.distributed as dist
+        return sharding.init_ranks("nccl", timeout_s=120)
+    with _StdoutToStderr():
+        ranks = sharding.init_ranks("nccl", timeout_s=120)
+        sharding.barrier(world)  # the communicator exists after the first collective
+    return ranks
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
 
-
-def barrier(world: int):
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize()
+max_over_ranks = sharding.max_over_ranks
+barrier = sharding.barrier
 
 
 # ---------------------------------------------------------------------------
@@ -315,17 +319,25 @@ def e2e_leg(x, steps, warmup, fp32_acc):
     return step, h2d, d2h
 
 
+CPU_SAMPLE_MAX_BATCH = 4  # the CPU legs time at most 4 batch items per step
+
+
+def cpu_sample_batch(preset):
+    return min(preset.B, CPU_SAMPLE_MAX_BATCH)
+
+
 def cpu_reference_time(preset, dtype, steps, seed=0, min_seconds=0.0):
     """The reference's CPU implementation (grid_sample forward + autograd
-    backward, oracle/msda_oracle.py) on all host cores: (seconds per step,
-    threads, steps run). Runs at least `steps` steps and at least
-    `min_seconds`."""
+    backward, oracle/msda_oracle.py) on all host cores, over
+    cpu_sample_batch(preset) batch items: (seconds per step, threads, steps
+    run). Runs at least `steps` steps and at least `min_seconds`."""
     sys.path.insert(0, str(REPO))
     from oracle import msda_oracle as orc
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    x = presets.make_inputs(preset, dtype=dtype, device="cpu", seed=seed)
+    x = presets.make_inputs(preset, dtype=dtype, device="cpu", seed=seed,
+                            batch=cpu_sample_batch(preset))
 
     def step():
         v = x["value"].clone().requires_grad_(True)
@@ -370,12 +382,14 @@ def run_reference_arm(args, preset, dtype):
     for _ in range(min(args.warmup, 2)):
         cpu_reference_time(preset, dtype, 1)
     sec, threads, steps = cpu_reference_time(preset, dtype, steps)
-    qps = preset.B * preset.num_queries / sec
-    sample = f"{steps} full fwd+bwd steps of the {preset.name} workload ({dtype}) on {threads} threads"
+    nb = cpu_sample_batch(preset)
+    qps = nb * preset.num_queries / sec
+    sample = (f"{steps} fwd+bwd steps of {nb} batch item(s) of the {preset.name} workload "
+              f"({dtype}) on {threads} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": preset.scaling, "vs_baseline": None,
         "dtype": str(dtype).replace("torch.", ""), "data": "synthetic",
         "config": config_dict(preset, dtype, args.gpus),
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
@@ -387,8 +401,9 @@ def run_reference_arm(args, preset, dtype):
 
 
 def config_dict(preset, dtype, n):
-    return {"workload": f"{preset.name} preset: {preset.note}", "batch_per_gpu": preset.B,
-            "global_batch": preset.B * n, "queries": preset.num_queries, "heads": preset.M,
+    gb = sharding.global_batch(preset, n)
+    return {"workload": f"{preset.name} preset: {preset.note}", "batch_per_gpu": gb // n,
+            "global_batch": gb, "queries": preset.num_queries, "heads": preset.M,
             "head_dim": preset.D, "levels": preset.L, "points": preset.K,
             "spatial_shapes": [list(s) for s in preset.shapes], "S": preset.S,
             "dtype": str(dtype).replace("torch.", ""), "parallelism": f"batch-sharded x{n}",
@@ -424,7 +439,8 @@ def main(argv=None) -> int:
 
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
-    x = presets.make_inputs(preset, dtype=dtype, device="cuda", seed=rank)
+    b0, nb = sharding.rank_batch(preset, world, rank)
+    x = presets.make_inputs(preset, dtype=dtype, device="cuda", batch=nb, batch_offset=b0)
     fp32_acc = {"auto": msda_ops._use_fp32_grad_accum(x["value"]), "on": True,
                 "off": False}[args.fp32_grad_accum]
 
@@ -450,7 +466,7 @@ def main(argv=None) -> int:
     B, S, M, D = x["value"].shape
     Q = x["sampling_locations"].shape[1]
     L, K = preset.L, preset.K
-    queries_per_step = B * Q * world
+    queries_per_step = sharding.global_batch(preset, world) * Q
     value = queries_per_step * args.steps / (dev_total_ms / 1e3)
 
     # ---- e2e leg ----------------------------------------------------------
@@ -502,15 +518,17 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, threads, n = cpu_reference_time(preset, dtype, 3, min_seconds=10.0)
-        cpu = {"value": preset.B * preset.num_queries / sec, "unit": "queries/s", "cores": threads,
-               "kind": "port", "sample": f"{n} full fwd+bwd steps of the {preset.name} workload, "
-                                         f"grid_sample oracle in {str(dtype).replace('torch.', '')}"}
+        nb = cpu_sample_batch(preset)
+        cpu = {"value": nb * preset.num_queries / sec, "unit": "queries/s", "cores": threads,
+               "kind": "port", "sample": f"{n} fwd+bwd steps of {nb} batch item(s) of the "
+                                         f"{preset.name} workload, grid_sample oracle in "
+                                         f"{str(dtype).replace('torch.', '')}"}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": preset.scaling, "vs_baseline": None,
             "dtype": str(dtype).replace("torch.", ""), "data": "synthetic",
             "config": config_dict(preset, dtype, world),
             "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,

@@ -3,8 +3,10 @@
 The pyramid shapes follow the reference benchmark's presets
 (benchmarks/modal_benchmark.py:73-98: strides 8..64 with ceil division on an
 800x1333 image, 8 heads x 32 channels, 4 levels x 4 points). Inputs are
-generated on the CPU from one ``torch.Generator`` seed, in a fixed draw order,
-so every process (test, bench rank, CPU baseline) builds identical tensors:
+generated on the CPU, batch item by batch item, each item from its own
+``torch.Generator`` seeded by (seed, global item index) in a fixed draw order,
+so every process (test, bench rank, CPU baseline) builds identical tensors and
+a rank can build just its own slice of a global batch:
 
 * value ~ N(0, 1);
 * attention_weights = softmax over the L*K axis of N(0, 1) logits;
@@ -44,6 +46,7 @@ class Preset:
     loc_mode: str = "uniform"  # "uniform" or "pixel_centre"
     loc_lo: float = 0.0
     loc_hi: float = 1.0
+    scaling: str = "weak"  # "weak": B per rank; "strong": B is the global batch, split over ranks
     note: str = field(default="", compare=False)
 
     @property
@@ -72,10 +75,11 @@ PRESETS: dict[str, Preset] = {
                   dtype=torch.float16, loc_lo=-0.1, loc_hi=1.1,
                   note="Mask2Former pixel decoder; out-of-bounds corners"),
     "scale": Preset("scale", B=64, M=8, D=32, K=4, shapes=_DETR, Q=None, dtype=torch.bfloat16,
-                    loc_mode="pixel_centre", note="global batch for the batch-sharded sweep"),
+                    loc_mode="pixel_centre", scaling="strong",
+                    note="global batch 64 split over the ranks, encoder shapes"),
     "scale_d64": Preset("scale_d64", B=64, M=4, D=64, K=4, shapes=_DETR, Q=None,
-                        dtype=torch.bfloat16, loc_mode="pixel_centre",
-                        note="256 channels as 4 heads x 64"),
+                        dtype=torch.bfloat16, loc_mode="pixel_centre", scaling="strong",
+                        note="global batch 64 split over the ranks, 256 channels as 4 heads x 64"),
 }
 
 
@@ -94,24 +98,38 @@ def _pixel_centres(shapes) -> torch.Tensor:
     return torch.cat(parts)
 
 
+def _item_generator(seed: int, item: int) -> torch.Generator:
+    return torch.Generator().manual_seed((seed * 1_000_003 + item) & 0x7FFF_FFFF_FFFF_FFFF)
+
+
 def make_inputs(preset: Preset, *, dtype: torch.dtype | None = None, device="cpu", seed: int = 0,
-                batch: int | None = None, with_grad: bool = True) -> dict[str, torch.Tensor]:
-    """Seeded synthetic inputs for ``preset`` (B overridden by ``batch``)."""
+                batch: int | None = None, batch_offset: int = 0,
+                with_grad: bool = True) -> dict[str, torch.Tensor]:
+    """Seeded synthetic inputs for ``preset``: global batch items
+    ``batch_offset .. batch_offset + batch - 1`` (``batch`` defaults to B)."""
     dtype = dtype or preset.dtype
     B = preset.B if batch is None else batch
     M, D, K, L, S, Q = preset.M, preset.D, preset.K, preset.L, preset.S, preset.num_queries
-    gen = torch.Generator().manual_seed(seed)
-    value = torch.randn(B, S, M, D, generator=gen)
+    centre = None
     if preset.loc_mode == "pixel_centre":
         if Q != S:
             raise ValueError("pixel_centre locations need one query per value row")
-        centre = _pixel_centres(preset.shapes).view(1, Q, 1, 1, 1, 2)
-        loc = centre + 0.02 * torch.randn(B, Q, M, L, K, 2, generator=gen)
-        loc = loc.clamp_(-0.05, 1.05)
-    else:
-        loc = preset.loc_lo + (preset.loc_hi - preset.loc_lo) * torch.rand(
-            B, Q, M, L, K, 2, generator=gen)
-    logits = torch.randn(B, Q, M, L * K, generator=gen)
+        centre = _pixel_centres(preset.shapes).view(Q, 1, 1, 1, 2)
+    value = torch.empty(B, S, M, D)
+    loc = torch.empty(B, Q, M, L, K, 2)
+    logits = torch.empty(B, Q, M, L * K)
+    grad = torch.empty(B, Q, M * D) if with_grad else None
+    for b in range(B):
+        gen = _item_generator(seed, batch_offset + b)
+        value[b] = torch.randn(S, M, D, generator=gen)
+        if centre is not None:
+            loc[b] = (centre + 0.02 * torch.randn(Q, M, L, K, 2, generator=gen)).clamp_(-0.05, 1.05)
+        else:
+            loc[b] = preset.loc_lo + (preset.loc_hi - preset.loc_lo) * torch.rand(
+                Q, M, L, K, 2, generator=gen)
+        logits[b] = torch.randn(Q, M, L * K, generator=gen)
+        if with_grad:
+            grad[b] = torch.randn(Q, M * D, generator=gen)
     attn = logits.softmax(-1).view(B, Q, M, L, K)
     out = {
         "value": value.to(device=device, dtype=dtype),
@@ -122,5 +140,5 @@ def make_inputs(preset: Preset, *, dtype: torch.dtype | None = None, device="cpu
     hw = out["spatial_shapes"].prod(-1)
     out["level_start_index"] = torch.cat([hw.new_zeros(1), hw.cumsum(0)[:-1]])
     if with_grad:
-        out["grad_output"] = torch.randn(B, Q, M * D, generator=gen).to(device=device, dtype=dtype)
+        out["grad_output"] = grad.to(device=device, dtype=dtype)
     return out
