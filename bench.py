@@ -18,8 +18,9 @@ Reported (one JSON line on rank 0):
              per step (forward then backward launches), L2 flushed before
              every step, max over ranks.
   e2e        the same metric through the public op with pinned HOST buffers:
-             host->device copies of the inputs and device->host copies of the
-             output and the three gradients inside the timed region.
+             every step copies its inputs host->device and the output and the
+             three gradients device->host inside the timed region (copies of
+             neighbouring steps overlap on two copy streams).
   roofline   the backward call (the dominant launch sequence): algorithmic
              bytes / its CUDA-event time against the measured HBM copy
              bandwidth; `step` gives the same for forward + backward.
@@ -287,10 +288,16 @@ def backward_algorithm(kernels):
 
 
 def e2e_leg(x, steps, warmup, fp32_acc):
-    """Public op with pinned host buffers: H2D inputs, forward, backward, D2H
-    output and gradients, all inside each timed step."""
-    host = {k: x[k].cpu().pin_memory() for k in ("value", "sampling_locations", "attention_weights",
-                                                 "grad_output")}
+    """Public op with pinned host buffers. Every step copies its inputs
+    host->device, runs forward + backward through
+    multi_scale_deformable_attention, and copies the output and the three
+    gradients device->host. The steps are pipelined the way a data loader
+    would run them: the inputs of step i+1 go up on one copy stream and the
+    results of step i come down on another while step i computes (PCIe is
+    full duplex), with two device input buffers. Returns run(n) -> None,
+    which runs n such steps, and the bytes copied per step each way."""
+    keys = ("value", "sampling_locations", "attention_weights", "grad_output")
+    host = {k: x[k].cpu().pin_memory() for k in keys}
     shapes, starts = x["spatial_shapes"], x["level_start_index"]
     B, S, M, D = x["value"].shape
     Q = x["sampling_locations"].shape[1]
@@ -300,23 +307,46 @@ def e2e_leg(x, steps, warmup, fp32_acc):
     ga_h = torch.empty_like(host["attention_weights"]).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in (out_h, gv_h, gl_h, ga_h))
+    compute = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    bufs = [{k: torch.empty_like(x[k]) for k in keys} for _ in range(2)]
 
-    def step():
-        v = host["value"].to("cuda", non_blocking=True).requires_grad_(True)
-        l = host["sampling_locations"].to("cuda", non_blocking=True).requires_grad_(True)
-        a = host["attention_weights"].to("cuda", non_blocking=True).requires_grad_(True)
-        g = host["grad_output"].to("cuda", non_blocking=True)
-        out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc)
-        out.backward(g)
-        out_h.copy_(out.detach(), non_blocking=True)
-        gv_h.copy_(v.grad, non_blocking=True)
-        gl_h.copy_(l.grad, non_blocking=True)
-        ga_h.copy_(a.grad, non_blocking=True)
+    def run(n):
+        up = [torch.cuda.Event() for _ in range(2)]    # inputs of a buffer are on the device
+        used = [torch.cuda.Event() for _ in range(2)]  # a buffer's step has finished with it
+        used[0].record(compute)
+        used[1].record(compute)
 
-    for _ in range(warmup):
-        step()
+        def upload(i):
+            s_in.wait_event(used[i % 2])
+            with torch.cuda.stream(s_in):
+                for k in keys:
+                    bufs[i % 2][k].copy_(host[k], non_blocking=True)
+            up[i % 2].record(s_in)
+
+        upload(0)
+        for i in range(n):
+            compute.wait_event(up[i % 2])
+            b = bufs[i % 2]
+            v = b["value"].detach().requires_grad_(True)
+            l = b["sampling_locations"].detach().requires_grad_(True)
+            a = b["attention_weights"].detach().requires_grad_(True)
+            out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc)
+            out.backward(b["grad_output"])
+            used[i % 2].record(compute)
+            if i + 1 < n:
+                upload(i + 1)  # into the other buffer, once step i-1 is done with it
+            s_out.wait_stream(compute)
+            with torch.cuda.stream(s_out):
+                results = (out.detach(), v.grad, l.grad, a.grad)
+                for dst, src in zip((out_h, gv_h, gl_h, ga_h), results):
+                    dst.copy_(src, non_blocking=True)
+                    src.record_stream(s_out)
+        compute.wait_stream(s_out)
+
+    run(warmup)
     torch.cuda.synchronize()
-    return step, h2d, d2h
+    return run, h2d, d2h
 
 
 CPU_SAMPLE_MAX_BATCH = 4  # the CPU legs time at most 4 batch items per step
@@ -472,12 +502,11 @@ def main(argv=None) -> int:
     # ---- e2e leg ----------------------------------------------------------
     e2e = None
     if not args.no_e2e:
-        step, h2d, d2h = e2e_leg(x, args.steps, args.warmup, fp32_acc)
+        run_e2e, h2d, d2h = e2e_leg(x, args.steps, args.warmup, fp32_acc)
         barrier(world)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
-        for _ in range(args.steps):
-            step()
+        run_e2e(args.steps)
         t1.record()
         barrier(world)
         e2e_ms = max_over_ranks(t0.elapsed_time(t1), world)

@@ -58,20 +58,22 @@ typedef enum msda_status {
 
 /* Backward flags. */
 /* Accumulate grad_value in fp32 and round to the value dtype once (the
- * fp32_grad_accum=True path of src/msda_triton/ops.py:76-92). Without it the
- * library may use native fp16/bf16 atomics; it still accumulates in fp32
- * whenever the fp32 kernel is the faster one (see MSDA_BWD_FORCE_*). */
+ * fp32_grad_accum=True path of src/msda_triton/ops.py:76-92). Without it
+ * fp16/bf16 gradients are added with native packed fp16x2/bf16x2 reductions
+ * (fp32 inputs always accumulate in fp32). */
 #define MSDA_BWD_FP32_ACCUM 1u
 /* Force the grad_value algorithm (tests and benchmarks; default: automatic).
  * SCATTER: one pass over sampling points with vector `red.global` adds
  *   (fp32 workspace + downcast when MSDA_BWD_FP32_ACCUM is set for fp16/bf16,
  *   native packed fp16x2/bf16x2 adds otherwise).
  * COUNTED: hit-counted scatter -- a first pass counts the bilinear hits of
- *   every grad_value row; rows hit once get their single contribution stored,
- *   rows hit more often accumulate in fp32 rows of the workspace; a last pass
- *   writes zeros / rounds the multi-hit rows. Same result as fp32
- *   accumulation, with fp32 traffic only for the multi-hit rows (the
- *   automatic choice for fp32 accumulation when sampling is sparse).
+ *   the grad_value rows of the sparse levels (levels with fewer than two
+ *   corner hits per row on average) and flags the rows of the dense levels;
+ *   rows hit once get their single contribution stored, rows hit more often
+ *   and flagged rows accumulate in fp32 rows of the workspace; a last pass
+ *   writes zeros / rounds the fp32 rows. Same result as fp32 accumulation,
+ *   with fp32 traffic only where rows are hit more than once (the automatic
+ *   choice for fp32 accumulation when sampling is sparse, Q*L*K <= 2*S).
  * OWNER: pixel-chunk ownership -- each CTA accumulates chunks of grad_value
  *   rows in fp32 shared memory and writes each once; no workspace, no
  *   zero-fill, no global atomics. Falls back to SCATTER when a head slice has

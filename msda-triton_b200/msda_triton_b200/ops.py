@@ -34,11 +34,11 @@ def _use_fp32_grad_accum(value: torch.Tensor) -> bool:
     default: a native bf16/fp16 add rounds the running sum at every hit, and
     at encoder density (about 1300 hits per coarse-level element) that error
     exceeds 1e-2 relative. fp32 inputs always accumulate in fp32, so the flag
-    only matters for fp16/bf16. ``fp32_grad_accum=False`` permits the native
-    packed f16x2/bf16x2 `red` path; where sampling is sparse (fewer sampling
-    points than value rows per head, e.g. a DETR decoder) the library uses
-    its pixel-chunk owner kernel either way, which accumulates in fp32 and is
-    the faster of the two there.
+    only matters for fp16/bf16. ``fp32_grad_accum=False`` selects the native
+    packed f16x2/bf16x2 `red` path. With fp32 accumulation and sparse
+    sampling (Q*L*K <= 2*S per head, e.g. a DETR decoder) the library uses
+    its hit-counted backward, which writes rows hit once directly and keeps
+    fp32 rows only where a row is hit more than once.
     """
     return value.dtype != torch.float32
 
