@@ -313,12 +313,18 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
     counted_ws_bytes(s, dtype, &acc_off);
     e = cudaMemsetAsync(workspace, 0, (size_t)s.B * s.S * s.M * sizeof(unsigned), st);
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count zero-fill");
-  } else if (algo != Algo::kOwner) {
+  }
+  // The backward may overlap the tail of the kernel before it when that
+  // kernel is ours (the hit count, or the zero-fill kernel; not a memset).
+  bool bwd_pdl = counted;
+  if (!counted && algo != Algo::kOwner) {
     const size_t zbytes = fp32_ws ? ws_need : gv_bytes;
-    if (zbytes % 16 == 0 && aligned(target, 16))
+    if (zbytes % 16 == 0 && aligned(target, 16)) {
       e = msda::launch_zero(target, zbytes, sm_count(), st);
-    else
+      bwd_pdl = zbytes >= 16;
+    } else {
       e = cudaMemsetAsync(target, 0, zbytes, st);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
   }
 
@@ -351,9 +357,9 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   }
   const int mode = algo == Algo::kOwner ? msda::kNoScatter : counted ? msda::kCounted : msda::kScatter;
   switch (dtype) {
-    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, true, st); break;
-    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, fp32_ws, st); break;
-    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, mode, fp32_ws, st); break;
+    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, true, bwd_pdl, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, fp32_ws, bwd_pdl, st); break;
+    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, mode, fp32_ws, bwd_pdl, st); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
   if (counted) {

@@ -90,6 +90,17 @@ __device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the kernel before it still runs; pdl_wait()
+// blocks until that kernel has completed and its writes are visible (it
+// returns at once for a kernel launched without the attribute).
+// pdl_trigger() lets the kernel after this one be scheduled as soon as
+// every CTA of this grid has issued it (it still waits in pdl_wait()).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // Packed fp32 pairs for sm_100's f32x2 FMA (two fp32 lanes per 64-bit register).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {

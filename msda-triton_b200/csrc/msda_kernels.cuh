@@ -246,6 +246,7 @@ template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, 
 __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS)
     msda_bwd_kernel(const OpParams p) {
   constexpr bool SCATTER = MODE != kNoScatter;
+  pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
   load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
 
@@ -325,16 +326,6 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
 #pragma unroll
     for (int n = 0; n < NB; ++n)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        hits[n][c] = 0u;
-        // Dense-level rows are always reduced in fp32: no count to read.
-        if constexpr (MODE == kCounted)
-          if ((bl[n].valid >> c) & 1u)
-            hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
-      }
-#pragma unroll
-    for (int n = 0; n < NB; ++n)
-#pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int j = 0; j < CPL; ++j) {
@@ -351,6 +342,19 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
           raw[n][c][j] = r;
         }
 
+    // The value gathers above need nothing from the kernel before this one
+    // (the zero-fill or the hit count); the counts and the reduction target do.
+    if constexpr (SCATTER) pdl_wait();
+#pragma unroll
+    for (int n = 0; n < NB; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        hits[n][c] = 0u;
+        // Dense-level rows are always reduced in fp32: no count to read.
+        if constexpr (MODE == kCounted)
+          if ((bl[n].valid >> c) & 1u)
+            hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
+      }
 #pragma unroll
     for (int n = 0; n < NB; ++n) {
       // Per-corner dot products over this lane's channels,
@@ -984,6 +988,7 @@ __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelI
 
 template <typename T>
 __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsigned point_blocks) {
+  pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
   const int LK = p.L * p.K;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -1029,41 +1034,45 @@ __global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {
   const int D = p.D;
   const int per_row = D / VEC;
   const int64_t rows = p.B * p.S * p.M;
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t quad = t / per_row;  // rows 4*quad .. 4*quad+3
-  if (quad * 4 >= rows) return;
-  const int chunk = (int)(t - quad * per_row);
-  unsigned cnt[4];
-  if (quad * 4 + 3 < rows && (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0) {
-    const uint4 c4 = __ldg(reinterpret_cast<const uint4*>(p.counts) + quad);
-    cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
-  } else {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) cnt[r] = quad * 4 + r < rows ? __ldg(p.counts + quad * 4 + r) : 1u;
-  }
+  const int64_t quads = (rows + 3) / 4;
   const bool in_place = reinterpret_cast<const void*>(p.acc) == p.grad_value;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    if (cnt[r] == 1u || (cnt[r] > 1u && in_place)) continue;
-    const int64_t e = (quad * 4 + r) * D + chunk * VEC;
-    float v[VEC];
-    if (cnt[r] == 0u) {
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = 0.f;
-    } else if constexpr (VEC % 4 == 0) {
-#pragma unroll
-      for (int k = 0; k < VEC; k += 4) {
-        const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
-        v[k] = f.x;
-        v[k + 1] = f.y;
-        v[k + 2] = f.z;
-        v[k + 3] = f.w;
-      }
+  const bool quad_loads = (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0;
+  pdl_wait();  // counts and fp32 rows come from the count pass and the backward
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < quads * per_row;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t quad = t / per_row;  // rows 4*quad .. 4*quad+3
+    const int chunk = (int)(t - quad * per_row);
+    unsigned cnt[4];
+    if (quad * 4 + 3 < rows && quad_loads) {
+      const uint4 c4 = __ldg(reinterpret_cast<const uint4*>(p.counts) + quad);
+      cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+      for (int r = 0; r < 4; ++r) cnt[r] = quad * 4 + r < rows ? __ldg(p.counts + quad * 4 + r) : 1u;
     }
-    store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      if (cnt[r] == 1u || (cnt[r] > 1u && in_place)) continue;
+      const int64_t e = (quad * 4 + r) * D + chunk * VEC;
+      float v[VEC];
+      if (cnt[r] == 0u) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+      } else if constexpr (VEC % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < VEC; k += 4) {
+          const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
+          v[k] = f.x;
+          v[k + 1] = f.y;
+          v[k + 2] = f.z;
+          v[k + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+      }
+      store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
+    }
   }
 }
 
@@ -1071,6 +1080,7 @@ __global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {
 // evict_last stores, so the lines the reductions hit next are already in L2.
 template <int kUnused = 0>  // a template, so the header can define it in every unit
 __global__ void __launch_bounds__(256) msda_zero_kernel(void* __restrict__ dst, int64_t n16) {
+  pdl_trigger();
   const uint64_t pol = policy_evict_last();
   char* d = reinterpret_cast<char*>(dst);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
@@ -1082,6 +1092,7 @@ __global__ void __launch_bounds__(256) msda_zero_kernel(void* __restrict__ dst, 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict__ src, T* __restrict__ dst,
                                                        int64_t nvec) {
+  pdl_wait();  // the fp32 rows come from the backward
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
     float v[VEC];

@@ -19,6 +19,26 @@ struct Cfg {
 // register-richer forward variant.
 constexpr int kShortGridWaves = 4;
 
+// Launch `kernel` on `st`; with `pdl` the launch may overlap the tail of the
+// kernel before it in the stream (programmatic stream serialization): the
+// kernel must call pdl_wait() before it reads anything that kernel writes.
+// Only for a kernel whose predecessor in the stream is one of ours.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 constexpr int kWarpsPerCta = 8;
 
 template <typename T>
@@ -27,9 +47,12 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
 // handling `mode` (ScatterMode): kScatter adds with vector `red` into
 // p.grad_value (fp32 when fp32_scatter, else the value dtype); kCounted stores
 // one-hit rows and reduces multi-hit rows into p.acc (needs the counts).
+// `pdl`: the kernel before this one in the stream is our zero-fill or hit
+// count (the backward waits for it only before its first count read /
+// reduction).
 template <typename T>
 cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
-                            cudaStream_t st);
+                            bool pdl, cudaStream_t st);
 // Hit-counted scatter passes 1 (count hits, zero the accumulators that will
 // be reduced into) and 3 (zeros / downcast). p.counts must be zeroed before
 // launch_count.
@@ -94,16 +117,15 @@ static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st
 }
 
 template <typename T, typename A, int VEC, int MODE>
-static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
+static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, bool pdl, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid = query_block_grid(p);
 // The backward keeps one point per group in flight (NB = 1): its per-point
 // state (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
-#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                            \
-  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                           \
-    msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE><<<grid, block, 0, st>>>(p);      \
-    return cudaGetLastError();                                                                    \
-  }
+#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                             \
+  if (c.lpr == LPR_ && c.cpl == CPL_)                                                              \
+    return launch_ex(msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE>, grid, block, 0, \
+                     st, pdl, p);
   MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
 #undef MSDA_BWD_CASE
   return cudaErrorInvalidConfiguration;
@@ -119,20 +141,20 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
 
 template <typename T>
 cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
-                            cudaStream_t st) {
+                            bool pdl, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
   if (mode == kNoScatter) {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, kNoScatter>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, kNoScatter>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kNoScatter>(p, c, false, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kNoScatter>(p, c, false, st);
   } else if (mode == kCounted) {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, kCounted>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, kCounted>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kCounted>(p, c, pdl, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kCounted>(p, c, pdl, st);
   } else if (fp32_scatter || sizeof(T) == 4) {
-    if (c.vec == V16) return bwd_by_shape<T, float, V16, kScatter>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, float, 1, kScatter>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, float, V16, kScatter>(p, c, pdl, st);
+    if (c.vec == 1) return bwd_by_shape<T, float, 1, kScatter>(p, c, pdl, st);
   } else {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, kScatter>(p, c, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, kScatter>(p, c, st);
+    if (c.vec == V16) return bwd_by_shape<T, T, V16, kScatter>(p, c, pdl, st);
+    if (c.vec == 1) return bwd_by_shape<T, T, 1, kScatter>(p, c, pdl, st);
   }
   return cudaErrorInvalidConfiguration;
 }
@@ -143,6 +165,8 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
   const int64_t point_blocks = (n + 255) / 256;
   // The dense rows are not known on the host (the level table is on the
   // device): enough blocks for all of them, capped at two waves' worth.
+  // (One block per SM, which keeps the decoder's grid to one wave, measured
+  // 1-2 us slower end to end.)
   const int64_t acc_vec4 = (p.B * p.S * p.M * p.D + 3) / 4;
   const int64_t dense_blocks = std::max<int64_t>(1, std::min<int64_t>(2 * num_sms, (acc_vec4 + 255) / 256));
   if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
@@ -152,18 +176,18 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
 
 template <typename T>
 cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st) {
-  (void)num_sms;
   constexpr int V16 = 16 / (int)sizeof(T);
   const int64_t rows = p.B * p.S * p.M;
   const int vec = (vec_ok && p.D % V16 == 0 && p.D % 4 == 0) ? V16 : 1;
   const int64_t n = (rows + 3) / 4 * (p.D / vec);
+  // One thread per 4 rows x VEC elements (a one-wave grid-stride variant
+  // measured slower behind the backward's programmatic launch).
+  (void)num_sms;
   const int64_t blocks = (n + 255) / 256;
-  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  if (vec == V16)
-    msda_finalize_kernel<T, V16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
-  else
-    msda_finalize_kernel<T, 1><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(p);
-  return cudaGetLastError();
+  // The backward runs right before: overlap its tail (the finalize waits).
+  const dim3 grid((unsigned)std::max<int64_t>(blocks, 1));
+  if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16>, grid, dim3(256), 0, st, true, p);
+  return launch_ex(msda_finalize_kernel<T, 1>, grid, dim3(256), 0, st, true, p);
 }
 
 template <typename T, int OVEC, int DT>
@@ -193,15 +217,16 @@ template <typename T>
 cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
   const int64_t max_blocks = (int64_t)num_sms * 8;
+  // The backward runs right before: overlap its tail (the cast waits).
   if (vec_ok && n % V16 == 0) {
     const int64_t nvec = n / V16;
     const int64_t blocks = std::min<int64_t>(max_blocks, (nvec + 255) / 256);
-    msda_cast_kernel<T, V16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(src, dst, nvec);
-  } else {
-    const int64_t blocks = std::min<int64_t>(max_blocks, (n + 255) / 256);
-    msda_cast_kernel<T, 1><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, st>>>(src, dst, n);
+    return launch_ex(msda_cast_kernel<T, V16>, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256),
+                     0, st, true, src, dst, nvec);
   }
-  return cudaGetLastError();
+  const int64_t blocks = std::min<int64_t>(max_blocks, (n + 255) / 256);
+  return launch_ex(msda_cast_kernel<T, 1>, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256), 0,
+                   st, true, src, dst, n);
 }
 
 #endif  // MSDA_LAUNCH_IMPL
@@ -219,7 +244,7 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
 #ifdef MSDA_LAUNCH_IMPL
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
-  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, bool, cudaStream_t);  \
+  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, bool, bool, cudaStream_t); \
   template cudaError_t launch_count<T>(const OpParams&, int, cudaStream_t);                         \
   template cudaError_t launch_finalize<T>(const OpParams&, bool, int, cudaStream_t);              \
   template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
