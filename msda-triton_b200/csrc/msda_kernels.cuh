@@ -297,6 +297,30 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   for (int j = 0; j < CPL; ++j)
 #pragma unroll
     for (int e = 0; e < VEC / 2; ++e) g2[j][e] = f2_pack(g[j][2 * e], g[j][2 * e + 1]);
+  // fp32 reductions of 16-bit data: a lane's 8 channels are 32 bytes of
+  // fp32, and two `red.v4` per lane would put the lanes of one instruction
+  // in different 32-byte sectors. Reduce channel quads interleaved instead:
+  // in reduction k (0, 1) lane `sub` adds channels (k*LPR + sub)*4 .. +3, so
+  // neighbouring lanes fill one sector per instruction. gq holds grad_out in
+  // that order.
+  constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 &&
+                         (MODE == kCounted || (MODE == kScatter && sizeof(A) == 4));
+  float gq[QUADS ? CPL : 1][2][4];
+  if constexpr (QUADS) {
+    const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int ch = j * LPR * VEC + (k * LPR + sub) * 4;
+        if (ch < D) {
+          load_vec<T, 4>(gp + ch, gq[j][k]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) gq[j][k][e] = 0.f;
+        }
+      }
+  }
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -424,6 +448,22 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
 #pragma unroll
               for (int j = 0; j < CPL; ++j) {
                 const int ch = (j * LPR + sub) * VEC;
+                if constexpr (QUADS) {
+                  // fp32 reduction in interleaved quads (see gq); a
+                  // counted one-hit row is stored in the natural layout.
+                  const bool reduce = MODE != kCounted || hits[n][c] != 1u;
+                  if (reduce) {
+                    float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + bl[n].pix[c] * rs;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                      const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
+                      if (cq < D)
+                        red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
+                                           wc * gq[j][k][3], pol_keep);
+                    }
+                    continue;
+                  }
+                }
                 if (ch < D) {
                   float contrib[VEC];
                   if constexpr (VEC % 2 == 0) {
