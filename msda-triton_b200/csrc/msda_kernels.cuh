@@ -990,38 +990,28 @@ __device__ __forceinline__ int64_t dense_pixel(const LevelInfo* lv, int L, int64
   return 0;  // unreachable for r < dense pixels per batch
 }
 
-__device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelInfo* lv, int64_t tid,
-                                                 int64_t nthreads) {
+// One warp per dense pixel row (the M*D floats of all heads of one pixel):
+// flag its M counts and zero its fp32 accumulator.
+__device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelInfo* lv, int64_t warp,
+                                                 int64_t nwarps) {
   int64_t per_batch = 0;
   for (int l = 0; l < p.L; ++l)
     if (lv[l].dense) per_batch += (int64_t)lv[l].H * lv[l].W;
   if (per_batch == 0) return;
-  const int64_t pixels = p.B * per_batch;
-  for (int64_t u = tid; u < pixels * p.M; u += nthreads) {
-    const int64_t px = u / p.M;
-    const int m = (int)(u - px * p.M);
+  const int lane = threadIdx.x & 31;
+  const int64_t row_floats = (int64_t)p.M * p.D;
+  const bool vec = row_floats % 4 == 0 && (reinterpret_cast<uintptr_t>(p.acc) & 15) == 0;
+  for (int64_t px = warp; px < p.B * per_batch; px += nwarps) {
     const int64_t b = px / per_batch;
     const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
-    atomicOr(p.counts + (b * p.S + pix) * p.M + m, kDenseRow);
-  }
-  // A pixel's rows of all heads are contiguous: M*D floats.
-  const int64_t row_floats = (int64_t)p.M * p.D;
-  if (row_floats % 4 == 0 && (reinterpret_cast<uintptr_t>(p.acc) & 15) == 0) {
-    const int64_t q4 = row_floats / 4;
-    for (int64_t u = tid; u < pixels * q4; u += nthreads) {
-      const int64_t px = u / q4;
-      const int64_t k = u - px * q4;
-      const int64_t b = px / per_batch;
-      const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
-      reinterpret_cast<float4*>(p.acc + (b * p.S + pix) * row_floats)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  } else {
-    for (int64_t u = tid; u < pixels * row_floats; u += nthreads) {
-      const int64_t px = u / row_floats;
-      const int64_t k = u - px * row_floats;
-      const int64_t b = px / per_batch;
-      const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
-      p.acc[(b * p.S + pix) * row_floats + k] = 0.f;
+    const int64_t row0 = (b * p.S + pix) * p.M;  // first (b, pix, m) row
+    for (int m = lane; m < p.M; m += 32) atomicOr(p.counts + row0 + m, kDenseRow);
+    float* a = p.acc + row0 * p.D;
+    if (vec) {
+      for (int64_t k = lane; k < row_floats / 4; k += 32)
+        reinterpret_cast<float4*>(a)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      for (int64_t k = lane; k < row_floats; k += 32) a[k] = 0.f;
     }
   }
 }
@@ -1037,17 +1027,28 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   if (point) xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);  // in flight across the sync
   load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
   if (blockIdx.x >= point_blocks) {
-    count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * blockDim.x + threadIdx.x,
-                     (int64_t)(gridDim.x - point_blocks) * blockDim.x);
+    const int wpb = blockDim.x >> 5;
+    count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * wpb + (threadIdx.x >> 5),
+                     (int64_t)(gridDim.x - point_blocks) * wpb);
     return;
   }
   if (!point) return;
-  const int64_t qm = i / LK;
-  const int s = (int)(i - qm * LK);
+  int64_t qm, b;
+  int s, m;
+  if (p.BQM * LK <= 0xffffffffll) {  // 32-bit index arithmetic
+    const unsigned u = (unsigned)i, qmu = u / (unsigned)LK;
+    s = (int)(u - qmu * (unsigned)LK);
+    qm = qmu;
+    b = qmu / (unsigned)(p.Q * p.M);
+    m = (int)(qmu % (unsigned)p.M);
+  } else {
+    qm = i / LK;
+    s = (int)(i - qm * LK);
+    b = qm / (p.Q * p.M);
+    m = (int)(qm % p.M);
+  }
   const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
   if (L.dense) return;
-  const int64_t b = qm / (p.Q * p.M);
-  const int m = (int)(qm % p.M);
   const Bilinear bl = resolve(xy.x, xy.y, L);
   unsigned old[4];
   int64_t row[4];
