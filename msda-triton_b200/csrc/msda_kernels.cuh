@@ -248,14 +248,13 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   constexpr bool SCATTER = MODE != kNoScatter;
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
-  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
 
   constexpr int G = 32 / LPR;
   using Raw = typename Pack<T, VEC>::Raw;
   const int lane = threadIdx.x & 31;
   int64_t b, q;
   int m;
-  if (!query_block_of(p, WARPS, b, m, q)) return;
+  const bool live = query_block_of(p, WARPS, b, m, q);
   const int64_t qm = (b * p.Q + q) * p.M + m;
   const int grp = lane / LPR, sub = lane % LPR;
   const int D = p.D;
@@ -283,7 +282,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
       const int ch = (j * LPR + sub) * VEC;
-      if (ch < D) {
+      if (live && ch < D) {
         load_vec<T, VEC>(gp + ch, g[j]);
       } else {
 #pragma unroll
@@ -313,7 +312,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int ch = j * LPR * VEC + (k * LPR + sub) * 4;
-        if (ch < D) {
+        if (live && ch < D) {
           load_vec<T, 4>(gp + ch, gq[j][k]);
         } else {
 #pragma unroll
@@ -321,6 +320,22 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
         }
       }
   }
+
+  // The first NB points' (x, y, a) are in flight while the level table loads.
+  float2 pxy[NB];
+  float pat[NB];
+#pragma unroll
+  for (int n = 0; n < NB; ++n) {
+    const int s = n * G + grp;
+    pxy[n] = make_float2(0.f, 0.f);
+    pat[n] = 0.f;
+    if (live && s < LK) {
+      pxy[n] = load_pair(lp + 2 * s);
+      pat[n] = to_f32(ap[s]);
+    }
+  }
+  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
+  if (!live) return;
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -331,8 +346,12 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
     for (int n = 0; n < NB; ++n) {
       const int s = s0 + n * G + grp;
       if (s < LK) {
-        const float2 xy = load_pair(lp + 2 * s);
-        at[n] = to_f32(ap[s]);
+        float2 xy = pxy[n];
+        at[n] = pat[n];
+        if (s0 > 0) {
+          xy = load_pair(lp + 2 * s);
+          at[n] = to_f32(ap[s]);
+        }
         const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
         bl[n] = resolve(xy.x, xy.y, L);
         fw[n] = L.fW;
