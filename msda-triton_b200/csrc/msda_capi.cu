@@ -62,6 +62,11 @@ int check_shape(const Shape& s, int32_t dtype) {
   if (s.M < 1 || s.D < 1 || s.K < 1) return fail(MSDA_ERR_INVALID_ARGUMENT, "num_heads (%d), head_dim (%d) and num_points (%d) must be >= 1", s.M, s.D, s.K);
   if (s.L < 1 || s.L > msda::kMaxLevels) return fail(MSDA_ERR_UNSUPPORTED, "num_levels=%d outside [1, %d]", s.L, msda::kMaxLevels);
   if ((int64_t)s.L * s.K > 4096) return fail(MSDA_ERR_UNSUPPORTED, "num_levels*num_points=%lld exceeds 4096", (long long)s.L * s.K);
+  // The kernels address a (batch item, head) slice of value / grad_value with
+  // 32-bit offsets: S*M*D elements per batch item must stay below 2^31.
+  if (s.S * (int64_t)s.M * s.D >= (int64_t(1) << 31))
+    return fail(MSDA_ERR_UNSUPPORTED, "num_values*num_heads*head_dim=%lld per batch item exceeds 2^31 - 1",
+                (long long)(s.S * (int64_t)s.M * s.D));
   // Grid (ceil(Q / 8), M, B): y and z are limited to 65535.
   if (s.B > 65535 || s.M > 65535)
     return fail(MSDA_ERR_UNSUPPORTED, "batch (%lld) and num_heads (%d) must be <= 65535", (long long)s.B, s.M);

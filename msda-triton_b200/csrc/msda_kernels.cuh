@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpPara
   const int64_t qm = (b * p.Q + q) * p.M + m;
   const int grp = lane / LPR, sub = lane % LPR;
   const int D = p.D;
-  const int64_t rs = (int64_t)p.M * D;
+  const int rs = p.M * D;  // row stride; pix * rs < S*M*D < 2^31 (checked on the host)
   const T* vb = reinterpret_cast<const T*>(p.value) + (b * p.S * p.M + m) * D;
   const int LK = p.L * p.K;
   const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   const int64_t qm = (b * p.Q + q) * p.M + m;
   const int grp = lane / LPR, sub = lane % LPR;
   const int D = p.D;
-  const int64_t rs = (int64_t)p.M * D;
+  const int rs = p.M * D;  // row stride; pix * rs < S*M*D < 2^31 (checked on the host)
   const int64_t head_base = (b * p.S * p.M + m) * D;
   const T* vb = reinterpret_cast<const T*>(p.value) + head_base;
   A* gvb = reinterpret_cast<A*>(p.grad_value) + head_base;

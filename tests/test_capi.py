@@ -60,6 +60,9 @@ def test_abi_rejects_bad_arguments_before_any_device_work():
     assert _fwd(lib, S=(1 << 30) + 1) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert _fwd(lib, D=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert _fwd(lib, B=-1) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    # A batch item's value slice is addressed with 32-bit offsets.
+    assert _fwd(lib, S=1 << 28, M=8, D=1) == _lib.MSDA_ERR_UNSUPPORTED
+    assert b"2^31" in lib.msda_last_error()
     # Null pointers and misaligned sampling locations are caught on the host.
     assert _fwd(lib, value=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert b"null" in lib.msda_last_error()
