@@ -19,8 +19,8 @@ Reported (one JSON line on rank 0):
              every step, max over ranks.
   e2e        the same metric through the public op with pinned HOST buffers:
              every step copies its inputs host->device and the output and the
-             three gradients device->host inside the timed region (copies of
-             neighbouring steps overlap on two copy streams).
+             three gradients device->host inside the timed region (the next
+             step's uploads overlap this step's downloads on a copy stream).
   roofline   the backward call (the dominant launch sequence): algorithmic
              bytes / its CUDA-event time against the measured HBM copy
              bandwidth; `step` gives the same for forward + backward.
@@ -292,10 +292,12 @@ def e2e_leg(x, steps, warmup, fp32_acc):
     host->device, runs forward + backward through
     multi_scale_deformable_attention, and copies the output and the three
     gradients device->host. The steps are pipelined the way a data loader
-    would run them: the inputs of step i+1 go up on one copy stream and the
-    results of step i come down on another while step i computes (PCIe is
-    full duplex), with two device input buffers. Returns run(n) -> None,
-    which runs n such steps, and the bytes copied per step each way."""
+    would run them: the inputs of step i+1 go up on a copy stream while the
+    compute stream runs step i and copies its results down (PCIe is full
+    duplex), with two device input buffers. The results are copied on the
+    compute stream itself, so no tensor outlives its stream. Returns
+    run(n) -> None, which runs n such steps, and the bytes copied per step
+    each way."""
     keys = ("value", "sampling_locations", "attention_weights", "grad_output")
     host = {k: x[k].cpu().pin_memory() for k in keys}
     shapes, starts = x["spatial_shapes"], x["level_start_index"]
@@ -308,7 +310,7 @@ def e2e_leg(x, steps, warmup, fp32_acc):
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in (out_h, gv_h, gl_h, ga_h))
     compute = torch.cuda.current_stream()
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    s_in = torch.cuda.Stream()
     bufs = [{k: torch.empty_like(x[k]) for k in keys} for _ in range(2)]
 
     def run(n):
@@ -336,13 +338,8 @@ def e2e_leg(x, steps, warmup, fp32_acc):
             used[i % 2].record(compute)
             if i + 1 < n:
                 upload(i + 1)  # into the other buffer, once step i-1 is done with it
-            s_out.wait_stream(compute)
-            with torch.cuda.stream(s_out):
-                results = (out.detach(), v.grad, l.grad, a.grad)
-                for dst, src in zip((out_h, gv_h, gl_h, ga_h), results):
-                    dst.copy_(src, non_blocking=True)
-                    src.record_stream(s_out)
-        compute.wait_stream(s_out)
+            for dst, src in zip((out_h, gv_h, gl_h, ga_h), (out.detach(), v.grad, l.grad, a.grad)):
+                dst.copy_(src, non_blocking=True)
 
     run(warmup)
     torch.cuda.synchronize()
