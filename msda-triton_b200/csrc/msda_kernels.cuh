@@ -1090,7 +1090,7 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
 // one-hit rows were already stored by the backward.
 // One thread per 4 consecutive rows x VEC elements (one 16-byte count load).
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) msda_finalize_kernel(const OpParams p) {
+__global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p) {
   const int D = p.D;
   const int per_row = D / VEC;
   const int64_t rows = p.B * p.S * p.M;

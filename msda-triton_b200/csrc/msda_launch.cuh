@@ -164,11 +164,12 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
   const int64_t n = p.BQM * p.L * p.K;
   const int64_t point_blocks = (n + 255) / 256;
   // The dense rows are not known on the host (the level table is on the
-  // device): enough blocks for all of them, capped at two waves' worth.
-  // (One block per SM, which keeps the decoder's grid to one wave, measured
-  // 1-2 us slower end to end.)
-  const int64_t acc_vec4 = (p.B * p.S * p.M * p.D + 3) / 4;
-  const int64_t dense_blocks = std::max<int64_t>(1, std::min<int64_t>(2 * num_sms, (acc_vec4 + 255) / 256));
+  // device; one warp per dense pixel row, grid-stride): the blocks that the
+  // point blocks leave free in one wave, at least one per SM.
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, msda_count_kernel<T>, 256, 0) != cudaSuccess)
+    per_sm = 4;
+  const int64_t dense_blocks = std::max<int64_t>(num_sms, (int64_t)per_sm * num_sms - point_blocks);
   if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   msda_count_kernel<T><<<(unsigned)(point_blocks + dense_blocks), 256, 0, st>>>(p, (unsigned)point_blocks);
   return cudaGetLastError();
