@@ -112,6 +112,10 @@ constexpr double kOwnerMaxPointsPerRow = 0.0;
 // than once, and the plain fp32 scatter is cheaper.
 constexpr double kCountedMaxPointsPerRow = 2.0;
 
+// Sampling points per value row (per head) above which the scatter merges a
+// warp's same-row contributions before reducing them.
+constexpr double kMergeMinPointsPerRow = 2.0;
+
 enum class Algo { kScatterNative, kScatterF32, kCounted, kOwner };
 
 Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
@@ -360,7 +364,14 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count launch");
   }
-  const int mode = algo == Algo::kOwner ? msda::kNoScatter : counted ? msda::kCounted : msda::kScatter;
+  // Dense sampling (more points than value rows per head, e.g. an encoder's
+  // queries at every pixel) makes the points of one query share rows: merge
+  // them before the reductions. Sparse sampling rarely does.
+  const bool merge = (double)s.Q * s.L * s.K > kMergeMinPointsPerRow * (double)s.S;
+  const int mode = algo == Algo::kOwner ? msda::kNoScatter
+                   : counted            ? msda::kCounted
+                   : merge              ? msda::kScatterMerge
+                                        : msda::kScatter;
   switch (dtype) {
     case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, true, bwd_pdl, st); break;
     case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, fp32_ws, bwd_pdl, st); break;

@@ -226,6 +226,7 @@ enum ScatterMode : int {
   kNoScatter = 0,  // grad_value written by another kernel
   kScatter = 1,    // vector `red` into p.grad_value (type A), zero-filled beforehand
   kCounted = 2,    // hit-counted: one-hit rows stored, multi-hit rows reduced in fp32
+  kScatterMerge = 3,  // kScatter with same-row contributions of a warp merged first
 };
 
 // Hit-counted scatter: flag in a row's hit count marking a row of a dense
@@ -303,7 +304,12 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   // neighbouring lanes fill one sector per instruction. gq holds grad_out in
   // that order.
   constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 &&
-                         (MODE == kCounted || (MODE == kScatter && sizeof(A) == 4));
+                         (MODE == kCounted || (MODE != kNoScatter && sizeof(A) == 4));
+  // Same-row merging (see the scatter below): one corner item per lane needs
+  // the 4 corners of a group to fit in its LPR lanes, one point per group.
+  // It pays where a query's points share rows (dense, local sampling such as
+  // an encoder's) and costs where they do not, so the host selects it.
+  constexpr bool COMBINE = MODE == kScatterMerge && LPR >= 4 && NB == 1;
   float gq[QUADS ? CPL : 1][2][4];
   if constexpr (QUADS) {
     const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
@@ -394,7 +400,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
       for (int c = 0; c < 4; ++c) {
         hits[n][c] = 0u;
         // Dense-level rows are always reduced in fp32: no count to read.
-        if constexpr (MODE == kCounted)
+        if constexpr (MODE == kCounted && !COMBINE)
           if ((bl[n].valid >> c) & 1u)
             hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
       }
@@ -454,61 +460,105 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
         gy += __shfl_xor_sync(kFullMask, gy, off);
       }
       const int s = s0 + n * G + grp;
-      if (s < LK) {
-        if (sub == 0) {
-          store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
-          gap[s] = from_f32<T>(ga);
-        }
-        if constexpr (SCATTER) {
+      if (s < LK && sub == 0) {
+        store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
+        gap[s] = from_f32<T>(ga);
+      }
+      if constexpr (SCATTER) {
+        // Writes this lane's channels of a * w * grad_out into row `pix`
+        // (weight wc; `hits` is the row's count in the counted mode).
+        auto scatter_row = [&](int pix, float wc, unsigned hits) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            if ((bl[n].valid >> c) & 1u) {
-              const float wc = at[n] * bl[n].w[c];
+          for (int j = 0; j < CPL; ++j) {
+            const int ch = (j * LPR + sub) * VEC;
+            if constexpr (QUADS) {
+              // fp32 reduction in interleaved quads (see gq); a counted
+              // one-hit row is stored in the natural layout.
+              if (MODE != kCounted || hits != 1u) {
+                float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + pix * rs;
 #pragma unroll
-              for (int j = 0; j < CPL; ++j) {
-                const int ch = (j * LPR + sub) * VEC;
-                if constexpr (QUADS) {
-                  // fp32 reduction in interleaved quads (see gq); a
-                  // counted one-hit row is stored in the natural layout.
-                  const bool reduce = MODE != kCounted || hits[n][c] != 1u;
-                  if (reduce) {
-                    float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + bl[n].pix[c] * rs;
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
-                      const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
-                      if (cq < D)
-                        red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
-                                           wc * gq[j][k][3], pol_keep);
-                    }
-                    continue;
-                  }
+                for (int k = 0; k < 2; ++k) {
+                  const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
+                  if (cq < D)
+                    red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
+                                       wc * gq[j][k][3], pol_keep);
                 }
-                if (ch < D) {
-                  float contrib[VEC];
-                  if constexpr (VEC % 2 == 0) {
-                    const uint64_t wc2 = f2_pack(wc, wc);
+                continue;
+              }
+            }
+            if (ch < D) {
+              float contrib[VEC];
+              if constexpr (VEC % 2 == 0) {
+                const uint64_t wc2 = f2_pack(wc, wc);
 #pragma unroll
-                    for (int e = 0; e < VEC / 2; ++e)
-                      f2_unpack(f2_mul(wc2, g2[j][e]), contrib[2 * e], contrib[2 * e + 1]);
-                  } else {
+                for (int e = 0; e < VEC / 2; ++e)
+                  f2_unpack(f2_mul(wc2, g2[j][e]), contrib[2 * e], contrib[2 * e + 1]);
+              } else {
 #pragma unroll
-                    for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
-                  }
-                  if constexpr (MODE == kCounted) {
-                    // A row with one hit gets its only contribution stored
-                    // (rounded once, as fp32 accumulation would); rows with
-                    // more hits accumulate in fp32.
-                    if (hits[n][c] == 1u)
-                      store_vec<T, VEC>(reinterpret_cast<T*>(gvb) + bl[n].pix[c] * rs + ch, contrib);
-                    else
-                      red_add_vec_hint<float, VEC>(accb + bl[n].pix[c] * rs + ch, contrib, pol_keep);
-                  } else {
-                    red_add_vec_hint<A, VEC>(gvb + bl[n].pix[c] * rs + ch, contrib, pol_keep);
-                  }
-                }
+                for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
+              }
+              if constexpr (MODE == kCounted) {
+                // A row with one hit gets its only contribution stored
+                // (rounded once, as fp32 accumulation would); rows with
+                // more hits accumulate in fp32.
+                if (hits == 1u)
+                  store_vec<T, VEC>(reinterpret_cast<T*>(gvb) + pix * rs + ch, contrib);
+                else
+                  red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
+              } else {
+                red_add_vec_hint<A, VEC>(gvb + pix * rs + ch, contrib, pol_keep);
               }
             }
           }
+        };
+        if constexpr (COMBINE) {
+          // Same-row merging. Every contribution of this query is a multiple
+          // of the same grad_out vector, so corners of the warp's points that
+          // land on one row need one write of (sum of their weights) *
+          // grad_out. Lane `sub` < 4 of a group holds corner `sub` of the
+          // group's point as an item (row, weight); lanes with equal rows
+          // find each other with a match, the lowest one leads and owns the
+          // summed weight (added in lane order: deterministic).
+          const int cs = sub & 3;
+          const unsigned vbit = (bl[n].valid >> cs) & 1u;
+          const bool have = s < LK && sub < 4 && vbit != 0u;
+          const int pix_s = cs == 0 ? bl[n].pix[0] : cs == 1 ? bl[n].pix[1] : cs == 2 ? bl[n].pix[2] : bl[n].pix[3];
+          const float w_s = cs == 0 ? bl[n].w[0] : cs == 1 ? bl[n].w[1] : cs == 2 ? bl[n].w[2] : bl[n].w[3];
+          const int key = have ? pix_s : -1 - lane;  // rows are >= 0; empty items never match
+          const float wt = have ? at[n] * w_s : 0.f;
+          const unsigned same = __match_any_sync(kFullMask, key);
+          float wsum = wt;
+          if (__any_sync(kFullMask, __popc(same) > 1)) {
+            wsum = 0.f;
+            unsigned rest = same;
+            const int rounds = __reduce_max_sync(kFullMask, (unsigned)__popc(same));
+            for (int r = 0; r < rounds; ++r) {
+              const int src = rest ? __ffs(rest) - 1 : lane;
+              const float v = __shfl_sync(kFullMask, wt, src);
+              if (rest) {
+                wsum += v;
+                rest &= rest - 1;
+              }
+            }
+          }
+          const int lead = have && __ffs(same) - 1 == lane;
+          unsigned hits_me = 0u;
+          if constexpr (MODE == kCounted)
+            if (lead) hits_me = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)key * p.M);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int src = grp * LPR + c;
+            const int lead_c = __shfl_sync(kFullMask, lead, src);
+            const int pix_c = __shfl_sync(kFullMask, key, src);
+            const float w_c = __shfl_sync(kFullMask, wsum, src);
+            unsigned hits_c = 0u;
+            if constexpr (MODE == kCounted) hits_c = __shfl_sync(kFullMask, hits_me, src);
+            if (lead_c) scatter_row(pix_c, w_c, hits_c);
+          }
+        } else if (s < LK) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if ((bl[n].valid >> c) & 1u) scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c]);
         }
       }
     }

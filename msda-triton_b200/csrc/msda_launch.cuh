@@ -44,7 +44,8 @@ constexpr int kWarpsPerCta = 8;
 template <typename T>
 cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
 // Backward over sampling points: grad_loc / grad_attn, plus the grad_value
-// handling `mode` (ScatterMode): kScatter adds with vector `red` into
+// handling `mode` (ScatterMode): kScatter (kScatterMerge: after merging a
+// warp's same-row contributions; vector path only) adds with vector `red` into
 // p.grad_value (fp32 when fp32_scatter, else the value dtype); kCounted stores
 // one-hit rows and reduces multi-hit rows into p.acc (needs the counts).
 // `pdl`: the kernel before this one in the stream is our zero-fill or hit
@@ -150,9 +151,11 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32
     if (c.vec == V16) return bwd_by_shape<T, T, V16, kCounted>(p, c, pdl, st);
     if (c.vec == 1) return bwd_by_shape<T, T, 1, kCounted>(p, c, pdl, st);
   } else if (fp32_scatter || sizeof(T) == 4) {
+    if (c.vec == V16 && mode == kScatterMerge) return bwd_by_shape<T, float, V16, kScatterMerge>(p, c, pdl, st);
     if (c.vec == V16) return bwd_by_shape<T, float, V16, kScatter>(p, c, pdl, st);
     if (c.vec == 1) return bwd_by_shape<T, float, 1, kScatter>(p, c, pdl, st);
   } else {
+    if (c.vec == V16 && mode == kScatterMerge) return bwd_by_shape<T, T, V16, kScatterMerge>(p, c, pdl, st);
     if (c.vec == V16) return bwd_by_shape<T, T, V16, kScatter>(p, c, pdl, st);
     if (c.vec == 1) return bwd_by_shape<T, T, 1, kScatter>(p, c, pdl, st);
   }

@@ -425,6 +425,10 @@ ALGO_CASES = [
     ("odd_d", dict(B=2, Q=9, M=3, D=5, K=2, shapes=[(7, 9), (4, 5)]), -0.2, 1.2),
     ("d128", dict(B=1, Q=40, M=2, D=128, K=4, shapes=[(20, 30), (10, 15)]), 0.0, 1.0),
     ("one_pixel_levels", dict(B=2, Q=50, M=2, D=32, K=4, shapes=[(1, 1), (2, 1), (1, 3)]), -0.3, 1.3),
+    # Dense sampling clustered in a few rows (Q*L*K > 2*S): the scatter merges
+    # a warp's same-row contributions before reducing them.
+    ("dense_local", dict(B=2, Q=64, M=4, D=32, K=4, shapes=[(8, 8), (4, 4)]), 0.45, 0.55),
+    ("dense_local_d64", dict(B=1, Q=96, M=2, D=64, K=4, shapes=[(6, 10), (3, 5)]), 0.4, 0.6),
 ]
 
 
