@@ -121,6 +121,35 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// Mixed-precision FMA (sm_100): c + a*b for the low or high 16-bit halves
+// of two words, a and b both bf16 (or both fp16), accumulated in fp32. The
+// product of two 16-bit floats is exact in fp32, so this equals converting
+// both to fp32 first.
+__device__ __forceinline__ float fma_lo16(unsigned a, unsigned b, float c, const __nv_bfloat16*) {
+  float d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %3;\n\t}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_hi16(unsigned a, unsigned b, float c, const __nv_bfloat16*) {
+  float d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, ah, bh, %3;\n\t}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_lo16(unsigned a, unsigned b, float c, const __half*) {
+  float d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.f16 %0, al, bl, %3;\n\t}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fma_hi16(unsigned a, unsigned b, float c, const __half*) {
+  float d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.f16 %0, ah, bh, %3;\n\t}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
+  return d;
+}
+
 // A 32-bit word holding two 16-bit values -> packed fp32 pair.
 __device__ __forceinline__ uint64_t word_to_f2(unsigned w, const __nv_bfloat16*) {
   uint64_t r;  // bf16 is the upper half of fp32: shift / mask, no conversion
