@@ -331,7 +331,8 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
       }
   }
 
-  // The first NB points' (x, y, a) are in flight while the level table loads.
+  // The first NB points' (x, y, a) are in flight while the level table loads;
+  // every iteration then loads the next one's while its gathers are in flight.
   float2 pxy[NB];
   float pat[NB];
 #pragma unroll
@@ -356,12 +357,8 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
     for (int n = 0; n < NB; ++n) {
       const int s = s0 + n * G + grp;
       if (s < LK) {
-        float2 xy = pxy[n];
+        const float2 xy = pxy[n];  // loaded one iteration ahead
         at[n] = pat[n];
-        if (s0 > 0) {
-          xy = load_pair(lp + 2 * s);
-          at[n] = to_f32(ap[s]);
-        }
         const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
         bl[n] = resolve(xy.x, xy.y, L);
         fw[n] = L.fW;
@@ -395,6 +392,15 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
           raw[n][c][j] = r;
         }
 
+    // The next iteration's (x, y, a), in flight with this iteration's gathers.
+#pragma unroll
+    for (int n = 0; n < NB; ++n) {
+      const int sn = s0 + G * NB + n * G + grp;
+      if (sn < LK) {
+        pxy[n] = load_pair(lp + 2 * sn);
+        pat[n] = to_f32(ap[sn]);
+      }
+    }
     // The value gathers above need nothing from the kernel before this one
     // (the zero-fill or the hit count); the counts and the reduction target do.
     if constexpr (SCATTER) pdl_wait();
