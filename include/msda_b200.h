@@ -103,6 +103,45 @@ MSDA_API int msda_forward(const void* value, const int64_t* spatial_shapes, cons
                  void* stream);
 
 /*
+ * Forward with the layer's prologue fused in (no counterpart in the
+ * reference op; it replaces the prologue of the reference's Deformable-DETR
+ * layer, labs/solutions/lab00.py:199-208, followed by msda_forward): instead
+ * of sampling locations and attention weights it takes
+ *   reference_points  (B, Q, 2)          normalised (x, y) per query,
+ *   sampling_offsets  (B, Q, M, L, K, 2) in pixels of each level,
+ *   attention_logits  (B, Q, M, L, K),
+ * and samples point (l, k) of head m at reference + offset / (W_l, H_l) with
+ * weight softmax over the head's L*K logits -- the same maths as
+ * msda_forward on the materialised locations and weights, without writing
+ * or reading them. All in `dtype`.
+ */
+MSDA_API int msda_forward_fused(const void* value, const int64_t* spatial_shapes,
+                                const int64_t* level_start_index, const void* reference_points,
+                                const void* sampling_offsets, const void* attention_logits,
+                                void* output, int64_t batch, int64_t num_values,
+                                int64_t num_queries, int32_t num_heads, int32_t head_dim,
+                                int32_t num_levels, int32_t num_points, int32_t dtype,
+                                void* stream);
+
+/*
+ * Backward of msda_forward_fused: grad_value (B,S,M,D), the gradient of the
+ * sampling offsets (B,Q,M,L,K,2) and of the attention logits (B,Q,M,L,K)
+ * (through the softmax), in `dtype`. The reference points' gradient is the
+ * offsets' gradient times (W_l, H_l), summed over (m, l, k); the caller forms
+ * it. Workspace and flags as msda_backward (same workspace size);
+ * MSDA_BWD_FORCE_OWNER is not supported here.
+ */
+MSDA_API int msda_backward_fused(const void* value, const int64_t* spatial_shapes,
+                                 const int64_t* level_start_index, const void* reference_points,
+                                 const void* sampling_offsets, const void* attention_logits,
+                                 const void* grad_output, void* grad_value,
+                                 void* grad_sampling_offsets, void* grad_attention_logits,
+                                 void* workspace, size_t workspace_bytes, int64_t batch,
+                                 int64_t num_values, int64_t num_queries, int32_t num_heads,
+                                 int32_t head_dim, int32_t num_levels, int32_t num_points,
+                                 int32_t dtype, uint32_t flags, void* stream);
+
+/*
  * Bytes of fp32 workspace msda_backward needs for these sizes and flags
  * (0 when the chosen algorithm uses none). Replaces the allocation of the
  * fp32 grad_value buffer at src/msda_triton/ops.py:76-77.

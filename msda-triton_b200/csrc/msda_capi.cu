@@ -201,22 +201,29 @@ const char* msda_version(void) { return "msda_b200 0.1.0 sm_100a"; }
 
 const char* msda_last_error(void) { return g_last_error.c_str(); }
 
-int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
-                 const void* sampling_locations, const void* attention_weights, void* output,
-                 int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
-                 int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
-                 void* stream) {
-  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+// The forward behind msda_forward and msda_forward_fused. Fused: `loc` holds
+// sampling offsets in level pixels, `attn` attention logits, `ref` the
+// reference points.
+static int forward_impl(const char* fn, const void* value, const int64_t* spatial_shapes,
+                        const int64_t* level_start_index, const void* ref, const void* loc,
+                        const void* attn, void* output, bool fused, const Shape& s, int32_t dtype,
+                        void* stream) {
+  const void* sampling_locations = loc;
+  const void* attention_weights = attn;
   if (int rc = check_shape(s, dtype)) return rc;
   if (s.B == 0 || s.Q == 0) return succeed();
-  if (!value || !spatial_shapes || !level_start_index || !sampling_locations || !attention_weights || !output)
-    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_forward: null pointer argument");
+  if (!value || !spatial_shapes || !level_start_index || !sampling_locations || !attention_weights ||
+      !output || (fused && !ref))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   const int es = elem_size(dtype);
   if (!aligned(sampling_locations, 2 * es) || !aligned(value, es) || !aligned(output, es) ||
-      !aligned(attention_weights, es) || !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8))
-    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_forward: misaligned buffer (sampling_locations needs %d-byte alignment)", 2 * es);
+      !aligned(attention_weights, es) || !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8) ||
+      (fused && !aligned(ref, 2 * es)))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer (sampling_locations / offsets and reference points need %d-byte alignment)", fn, 2 * es);
   msda::Cfg cfg;
   if (int rc = choose_cfg(s.D, es, aligned(value, 16) && aligned(output, 16), &cfg)) return rc;
+  if (fused && cfg.vec != 16 / es)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: the fused prologue needs 16-byte aligned buffers and head_dim a multiple of %d", fn, 16 / es);
   {
     const int64_t ctas = (s.Q + msda::kWarpsPerCta - 1) / msda::kWarpsPerCta * s.M * s.B;
     cfg.short_grid = ctas <= (int64_t)msda::kShortGridWaves * 4 * sm_count();
@@ -228,6 +235,8 @@ int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t
   p.starts = level_start_index;
   p.loc = sampling_locations;
   p.attn = attention_weights;
+  p.ref = ref;
+  p.fused = fused ? 1 : 0;
   p.out = output;
   p.B = s.B; p.S = s.S; p.Q = s.Q;
   p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
@@ -240,8 +249,30 @@ int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t
     case MSDA_DTYPE_F16: e = msda::launch_forward<__half>(p, cfg, st); break;
     default: e = msda::launch_forward<__nv_bfloat16>(p, cfg, st); break;
   }
-  if (e != cudaSuccess) return cuda_fail(e, "msda_forward launch");
+  if (e != cudaSuccess) return cuda_fail(e, "forward launch");
   return succeed();
+}
+
+int msda_forward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                 const void* sampling_locations, const void* attention_weights, void* output,
+                 int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                 int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                 void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  return forward_impl("msda_forward", value, spatial_shapes, level_start_index, nullptr,
+                      sampling_locations, attention_weights, output, false, s, dtype, stream);
+}
+
+int msda_forward_fused(const void* value, const int64_t* spatial_shapes,
+                       const int64_t* level_start_index, const void* reference_points,
+                       const void* sampling_offsets, const void* attention_logits, void* output,
+                       int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                       int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                       void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  return forward_impl("msda_forward_fused", value, spatial_shapes, level_start_index,
+                      reference_points, sampling_offsets, attention_logits, output, true, s, dtype,
+                      stream);
 }
 
 static bool owner_possible(const Shape& s, int es, msda::OwnerPlan* plan) {
@@ -268,19 +299,21 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
   return (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim * sizeof(float);
 }
 
-int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
-                  const void* sampling_locations, const void* attention_weights,
-                  const void* grad_output, void* grad_value, void* grad_sampling_locations,
-                  void* grad_attention_weights, void* workspace, size_t workspace_bytes,
-                  int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
-                  int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
-                  uint32_t flags, void* stream) {
-  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+// The backward behind msda_backward and msda_backward_fused (fused: offsets
+// and logits in, their gradients out; the owner algorithm is not offered).
+static int backward_impl(const char* fn, const void* value, const int64_t* spatial_shapes,
+                         const int64_t* level_start_index, const void* ref,
+                         const void* sampling_locations, const void* attention_weights,
+                         const void* grad_output, void* grad_value, void* grad_sampling_locations,
+                         void* grad_attention_weights, void* workspace, size_t workspace_bytes,
+                         bool fused, const Shape& s, int32_t dtype, uint32_t flags, void* stream) {
   if (int rc = check_shape(s, dtype)) return rc;
+  if (fused && (flags & MSDA_BWD_FORCE_OWNER))
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: the owner algorithm does not take the fused prologue", fn);
   if (s.B == 0) return succeed();
   const int es = elem_size(dtype);
   const size_t gv_bytes = (size_t)s.B * s.S * s.M * s.D * es;
-  if (!grad_value) return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: null grad_value");
+  if (!grad_value) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null grad_value", fn);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (s.Q == 0) {
     cudaError_t e = cudaMemsetAsync(grad_value, 0, gv_bytes, st);
@@ -288,26 +321,25 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
     return succeed();
   }
   if (!value || !spatial_shapes || !level_start_index || !sampling_locations || !attention_weights ||
-      !grad_output || !grad_sampling_locations || !grad_attention_weights)
-    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: null pointer argument");
+      !grad_output || !grad_sampling_locations || !grad_attention_weights || (fused && !ref))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   if (!aligned(sampling_locations, 2 * es) || !aligned(grad_sampling_locations, 2 * es) ||
       !aligned(value, es) || !aligned(grad_value, es) || !aligned(grad_output, es) ||
       !aligned(attention_weights, es) || !aligned(grad_attention_weights, es) ||
-      !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8))
-    return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: misaligned buffer (locations need %d-byte alignment)", 2 * es);
+      !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8) || (fused && !aligned(ref, 2 * es)))
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer (locations / offsets and reference points need %d-byte alignment)", fn, 2 * es);
 
   msda::OwnerPlan plan;
-  const bool owner_ok = owner_possible(s, es, &plan);
+  const bool owner_ok = !fused && owner_possible(s, es, &plan);
   const Algo algo = choose_algo(s, dtype, flags, owner_ok);
   const bool fp32_ws = algo == Algo::kScatterF32;
   const bool counted = algo == Algo::kCounted;
-  const size_t ws_need = msda_backward_workspace_size(batch, num_values, num_queries, num_heads,
-                                                      head_dim, num_levels, num_points, dtype, flags);
+  const size_t ws_need = msda_backward_workspace_size(s.B, s.S, s.Q, s.M, s.D, s.L, s.K, dtype, flags);
   if (fp32_ws || counted) {
     if (!workspace || workspace_bytes < ws_need)
-      return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: fp32 accumulation needs a workspace of %zu bytes (got %zu)", ws_need, workspace_bytes);
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: fp32 accumulation needs a workspace of %zu bytes (got %zu)", fn, ws_need, workspace_bytes);
     if (!aligned(workspace, 16))
-      return fail(MSDA_ERR_INVALID_ARGUMENT, "msda_backward: workspace must be 16-byte aligned");
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
   }
   void* target = fp32_ws ? workspace : grad_value;
   msda::Cfg cfg;
@@ -315,6 +347,8 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
                       (algo == Algo::kOwner || aligned(target, 16)) &&
                       (!counted || aligned(grad_value, 16));
   if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
+  if (fused && cfg.vec != 16 / es)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: the fused prologue needs 16-byte aligned buffers and head_dim a multiple of %d", fn, 16 / es);
 
   cudaError_t e;
   size_t acc_off = 0;
@@ -343,6 +377,8 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
   p.starts = level_start_index;
   p.loc = sampling_locations;
   p.attn = attention_weights;
+  p.ref = ref;
+  p.fused = fused ? 1 : 0;
   p.grad_out = grad_output;
   p.grad_value = (algo == Algo::kOwner || counted) ? grad_value : target;
   p.grad_loc = grad_sampling_locations;
@@ -407,6 +443,35 @@ int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward downcast launch");
   }
   return succeed();
+}
+
+int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                  const void* sampling_locations, const void* attention_weights,
+                  const void* grad_output, void* grad_value, void* grad_sampling_locations,
+                  void* grad_attention_weights, void* workspace, size_t workspace_bytes,
+                  int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                  int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                  uint32_t flags, void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  return backward_impl("msda_backward", value, spatial_shapes, level_start_index, nullptr,
+                       sampling_locations, attention_weights, grad_output, grad_value,
+                       grad_sampling_locations, grad_attention_weights, workspace, workspace_bytes,
+                       false, s, dtype, flags, stream);
+}
+
+int msda_backward_fused(const void* value, const int64_t* spatial_shapes,
+                        const int64_t* level_start_index, const void* reference_points,
+                        const void* sampling_offsets, const void* attention_logits,
+                        const void* grad_output, void* grad_value, void* grad_sampling_offsets,
+                        void* grad_attention_logits, void* workspace, size_t workspace_bytes,
+                        int64_t batch, int64_t num_values, int64_t num_queries, int32_t num_heads,
+                        int32_t head_dim, int32_t num_levels, int32_t num_points, int32_t dtype,
+                        uint32_t flags, void* stream) {
+  const Shape s{batch, num_values, num_queries, num_heads, head_dim, num_levels, num_points};
+  return backward_impl("msda_backward_fused", value, spatial_shapes, level_start_index,
+                       reference_points, sampling_offsets, attention_logits, grad_output, grad_value,
+                       grad_sampling_offsets, grad_attention_logits, workspace, workspace_bytes, true,
+                       s, dtype, flags, stream);
 }
 
 }  // extern "C"

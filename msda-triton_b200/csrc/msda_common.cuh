@@ -400,10 +400,10 @@ __device__ __forceinline__ Bilinear empty_slot() {
 // location then lands fully outside the level instead of overflowing the
 // int cast); inside that range the clamp is the identity, so every in-bounds
 // result equals the unclamped formula of src/msda_triton/kernels.py:112-128.
-__device__ __forceinline__ Bilinear resolve(float locx, float locy, const LevelInfo& L) {
+// resolve_px takes pixel coordinates x = loc_x * W - 0.5 (or, for the fused
+// prologue, ref_x * W + offset_x - 0.5: the same point without forming loc).
+__device__ __forceinline__ Bilinear resolve_px(float x, float y, const LevelInfo& L) {
   Bilinear r;
-  float x = fmaf(locx, L.fW, -0.5f);
-  float y = fmaf(locy, L.fH, -0.5f);
   x = fminf(fmaxf(x, -2.0f), L.fW + 1.0f);
   y = fminf(fmaxf(y, -2.0f), L.fH + 1.0f);
   const float x0f = floorf(x), y0f = floorf(y);
@@ -427,6 +427,44 @@ __device__ __forceinline__ Bilinear resolve(float locx, float locy, const LevelI
   r.w[2] = (1.0f - lx) * ly;
   r.w[3] = lx * ly;
   return r;
+}
+
+__device__ __forceinline__ Bilinear resolve(float locx, float locy, const LevelInfo& L) {
+  return resolve_px(fmaf(locx, L.fW, -0.5f), fmaf(locy, L.fH, -0.5f), L);
+}
+
+// Fused prologue: the pixel coordinates of reference point + offset (offsets
+// in level pixels, Deformable-DETR style) on level L.
+__device__ __forceinline__ Bilinear resolve_fused(float2 ref, float2 off, const LevelInfo& L) {
+  return resolve_px(fmaf(ref.x, L.fW, off.x - 0.5f), fmaf(ref.y, L.fH, off.y - 0.5f), L);
+}
+
+// Softmax statistics of n logits spread over a warp (lane i holds
+// p[i], p[i + 32], ...): the maximum and 1 / sum(exp(v - max)), reduced with
+// shuffles (every lane returns the same pair).
+template <typename T>
+__device__ __forceinline__ void warp_softmax_stats(const T* __restrict__ p, int n, int lane, float& mx,
+                                                   float& inv_sum) {
+  float m = -3.402823466e38f, sum = 0.f;
+  for (int i = lane; i < n; i += 32) {  // online: rescale the running sum when the max grows
+    const float v = to_f32(p[i]);
+    if (v > m) {
+      sum = sum * expf(m - v) + 1.f;
+      m = v;
+    } else {
+      sum += expf(v - m);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+    const float s2 = __shfl_xor_sync(0xffffffffu, sum, off);
+    const float mm = fmaxf(m, m2);
+    sum = sum * expf(m - mm) + s2 * expf(m2 - mm);
+    m = mm;
+  }
+  mx = m;
+  inv_sum = 1.f / sum;
 }
 
 }  // namespace msda

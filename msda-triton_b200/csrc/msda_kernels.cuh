@@ -38,6 +38,12 @@ struct OpParams {
   void* grad_attn;
   unsigned* counts;   // counted scatter: bilinear hits per (b, pixel, m) row
   float* acc;         // counted scatter: fp32 rows of the multi-hit rows
+  // Fused prologue (fused != 0): `loc` holds sampling offsets in level
+  // pixels, `attn` attention logits (softmaxed over a query-head's L*K
+  // points), `ref` reference points (B, Q, 2); the sampling location of a
+  // point is ref + offset / (W_l, H_l).
+  const void* ref;
+  int fused;
   int64_t B, S, Q;
   int M, D, L, K;
   int kshift;  // log2(K) when K is a power of two, else -1
@@ -68,7 +74,8 @@ __device__ __forceinline__ bool query_block_of(const OpParams& p, int warps, int
 // the register budget to the compiler). A grid of a few waves runs faster
 // with fewer, register-richer warps per SM (MINB = 3); a long grid needs the
 // occupancy of the compiler's default.
-template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB, int MINB>
+// FUSED: the layer's prologue runs here (OpParams::ref / fused).
+template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB, int MINB, bool FUSED = false>
 __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpParams p) {
   __shared__ LevelInfo lv[kMaxLevels];
   load_levels(p.shapes, p.starts, p.L, p.S, lv);
@@ -87,6 +94,13 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpPara
   const int LK = p.L * p.K;
   const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
   const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
+  // Fused prologue: this query's reference point and its head's softmax.
+  float2 refp = make_float2(0.f, 0.f);
+  float smx = 0.f, sinv = 1.f;
+  if constexpr (FUSED) {
+    refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
+    warp_softmax_stats(ap, LK, lane, smx, sinv);
+  }
 
   // Packed-pair accumulators (f32x2 FMA) on the vector path, scalars otherwise.
   constexpr bool kPairs = VEC >= 2 && VEC % 2 == 0;
@@ -109,8 +123,15 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpPara
       const int s = s0 + n * G + grp;
       if (s < LK) {
         const float2 xy = load_pair(lp + 2 * s);
-        at[n] = to_f32(ap[s]);
-        bl[n] = resolve(xy.x, xy.y, lv[level_of(s, p.K, p.kshift)]);
+        const float a = to_f32(ap[s]);
+        const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
+        if constexpr (FUSED) {
+          at[n] = expf(a - smx) * sinv;
+          bl[n] = resolve_fused(refp, xy, L);
+        } else {
+          at[n] = a;
+          bl[n] = resolve(xy.x, xy.y, L);
+        }
       } else {
         at[n] = 0.f;
         bl[n] = empty_slot();
@@ -233,6 +254,11 @@ enum ScatterMode : int {
 // level (accumulated in fp32 whatever its count).
 constexpr unsigned kDenseRow = 0x80000000u;
 
+// Fused prologue: points per query-head whose attention-weight gradients the
+// backward keeps in fp32 shared memory for the softmax backward (beyond that
+// they take a round trip through the logits' gradient buffer).
+constexpr int kFusedMaxLK = 128;
+
 // Minimum resident CTAs per SM the backward is compiled for (register cap).
 // The hit-counted mode measured faster at 3 (80 registers), the plain
 // scatter modes at 4 (64 registers).
@@ -243,12 +269,13 @@ constexpr unsigned kDenseRow = 0x80000000u;
 #define MSDA_BWD_COUNTED_MIN_BLOCKS 3
 #endif
 
-template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE>
+template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE, bool FUSED = false>
 __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS)
     msda_bwd_kernel(const OpParams p) {
   constexpr bool SCATTER = MODE != kNoScatter;
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
+  __shared__ float fused_ga[FUSED ? WARPS : 1][FUSED ? kFusedMaxLK : 1];  // fused: dL/da per point
 
   constexpr int G = 32 / LPR;
   using Raw = typename Pack<T, VEC>::Raw;
@@ -347,6 +374,14 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   }
   load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
   if (!live) return;
+  // Fused prologue: this query's reference point and its head's softmax;
+  // sdot accumulates sum_s a_s * dL/da_s for the softmax backward.
+  float2 refp = make_float2(0.f, 0.f);
+  float smx = 0.f, sinv = 1.f, sdot = 0.f;
+  if constexpr (FUSED) {
+    refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
+    warp_softmax_stats(ap, LK, lane, smx, sinv);
+  }
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -358,9 +393,14 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
       const int s = s0 + n * G + grp;
       if (s < LK) {
         const float2 xy = pxy[n];  // loaded one iteration ahead
-        at[n] = pat[n];
         const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
-        bl[n] = resolve(xy.x, xy.y, L);
+        if constexpr (FUSED) {
+          at[n] = expf(pat[n] - smx) * sinv;
+          bl[n] = resolve_fused(refp, xy, L);
+        } else {
+          at[n] = pat[n];
+          bl[n] = resolve(xy.x, xy.y, L);
+        }
         fw[n] = L.fW;
         fh[n] = L.fH;
         dense[n] = L.dense;
@@ -489,8 +529,19 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
       }
       const int s = s0 + n * G + grp;
       if (s < LK && sub == 0) {
-        store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
-        gap[s] = from_f32<T>(ga);
+        if constexpr (FUSED) {
+          // d/d offset = d/d pixel coordinate; dL/da kept (fp32 in shared
+          // memory when it fits) for the softmax pass.
+          store_pair(glp + 2 * s, at[n] * gx, at[n] * gy);
+          sdot = fmaf(at[n], ga, sdot);
+          if (LK <= kFusedMaxLK)
+            fused_ga[threadIdx.x >> 5][s] = ga;
+          else
+            gap[s] = from_f32<T>(ga);
+        } else {
+          store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
+          gap[s] = from_f32<T>(ga);
+        }
       }
       if constexpr (SCATTER) {
         // Writes this lane's channels of a * w * grad_out into row `pix`
@@ -589,6 +640,19 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
             if ((bl[n].valid >> c) & 1u) scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c]);
         }
       }
+    }
+  }
+  if constexpr (FUSED) {
+    // Softmax backward over the query-head's L*K points:
+    //   dL/dlogit_s = a_s * (dL/da_s - sum_t a_t * dL/da_t),
+    // dL/da_s as written above by this warp's lanes.
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(kFullMask, sdot, off);
+    __syncwarp();
+    for (int s = lane; s < LK; s += 32) {
+      const float a = expf(to_f32(ap[s]) - smx) * sinv;
+      const float ga = LK <= kFusedMaxLK ? fused_ga[threadIdx.x >> 5][s] : to_f32(gap[s]);
+      gap[s] = from_f32<T>(a * (ga - sdot));
     }
   }
 }
@@ -1113,7 +1177,7 @@ __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelI
   }
 }
 
-template <typename T>
+template <typename T, bool FUSED = false>
 __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsigned point_blocks) {
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
@@ -1146,7 +1210,13 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   }
   const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
   if (L.dense) return;
-  const Bilinear bl = resolve(xy.x, xy.y, L);
+  Bilinear bl;
+  if constexpr (FUSED) {  // offsets around the query's reference point
+    const int64_t bq = qm / p.M;  // b * Q + q
+    bl = resolve_fused(load_pair(reinterpret_cast<const T*>(p.ref) + 2 * bq), xy, L);
+  } else {
+    bl = resolve(xy.x, xy.y, L);
+  }
   unsigned old[4];
   int64_t row[4];
 #pragma unroll

@@ -100,32 +100,32 @@ inline dim3 query_block_grid(const OpParams& p) {
   return dim3((unsigned)((p.Q + kWarpsPerCta - 1) / kWarpsPerCta), (unsigned)p.M, (unsigned)p.B);
 }
 
-template <typename T, int VEC>
+template <typename T, int VEC, bool FUSED = false>
 static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid = query_block_grid(p);
-#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                                   \
-  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                  \
-    if (VEC > 1 && c.short_grid)                                                         \
-      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 3><<<grid, block, 0, st>>>(p); \
-    else                                                                                 \
-      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 0><<<grid, block, 0, st>>>(p); \
-    return cudaGetLastError();                                                           \
+#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                                          \
+  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                         \
+    if (VEC > 1 && c.short_grid)                                                                \
+      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 3, FUSED><<<grid, block, 0, st>>>(p); \
+    else                                                                                        \
+      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 0, FUSED><<<grid, block, 0, st>>>(p); \
+    return cudaGetLastError();                                                                  \
   }
   MSDA_FOR_EACH_SHAPE(MSDA_FWD_CASE)
 #undef MSDA_FWD_CASE
   return cudaErrorInvalidConfiguration;
 }
 
-template <typename T, typename A, int VEC, int MODE>
+template <typename T, typename A, int VEC, int MODE, bool FUSED = false>
 static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, bool pdl, cudaStream_t st) {
   const dim3 block(kWarpsPerCta * 32);
   const dim3 grid = query_block_grid(p);
 // The backward keeps one point per group in flight (NB = 1): its per-point
 // state (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
-#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                             \
-  if (c.lpr == LPR_ && c.cpl == CPL_)                                                              \
-    return launch_ex(msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE>, grid, block, 0, \
+#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                                   \
+  if (c.lpr == LPR_ && c.cpl == CPL_)                                                                    \
+    return launch_ex(msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE, FUSED>, grid, block, 0, \
                      st, pdl, p);
   MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
 #undef MSDA_BWD_CASE
@@ -135,6 +135,7 @@ static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, bool pdl, cudaS
 template <typename T>
 cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
+  if (p.fused) return c.vec == V16 ? fwd_by_shape<T, V16, true>(p, c, st) : cudaErrorNotSupported;
   if (c.vec == V16) return fwd_by_shape<T, V16>(p, c, st);
   if (c.vec == 1) return fwd_by_shape<T, 1>(p, c, st);
   return cudaErrorInvalidConfiguration;
@@ -144,6 +145,15 @@ template <typename T>
 cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
                             bool pdl, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
+  if (p.fused) {  // vector path only
+    if (c.vec != V16 || mode == kNoScatter) return cudaErrorNotSupported;
+    if (mode == kCounted) return bwd_by_shape<T, T, V16, kCounted, true>(p, c, pdl, st);
+    if (fp32_scatter || sizeof(T) == 4)
+      return mode == kScatterMerge ? bwd_by_shape<T, float, V16, kScatterMerge, true>(p, c, pdl, st)
+                                   : bwd_by_shape<T, float, V16, kScatter, true>(p, c, pdl, st);
+    return mode == kScatterMerge ? bwd_by_shape<T, T, V16, kScatterMerge, true>(p, c, pdl, st)
+                                 : bwd_by_shape<T, T, V16, kScatter, true>(p, c, pdl, st);
+  }
   if (mode == kNoScatter) {
     if (c.vec == V16) return bwd_by_shape<T, T, V16, kNoScatter>(p, c, false, st);
     if (c.vec == 1) return bwd_by_shape<T, T, 1, kNoScatter>(p, c, false, st);
@@ -174,7 +184,9 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
     per_sm = 4;
   const int64_t dense_blocks = std::max<int64_t>(num_sms, (int64_t)per_sm * num_sms - point_blocks);
   if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  msda_count_kernel<T><<<(unsigned)(point_blocks + dense_blocks), 256, 0, st>>>(p, (unsigned)point_blocks);
+  const dim3 grid((unsigned)(point_blocks + dense_blocks));
+  if (p.fused) msda_count_kernel<T, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
+  else msda_count_kernel<T><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
   return cudaGetLastError();
 }
 

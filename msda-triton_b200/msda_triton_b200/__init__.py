@@ -2,11 +2,18 @@
 
 Drop-in for the public surface of roulbac/msda-triton
 (src/msda_triton/__init__.py:9-12): ``multi_scale_deformable_attention``,
-plus the mmcv-style ``MultiScaleDeformableAttnFunction``. The kernels live in
+plus the mmcv-style ``MultiScaleDeformableAttnFunction`` and the
+Deformable-DETR cross-attention layer ``MSDACrossAttention`` that calls it
+(layers.py), whose prologue (reference point + offsets, softmax of the
+attention logits) the kernels can take fused
+(``multi_scale_deformable_attention_fused``). The kernels live in
 ``libmsda_b200.so`` behind the C ABI of include/msda_b200.h.
 """
 
-from .ops import MultiScaleDeformableAttnFunction, multi_scale_deformable_attention
+from .layers import MSDACrossAttention
+from .ops import (MultiScaleDeformableAttnFunction, multi_scale_deformable_attention,
+                  multi_scale_deformable_attention_fused)
 
-__all__ = ["multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction"]
+__all__ = ["multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction",
+           "MSDACrossAttention", "multi_scale_deformable_attention_fused"]
 __version__ = "0.1.0"

@@ -45,6 +45,17 @@ SIGNATURES = {
         [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t,
          _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, ctypes.c_uint32, _VP],
     ),
+    # Fused layer prologue: reference points + offsets (level pixels) and
+    # attention logits instead of locations and weights.
+    "msda_forward_fused": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _VP],
+    ),
+    "msda_backward_fused": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t,
+         _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, ctypes.c_uint32, _VP],
+    ),
     # The backward for callers that cannot allocate: same as msda_backward
     # without the workspace arguments (fp32 scratch from a static device array).
     "msda_backward_noalloc": (

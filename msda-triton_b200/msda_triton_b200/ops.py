@@ -252,6 +252,27 @@ def multi_scale_deformable_attention(
         )
     _lib.load()  # RuntimeError if the CUDA library is missing
 
+    spatial_shapes, level_start_index = _level_tables(spatial_shapes, level_start_index, value, L, S)
+
+    if B == 0 or Q == 0:
+        return value.new_zeros(B, Q, M * D)
+
+    if fp32_grad_accum is None:
+        fp32_grad_accum = _use_fp32_grad_accum(value)
+
+    return _MSDAFunction.apply(
+        value.contiguous(),
+        spatial_shapes,
+        level_start_index,
+        sampling_locations.contiguous(),
+        attention_weights.contiguous(),
+        fp32_grad_accum,
+    )
+
+
+def _level_tables(spatial_shapes, level_start_index, value, L, S):
+    """int64 (L, 2) shapes and (L,) level starts on value's device (starts
+    derived from the shapes when None), checked against S when on the host."""
     shapes_host = spatial_shapes if spatial_shapes.device.type == "cpu" else None
     spatial_shapes = spatial_shapes.to(device=value.device, dtype=torch.int64).contiguous()
     if level_start_index is None:
@@ -280,18 +301,166 @@ def multi_scale_deformable_attention(
                 f"spatial_shapes/level_start_index address {int(ends.max())} value rows but "
                 f"value has S={S}"
             )
+    return spatial_shapes, level_start_index
 
+
+# ---------------------------------------------------------------------------
+# Fused prologue: reference points + offsets and attention logits
+# ---------------------------------------------------------------------------
+def _forward_fused(value, spatial_shapes, level_start_index, reference_points, sampling_offsets,
+                   attention_logits):
+    B, S, M, D = value.shape
+    _, Q, _, L, K, _ = sampling_offsets.shape
+    out = value.new_empty(B, Q, M, D)
+    lib = _lib.load()
+    with _device_guard(value.device):
+        rc = lib.msda_forward_fused(
+            _ptr(value), _ptr(spatial_shapes), _ptr(level_start_index), _ptr(reference_points),
+            _ptr(sampling_offsets), _ptr(attention_logits), _ptr(out),
+            B, S, Q, M, D, L, K, _DTYPE_CODE[value.dtype], _stream(value.device),
+        )
+    _lib.check("msda_forward_fused", rc)
+    return out
+
+
+def _backward_fused(value, spatial_shapes, level_start_index, reference_points, sampling_offsets,
+                    attention_logits, grad_out, fp32_grad_accum, algo_flags=0):
+    """(grad_value, grad_offsets, grad_logits) of the fused forward."""
+    B, S, M, D = value.shape
+    _, Q, _, L, K, _ = sampling_offsets.shape
+    grad_value = torch.empty_like(value)
+    grad_off = torch.empty_like(sampling_offsets)
+    grad_logits = torch.empty_like(attention_logits)
+    lib = _lib.load()
+    code = _DTYPE_CODE[value.dtype]
+    flags = (_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0) | algo_flags
+    ws_bytes = lib.msda_backward_workspace_size(B, S, Q, M, D, L, K, code, flags)
+    workspace = (
+        torch.empty(ws_bytes, dtype=torch.uint8, device=value.device) if ws_bytes else None
+    )
+    with _device_guard(value.device):
+        rc = lib.msda_backward_fused(
+            _ptr(value), _ptr(spatial_shapes), _ptr(level_start_index), _ptr(reference_points),
+            _ptr(sampling_offsets), _ptr(attention_logits), _ptr(grad_out),
+            _ptr(grad_value), _ptr(grad_off), _ptr(grad_logits), _ptr(workspace), ws_bytes,
+            B, S, Q, M, D, L, K, code, flags, _stream(value.device),
+        )
+    _lib.check("msda_backward_fused", rc)
+    return grad_value, grad_off, grad_logits
+
+
+class _MSDAFusedFunction(torch.autograd.Function):
+    """Autograd Function of :func:`multi_scale_deformable_attention_fused`."""
+
+    @staticmethod
+    def forward(ctx, value, spatial_shapes, level_start_index, reference_points, sampling_offsets,
+                attention_logits, fp32_grad_accum):
+        B, S, M, D = value.shape
+        Q = sampling_offsets.shape[1]
+        out = _forward_fused(value, spatial_shapes, level_start_index, reference_points,
+                             sampling_offsets, attention_logits)
+        ctx.save_for_backward(value, spatial_shapes, level_start_index, reference_points,
+                              sampling_offsets, attention_logits)
+        ctx.fp32_grad_accum = bool(fp32_grad_accum)
+        return out.view(B, Q, M * D)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_out):
+        value, shapes, starts, ref, off, logits = ctx.saved_tensors
+        B, S, M, D = value.shape
+        Q = off.shape[1]
+        grad_out = grad_out.reshape(B, Q, M, D).to(value.dtype).contiguous()
+        if grad_out.data_ptr() % 16:  # the fused kernels read 16-byte vectors
+            grad_out = grad_out.clone()
+        grad_value, grad_off, grad_logits = _backward_fused(
+            value, shapes, starts, ref, off, logits, grad_out, ctx.fp32_grad_accum)
+        grad_ref = None
+        if ctx.needs_input_grad[3]:
+            # location = ref + offset / (W_l, H_l): d/dref = sum over (m, l, k)
+            # of d/doffset * (W_l, H_l).
+            wh = shapes.flip(-1).to(torch.float32)  # (L, 2)
+            grad_ref = (grad_off.float() * wh[:, None, :]).sum(dim=(2, 3, 4)).to(ref.dtype)
+        return grad_value, None, None, grad_ref, grad_off, grad_logits, None
+
+
+def multi_scale_deformable_attention_fused(
+    value: torch.Tensor,
+    spatial_shapes: torch.Tensor,
+    level_start_index: torch.Tensor | None,
+    reference_points: torch.Tensor,
+    sampling_offsets: torch.Tensor,
+    attention_logits: torch.Tensor,
+    *,
+    fp32_grad_accum: bool | None = None,
+) -> torch.Tensor:
+    """Multi-scale deformable attention with the Deformable-DETR layer's
+    prologue fused in (the prologue of the reference's layer,
+    labs/solutions/lab00.py:199-208, followed by the operator).
+
+    Equivalent to ``multi_scale_deformable_attention(value, spatial_shapes,
+    level_start_index, reference_points[:, :, None, None, None, :] +
+    sampling_offsets / (W_l, H_l), attention_logits.softmax over (L, K))``
+    without materialising the locations and weights.
+
+    Args:
+        value: ``(B, S, M, D)``.
+        spatial_shapes: ``(L, 2)`` ``(H_l, W_l)``; level_start_index as in
+            :func:`multi_scale_deformable_attention`.
+        reference_points: ``(B, Q, 2)`` normalised ``(x, y)``.
+        sampling_offsets: ``(B, Q, M, L, K, 2)`` in pixels of each level.
+        attention_logits: ``(B, Q, M, L, K)``, softmaxed jointly over
+            ``(L, K)`` per query and head.
+        fp32_grad_accum: as in :func:`multi_scale_deformable_attention`.
+
+    Returns:
+        ``(B, Q, M * D)`` in ``value.dtype``; differentiable with respect to
+        value, reference_points, sampling_offsets and attention_logits.
+    """
+    if value.dim() != 4:
+        raise ValueError(f"value must be (B, S, M, D), got {tuple(value.shape)}")
+    if sampling_offsets.dim() != 6 or sampling_offsets.shape[-1] != 2:
+        raise ValueError(
+            f"sampling_offsets must be (B, Q, M, L, K, 2), got {tuple(sampling_offsets.shape)}")
+    B, S, M, D = value.shape
+    _, Q, _, L, K, _ = sampling_offsets.shape
+    if sampling_offsets.shape[0] != B or sampling_offsets.shape[2] != M:
+        raise ValueError(f"sampling_offsets {tuple(sampling_offsets.shape)} inconsistent with value "
+                         f"{tuple(value.shape)}")
+    if reference_points.shape != (B, Q, 2):
+        raise ValueError(f"reference_points must be {(B, Q, 2)}, got {tuple(reference_points.shape)}")
+    if attention_logits.shape != (B, Q, M, L, K):
+        raise ValueError(
+            f"attention_logits must be {(B, Q, M, L, K)}, got {tuple(attention_logits.shape)}")
+    if spatial_shapes.shape != (L, 2):
+        raise ValueError(f"spatial_shapes must be ({L}, 2), got {tuple(spatial_shapes.shape)}")
+    if not (value.dtype == reference_points.dtype == sampling_offsets.dtype == attention_logits.dtype):
+        raise ValueError("value/reference_points/sampling_offsets/attention_logits dtypes must match, "
+                         f"got {value.dtype}/{reference_points.dtype}/{sampling_offsets.dtype}/"
+                         f"{attention_logits.dtype}")
+    if value.dtype not in _FLOAT_DTYPES:
+        raise ValueError(f"unsupported dtype {value.dtype}; use fp32, fp16 or bf16")
+    if value.device.type != "cuda":
+        raise ValueError("the operator requires CUDA tensors on a B200 (sm_100a) GPU; MPS (Apple GPU) "
+                         "and CPU tensors are not supported")
+    if any(t.device != value.device for t in (reference_points, sampling_offsets, attention_logits)):
+        raise ValueError("value, reference_points, sampling_offsets and attention_logits must be on "
+                         "the same CUDA device")
+    _lib.load()
+    spatial_shapes, level_start_index = _level_tables(spatial_shapes, level_start_index, value, L, S)
     if B == 0 or Q == 0:
         return value.new_zeros(B, Q, M * D)
-
     if fp32_grad_accum is None:
         fp32_grad_accum = _use_fp32_grad_accum(value)
-
-    return _MSDAFunction.apply(
-        value.contiguous(),
-        spatial_shapes,
-        level_start_index,
-        sampling_locations.contiguous(),
-        attention_weights.contiguous(),
-        fp32_grad_accum,
+    if D % (16 // value.element_size()) or value.data_ptr() % 16:
+        # The fused kernels run on the 16-byte vector path only; otherwise the
+        # prologue is formed with tensor operations before the operator.
+        wh = spatial_shapes.flip(-1).to(value.dtype)
+        locations = reference_points[:, :, None, None, None, :] + sampling_offsets / wh[:, None, :]
+        weights = attention_logits.reshape(B, Q, M, L * K).softmax(-1).view(B, Q, M, L, K)
+        return multi_scale_deformable_attention(value, spatial_shapes, level_start_index,
+                                                locations, weights, fp32_grad_accum=fp32_grad_accum)
+    return _MSDAFusedFunction.apply(
+        value.contiguous(), spatial_shapes, level_start_index, reference_points.contiguous(),
+        sampling_offsets.contiguous(), attention_logits.contiguous(), fp32_grad_accum,
     )

@@ -27,7 +27,8 @@ def _declared():
 def test_header_declares_the_abi():
     assert set(_declared()) == {"msda_version", "msda_last_error", "msda_forward",
                                 "msda_backward_workspace_size", "msda_backward",
-                                "msda_backward_noalloc"}
+                                "msda_backward_noalloc", "msda_forward_fused",
+                                "msda_backward_fused"}
 
 
 def test_library_exports_every_declared_symbol():
@@ -146,7 +147,11 @@ def test_default_accumulator_policy():
 def test_package_surface():
     import msda_triton_b200 as pkg
 
-    assert pkg.__all__ == ["multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction"]
+    # The reference's export (src/msda_triton/__init__.py:9-12) plus the
+    # mmcv-style Function and the layer around the operator.
+    assert pkg.__all__[0] == "multi_scale_deformable_attention"
+    assert set(pkg.__all__) == {"multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction",
+                                "MSDACrossAttention", "multi_scale_deformable_attention_fused"}
     assert callable(MultiScaleDeformableAttnFunction.apply)
 
 

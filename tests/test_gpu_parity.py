@@ -498,3 +498,135 @@ def test_counted_scatter_matches_fp32_accumulation(dtype):
     torch.testing.assert_close(got[0].float(), ref[0].float(), **tol)
     torch.testing.assert_close(got[1], ref[1])
     torch.testing.assert_close(got[2], ref[2])
+
+
+# ---------------------------------------------------------------------------
+# Fused prologue: reference points + offsets (level pixels), attention logits
+# ---------------------------------------------------------------------------
+from msda_triton_b200 import multi_scale_deformable_attention_fused  # noqa: E402
+from oracle import msda_oracle as _orc  # noqa: E402
+
+FUSED_CASES = [
+    ("sparse", dict(B=2, Q=40, M=4, D=32, K=4, shapes=[(24, 32), (12, 16), (6, 8)])),
+    ("dense", dict(B=1, Q=160, M=2, D=32, K=2, shapes=[(8, 10), (4, 5)])),
+    ("d64_oob", dict(B=1, Q=24, M=2, D=64, K=3, shapes=[(10, 14), (5, 7)])),
+]
+FUSED_ALGOS = {
+    "auto_fp32": (0, True),
+    "native": (0, False),
+    "scatter_fp32": (_clib.MSDA_BWD_FORCE_SCATTER, True),
+    "counted": (_clib.MSDA_BWD_FORCE_COUNTED, True),
+}
+
+
+def _fused_inputs(kw, dtype, seed=11):
+    value, shapes, starts, _, _ = cases.make_inputs(**kw, dtype=dtype, device=DEV, seed=seed)
+    B, Q, M, K, L = kw["B"], kw["Q"], kw["M"], kw["K"], len(kw["shapes"])
+    gen = torch.Generator().manual_seed(seed + 1)
+    ref = torch.rand(B, Q, 2, generator=gen)
+    off = 3.0 * torch.randn(B, Q, M, L, K, 2, generator=gen)  # pixels; some corners fall outside
+    logits = torch.randn(B, Q, M, L, K, generator=gen)
+    return value, shapes, starts, ref.to(DEV, dtype), off.to(DEV, dtype), logits.to(DEV, dtype)
+
+
+def _kink_eps(dtype):
+    return 1e-3 if dtype == torch.float32 else 1e-6
+
+
+def _fused_reference(value, shapes, ref, off, logits, g):
+    """float64 composition on the CPU (the layer's prologue, then the
+    grid_sample oracle), differentiated by autograd."""
+    v, r, o, lg = (t.detach().double().cpu().requires_grad_(True) for t in (value, ref, off, logits))
+    B, Q, M, L, K, _ = o.shape
+    wh = shapes.detach().cpu().flip(-1).double()
+    loc = r[:, :, None, None, None, :] + o / wh[:, None, :]
+    attn = lg.reshape(B, Q, M, L * K).softmax(-1).view(B, Q, M, L, K)
+    out = _orc.msda_grid_sample(v, shapes.cpu(), loc, attn)
+    out.backward(g.detach().double().cpu().reshape(out.shape))
+    return out.detach(), v.grad, r.grad, o.grad, lg.grad, loc.detach()
+
+
+@pytest.mark.parametrize("algo", list(FUSED_ALGOS))
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,kw", FUSED_CASES, ids=[c[0] for c in FUSED_CASES])
+def test_fused_prologue_matches_the_composition(name, kw, dtype, algo):
+    flags, fp32 = FUSED_ALGOS[algo]
+    value, shapes, starts, ref, off, logits = _fused_inputs(kw, dtype)
+    B, Q, M, D = kw["B"], kw["Q"], kw["M"], kw["D"]
+    out = _ops._forward_fused(value, shapes, starts, ref, off, logits)
+    g = cases.grad_output_like(out)
+    gv, goff, glog = _ops._backward_fused(value, shapes, starts, ref, off, logits, g, fp32, flags)
+    out_r, gv_r, _, goff_r, glog_r, loc = _fused_reference(value, shapes, ref, off, logits, g)
+    tol = STRICT_TOL[dtype]
+    close(out.reshape(B, Q, M * D), out_r, tol, "out")
+    gv_tol = REF_BWD_TOL[dtype] if (algo == "native" and dtype != torch.float32) else tol
+    close(gv, gv_r, gv_tol, "grad_value")
+    close(glog, glog_r, tol, "grad_logits")
+    # Kinks of the bilinear interpolant are excluded for every dtype here:
+    # reference + offset lands exactly on integers often with 16-bit inputs,
+    # where the float64 composition (divide by W, then multiply) may round to
+    # the other side. For 16-bit inputs the kernel's pixel coordinate is
+    # exact, so only points within float64 rounding of an integer go.
+    keep = ~cases.kink_mask(loc, shapes, _kink_eps(dtype))
+    assert keep.double().mean() > 0.95
+    torch.testing.assert_close(goff.double().cpu()[keep], goff_r[keep], **tol, msg=lambda m: f"grad_offsets: {m}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_fused_public_op_gradients_including_reference_points(dtype):
+    value, shapes, starts, ref, off, logits = _fused_inputs(FUSED_CASES[0][1], dtype, seed=21)
+    leaves = [t.clone().requires_grad_(True) for t in (value, ref, off, logits)]
+    out = multi_scale_deformable_attention_fused(leaves[0], shapes, None, *leaves[1:])
+    g = cases.grad_output_like(out.detach())
+    out.backward(g)
+    out_r, gv_r, gr_r, goff_r, glog_r, loc = _fused_reference(value, shapes, ref, off, logits, g)
+    tol = STRICT_TOL[dtype]
+    close(out, out_r, tol, "out")
+    close(leaves[0].grad, gv_r, tol, "grad_value")
+    close(leaves[3].grad, glog_r, tol, "grad_logits")
+    # Kink points excluded (see above); the reference points' gradient sums
+    # over a query's points, so queries with any kink point are excluded.
+    keep = ~cases.kink_mask(loc, shapes, _kink_eps(dtype))
+    torch.testing.assert_close(leaves[2].grad.double().cpu()[keep], goff_r[keep], **tol)
+    q_keep = keep.all(-1).all(-1).all(-1)
+    assert q_keep.double().mean() > (0.5 if dtype == torch.float32 else 0.3)
+    got_r = leaves[1].grad.double().cpu()[q_keep]
+    if dtype == torch.float32:
+        torch.testing.assert_close(got_r, gr_r[q_keep], rtol=1e-3, atol=1e-3)
+    else:  # a sum of M*L*K 16-bit offset gradients
+        assert (got_r - gr_r[q_keep]).abs().max() <= 2e-2 * gr_r.abs().max()
+
+
+def test_fused_rejects_the_owner_algorithm():
+    value, shapes, starts, ref, off, logits = _fused_inputs(FUSED_CASES[0][1], torch.bfloat16)
+    g = torch.zeros(2, 40, 4, 32, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(_clib.MSDALibraryError, match="owner"):
+        _ops._backward_fused(value, shapes, starts, ref, off, logits, g, True, _clib.MSDA_BWD_FORCE_OWNER)
+
+
+def test_fused_op_falls_back_off_the_vector_path():
+    """Head dims that are not a multiple of the 16-byte vector (and
+    misaligned value buffers) take the tensor-op prologue + the operator."""
+    kw = dict(B=1, Q=12, M=2, D=6, K=2, shapes=[(5, 7), (3, 4)])
+    value, shapes, starts, ref, off, logits = _fused_inputs(kw, torch.bfloat16, seed=31)
+    lib = _clib.load()
+    out = torch.empty(1, 12, 2, 6, device=DEV, dtype=torch.bfloat16)
+    rc = lib.msda_forward_fused(_ops._ptr(value), _ops._ptr(shapes), _ops._ptr(starts), _ops._ptr(ref),
+                                _ops._ptr(off), _ops._ptr(logits), _ops._ptr(out), 1, value.shape[1], 12,
+                                2, 6, 2, 2, _clib.MSDA_DTYPE_BF16, None)
+    assert rc == _clib.MSDA_ERR_UNSUPPORTED
+    leaves = [t.clone().requires_grad_(True) for t in (value, ref, off, logits)]
+    out = multi_scale_deformable_attention_fused(leaves[0], shapes, None, *leaves[1:])
+    g = cases.grad_output_like(out.detach())
+    out.backward(g)
+    # The fallback feeds the operator bf16 locations and weights (formed
+    # with bf16 tensor ops, as the reference layer does): check it against
+    # the float64 oracle on those same inputs.
+    wh = shapes.flip(-1).to(torch.bfloat16)
+    loc = ref[:, :, None, None, None, :] + off / wh[:, None, :]
+    attn = logits.reshape(1, 12, 2, 4).softmax(-1).view(1, 12, 2, 2, 2)
+    _, (gv_r, _, _) = oracle64(value, shapes, starts, loc, attn, g.view(1, 12, 2, 6))
+    out_r = _orc.msda_grid_sample(value.double().cpu(), shapes.cpu(), loc.double().cpu(), attn.double().cpu())
+    close(out, out_r, STRICT_TOL[torch.bfloat16], "out")
+    close(leaves[0].grad, gv_r, STRICT_TOL[torch.bfloat16], "grad_value")
+    assert leaves[1].grad is not None and leaves[3].grad is not None
