@@ -278,6 +278,9 @@ def kernel_breakdown(one, steps=5):
 
 
 def backward_algorithm(kernels):
+    if "msda_absmax_kernel" in kernels:
+        kind = "counted" if "msda_count_kernel" in kernels else "scatter"
+        return f"deterministic {kind} (64-bit fixed-point rows)"
     if "msda_count_kernel" in kernels:
         return "counted (fp32 rows for multi-hit pixels)"
     if "msda_bwd_value_owner_kernel" in kernels:
@@ -287,7 +290,7 @@ def backward_algorithm(kernels):
     return "scatter (native packed reductions)"
 
 
-def e2e_leg(x, steps, warmup, fp32_acc):
+def e2e_leg(x, steps, warmup, fp32_acc, deterministic=False):
     """Public op with pinned host buffers. Every step copies its inputs
     host->device, runs forward + backward through
     multi_scale_deformable_attention, and copies the output and the three
@@ -333,7 +336,8 @@ def e2e_leg(x, steps, warmup, fp32_acc):
             v = b["value"].detach().requires_grad_(True)
             l = b["sampling_locations"].detach().requires_grad_(True)
             a = b["attention_weights"].detach().requires_grad_(True)
-            out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc)
+            out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc,
+                                                   deterministic=deterministic)
             out.backward(b["grad_output"])
             used[i % 2].record(compute)
             if i + 1 < n:
@@ -448,6 +452,8 @@ def main(argv=None) -> int:
     ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
     ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner", "counted"],
                     help="force the grad_value algorithm of the device leg (default: automatic)")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="bitwise-reproducible grad_value (64-bit fixed-point accumulation)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time direct launches instead of CUDA-graph replays")
     ap.add_argument("--no-e2e", action="store_true")
@@ -475,6 +481,8 @@ def main(argv=None) -> int:
     algo_flags = {"auto": 0, "scatter": lib.MSDA_BWD_FORCE_SCATTER,
                   "owner": lib.MSDA_BWD_FORCE_OWNER,
                   "counted": lib.MSDA_BWD_FORCE_COUNTED}[args.bwd_algo]
+    if args.deterministic:
+        algo_flags |= lib.MSDA_BWD_DETERMINISTIC
 
     # ---- device leg -------------------------------------------------------
     gs, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
@@ -499,7 +507,7 @@ def main(argv=None) -> int:
     # ---- e2e leg ----------------------------------------------------------
     e2e = None
     if not args.no_e2e:
-        run_e2e, h2d, d2h = e2e_leg(x, args.steps, args.warmup, fp32_acc)
+        run_e2e, h2d, d2h = e2e_leg(x, args.steps, args.warmup, fp32_acc, args.deterministic)
         barrier(world)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -559,7 +567,7 @@ def main(argv=None) -> int:
             "config": config_dict(preset, dtype, world),
             "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,
             "fwd_bwd_us": (fwd_mean + bwd_mean) * 1e3,
-            "fp32_grad_accum": fp32_acc, "bwd_algo": algo,
+            "fp32_grad_accum": fp32_acc, "deterministic": args.deterministic, "bwd_algo": algo,
             "kernels_us": {k: round(t, 2) for k, (t, _) in kernels.items()},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": (None if launches_per_step is None

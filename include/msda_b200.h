@@ -82,6 +82,23 @@ typedef enum msda_status {
 #define MSDA_BWD_FORCE_SCATTER 2u
 #define MSDA_BWD_FORCE_OWNER 4u
 #define MSDA_BWD_FORCE_COUNTED 8u
+/* Deterministic grad_value (no counterpart in the reference, which documents
+ * its backward as nondeterministic, README.md:179 and ops.py:135-138):
+ * contributions a * w_c * g are rounded once to 64-bit fixed point and
+ * accumulated with integer reductions, whose sum does not depend on the
+ * order the atomics land in, then each element is rounded once to the
+ * value dtype. Results are bitwise reproducible from run to run for the same
+ * inputs. The fixed-point scale is set on the device from max|attention
+ * weight| (1 for the fused prologue's softmax weights) and max|grad_output|
+ * so that no row sum can overflow; one contribution's rounding error is below
+ * 2^-45 of the largest possible contribution for Q*K <= 2^17 (finer than
+ * fp32 accumulation). Inputs with non-finite values fall back to fp32
+ * atomics (Inf / NaN propagate as in fp32 accumulation; no determinism
+ * claim then). Takes the hit-counted algorithm for sparse sampling
+ * (Q*L*K <= 2*S), else the scatter; MSDA_BWD_FORCE_SCATTER / _COUNTED pick
+ * one. MSDA_BWD_FP32_ACCUM is implied; MSDA_BWD_FORCE_OWNER is rejected.
+ * Needs a workspace (msda_backward_workspace_size with this flag). */
+#define MSDA_BWD_DETERMINISTIC 16u
 
 /* Library version string, e.g. "msda_b200 0.1.0 sm_100a". */
 MSDA_API const char* msda_version(void);
@@ -142,9 +159,9 @@ MSDA_API int msda_backward_fused(const void* value, const int64_t* spatial_shape
                                  int32_t dtype, uint32_t flags, void* stream);
 
 /*
- * Bytes of fp32 workspace msda_backward needs for these sizes and flags
- * (0 when the chosen algorithm uses none). Replaces the allocation of the
- * fp32 grad_value buffer at src/msda_triton/ops.py:76-77.
+ * Bytes of workspace msda_backward needs for these sizes and flags (0 when
+ * the chosen algorithm uses none). Replaces the allocation of the fp32
+ * grad_value buffer at src/msda_triton/ops.py:76-77.
  */
 MSDA_API size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t num_queries,
                                              int32_t num_heads, int32_t head_dim, int32_t num_levels,
@@ -156,8 +173,9 @@ MSDA_API size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, 
  * grad_value need not be zeroed by the caller: the call initialises it.
  * Replaces _MSDAFunction.backward's zero-fill, kernel launch and downcast
  * (src/msda_triton/ops.py:76-92; kernel src/msda_triton/kernels.py:166-291).
- * grad_value is accumulated with atomics: results are not bitwise
- * deterministic from run to run (as in the reference, ops.py:135-138).
+ * grad_value is accumulated with atomics: without MSDA_BWD_DETERMINISTIC
+ * results are not bitwise deterministic from run to run (as in the
+ * reference, ops.py:135-138).
  */
 MSDA_API int msda_backward(const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
                   const void* sampling_locations, const void* attention_weights,

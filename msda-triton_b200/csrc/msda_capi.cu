@@ -116,17 +116,22 @@ constexpr double kCountedMaxPointsPerRow = 2.0;
 // warp's same-row contributions before reducing them.
 constexpr double kMergeMinPointsPerRow = 2.0;
 
-enum class Algo { kScatterNative, kScatterF32, kCounted, kOwner };
+enum class Algo { kScatterNative, kScatterF32, kCounted, kOwner, kScatterFixed, kCountedFixed };
 
 Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
   const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
   const bool fp32_semantics = (flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32;
+  const double density = (double)s.Q * s.L * s.K / (double)s.S;
+  if (flags & MSDA_BWD_DETERMINISTIC) {  // 64-bit fixed-point accumulation
+    if (flags & MSDA_BWD_FORCE_SCATTER) return Algo::kScatterFixed;
+    if (flags & MSDA_BWD_FORCE_COUNTED) return Algo::kCountedFixed;
+    return density <= kCountedMaxPointsPerRow ? Algo::kCountedFixed : Algo::kScatterFixed;
+  }
   const Algo scatter = fp32_ws ? Algo::kScatterF32 : Algo::kScatterNative;
   if (flags & MSDA_BWD_FORCE_SCATTER) return scatter;
   if ((flags & MSDA_BWD_FORCE_OWNER) && owner_ok) return Algo::kOwner;
   if (flags & MSDA_BWD_FORCE_COUNTED) return Algo::kCounted;
   if (!fp32_semantics) return scatter;
-  const double density = (double)s.Q * s.L * s.K / (double)s.S;
   if (density <= kCountedMaxPointsPerRow) return Algo::kCounted;
   if (owner_ok && density < kOwnerMaxPointsPerRow) return Algo::kOwner;
   return scatter;
@@ -134,14 +139,31 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace of the hit-counted scatter: per-row hit counts, then (fp16/bf16
-// only) one fp32 row per grad_value row.
-size_t counted_ws_bytes(const Shape& s, int32_t dtype, size_t* acc_offset) {
+// Deterministic (fixed-point) algorithms: the workspace starts with the
+// absmax header (2 words, padded).
+constexpr size_t kFixedHeaderBytes = 256;
+
+// Workspace of the hit-counted scatter: [absmax header (fixed point only)]
+// per-row hit counts, then one accumulator row per grad_value row -- fp32
+// (fp16/bf16 only; fp32 values accumulate in grad_value itself) or 64-bit
+// fixed point (every dtype).
+size_t counted_ws_bytes(const Shape& s, int32_t dtype, bool fixed, size_t* counts_offset,
+                        size_t* acc_offset) {
   const size_t rows = (size_t)s.B * s.S * s.M;
+  const size_t head = fixed ? kFixedHeaderBytes : 0;
   const size_t counts = align256(rows * sizeof(unsigned));
-  *acc_offset = counts;
+  *counts_offset = head;
+  *acc_offset = head + counts;
+  if (fixed) return head + counts + rows * (size_t)s.D * sizeof(long long);
   if (dtype == MSDA_DTYPE_F32) return counts;
   return counts + rows * (size_t)s.D * sizeof(float);
+}
+
+// ceil(log2(n)) for n >= 1.
+int ceil_log2(int64_t n) {
+  int r = 0;
+  while (r < 62 && ((int64_t)1 << r) < n) ++r;
+  return r;
 }
 
 int sm_count() {
@@ -291,12 +313,14 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
     return 0;
   msda::OwnerPlan plan;
   const Algo a = choose_algo(s, dtype, flags, owner_possible(s, es, &plan));
-  if (a == Algo::kCounted) {
-    size_t off;
-    return counted_ws_bytes(s, dtype, &off);
+  if (a == Algo::kCounted || a == Algo::kCountedFixed) {
+    size_t coff, aoff;
+    return counted_ws_bytes(s, dtype, a == Algo::kCountedFixed, &coff, &aoff);
   }
+  const size_t elems = (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim;
+  if (a == Algo::kScatterFixed) return kFixedHeaderBytes + elems * sizeof(long long);
   if (a != Algo::kScatterF32) return 0;
-  return (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim * sizeof(float);
+  return elems * sizeof(float);
 }
 
 // The backward behind msda_backward and msda_backward_fused (fused: offsets
@@ -310,6 +334,8 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   if (int rc = check_shape(s, dtype)) return rc;
   if (fused && (flags & MSDA_BWD_FORCE_OWNER))
     return fail(MSDA_ERR_UNSUPPORTED, "%s: the owner algorithm does not take the fused prologue", fn);
+  if ((flags & MSDA_BWD_DETERMINISTIC) && (flags & MSDA_BWD_FORCE_OWNER))
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_DETERMINISTIC and MSDA_BWD_FORCE_OWNER are exclusive", fn);
   if (s.B == 0) return succeed();
   const int es = elem_size(dtype);
   const size_t gv_bytes = (size_t)s.B * s.S * s.M * s.D * es;
@@ -332,16 +358,21 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   msda::OwnerPlan plan;
   const bool owner_ok = !fused && owner_possible(s, es, &plan);
   const Algo algo = choose_algo(s, dtype, flags, owner_ok);
+  const bool fixed = algo == Algo::kScatterFixed || algo == Algo::kCountedFixed;
   const bool fp32_ws = algo == Algo::kScatterF32;
-  const bool counted = algo == Algo::kCounted;
+  const bool counted = algo == Algo::kCounted || algo == Algo::kCountedFixed;
+  const bool ws_target = fp32_ws || algo == Algo::kScatterFixed;  // reductions into the workspace
   const size_t ws_need = msda_backward_workspace_size(s.B, s.S, s.Q, s.M, s.D, s.L, s.K, dtype, flags);
-  if (fp32_ws || counted) {
+  if (fp32_ws || counted || fixed) {
     if (!workspace || workspace_bytes < ws_need)
-      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: fp32 accumulation needs a workspace of %zu bytes (got %zu)", fn, ws_need, workspace_bytes);
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: %s accumulation needs a workspace of %zu bytes (got %zu)", fn, fixed ? "deterministic" : "fp32", ws_need, workspace_bytes);
     if (!aligned(workspace, 16))
       return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
   }
-  void* target = fp32_ws ? workspace : grad_value;
+  unsigned* fixed_hdr = fixed ? static_cast<unsigned*>(workspace) : nullptr;
+  void* target = algo == Algo::kScatterFixed ? static_cast<void*>(static_cast<char*>(workspace) + kFixedHeaderBytes)
+                 : fp32_ws                 ? workspace
+                                           : grad_value;
   msda::Cfg cfg;
   const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) &&
                       (algo == Algo::kOwner || aligned(target, 16)) &&
@@ -351,24 +382,42 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
     return fail(MSDA_ERR_UNSUPPORTED, "%s: the fused prologue needs 16-byte aligned buffers and head_dim a multiple of %d", fn, 16 / es);
 
   cudaError_t e;
-  size_t acc_off = 0;
+  size_t counts_off = 0, acc_off = 0;
   if (counted) {
-    counted_ws_bytes(s, dtype, &acc_off);
-    e = cudaMemsetAsync(workspace, 0, (size_t)s.B * s.S * s.M * sizeof(unsigned), st);
+    counted_ws_bytes(s, dtype, fixed, &counts_off, &acc_off);
+    // Counts (and the absmax header before them).
+    e = cudaMemsetAsync(workspace, 0, counts_off + (size_t)s.B * s.S * s.M * sizeof(unsigned), st);
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count zero-fill");
   }
   // The backward may overlap the tail of the kernel before it when that
-  // kernel is ours (the hit count, or the zero-fill kernel; not a memset).
+  // kernel is ours (the hit count, the zero-fill kernel or the absmax pass;
+  // not a memset).
   bool bwd_pdl = counted;
+  bool zero_kernel = false;
   if (!counted && algo != Algo::kOwner) {
-    const size_t zbytes = fp32_ws ? ws_need : gv_bytes;
-    if (zbytes % 16 == 0 && aligned(target, 16)) {
-      e = msda::launch_zero(target, zbytes, sm_count(), st);
+    // The deterministic scatter zeroes the header with the accumulator.
+    void* zdst = algo == Algo::kScatterFixed ? workspace : target;
+    const size_t zbytes = ws_target ? ws_need : gv_bytes;
+    if (zbytes % 16 == 0 && aligned(zdst, 16)) {
+      e = msda::launch_zero(zdst, zbytes, sm_count(), st);
       bwd_pdl = zbytes >= 16;
+      zero_kernel = bwd_pdl;
     } else {
-      e = cudaMemsetAsync(target, 0, zbytes, st);
+      e = cudaMemsetAsync(zdst, 0, zbytes, st);
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward zero-fill");
+  }
+  if (fixed) {
+    // Pass 0: max |attention weight| (or the logits' finiteness) and
+    // max |grad_out| into the header.
+    const int64_t n_attn = s.B * s.Q * s.M * s.L * s.K, n_g = s.B * s.Q * s.M * s.D;
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = msda::launch_absmax<float>(attention_weights, n_attn, fused, grad_output, n_g, fixed_hdr, sm_count(), zero_kernel, st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_absmax<__half>(attention_weights, n_attn, fused, grad_output, n_g, fixed_hdr, sm_count(), zero_kernel, st); break;
+      default: e = msda::launch_absmax<__nv_bfloat16>(attention_weights, n_attn, fused, grad_output, n_g, fixed_hdr, sm_count(), zero_kernel, st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward absmax launch");
+    if (!counted) bwd_pdl = true;  // behind the absmax pass
   }
 
   msda::OpParams p{};
@@ -381,12 +430,15 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.fused = fused ? 1 : 0;
   p.grad_out = grad_output;
   p.grad_value = (algo == Algo::kOwner || counted) ? grad_value : target;
+  p.acc_words = fixed ? 2 : 1;
+  p.fixed_hdr = fixed_hdr;
+  p.fixed_log2n = ceil_log2(s.Q * s.K);
   p.grad_loc = grad_sampling_locations;
   p.grad_attn = grad_attention_weights;
   if (counted) {
-    p.counts = static_cast<unsigned*>(workspace);
-    p.acc = dtype == MSDA_DTYPE_F32 ? static_cast<float*>(grad_value)
-                                    : reinterpret_cast<float*>(static_cast<char*>(workspace) + acc_off);
+    p.counts = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + counts_off);
+    p.acc = (dtype == MSDA_DTYPE_F32 && !fixed) ? grad_value
+                                                : static_cast<void*>(static_cast<char*>(workspace) + acc_off);
   }
   p.B = s.B; p.S = s.S; p.Q = s.Q;
   p.M = s.M; p.D = s.D; p.L = s.L; p.K = s.K;
@@ -408,18 +460,19 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
                    : counted            ? msda::kCounted
                    : merge              ? msda::kScatterMerge
                                         : msda::kScatter;
+  const int acc = fixed ? msda::kAccFixed : (fp32_ws || dtype == MSDA_DTYPE_F32) ? msda::kAccF32 : msda::kAccNative;
   switch (dtype) {
-    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, true, bwd_pdl, st); break;
-    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, fp32_ws, bwd_pdl, st); break;
-    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, mode, fp32_ws, bwd_pdl, st); break;
+    case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, acc, bwd_pdl, st); break;
+    case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, acc, bwd_pdl, st); break;
+    default: e = msda::launch_backward<__nv_bfloat16>(p, cfg, mode, acc, bwd_pdl, st); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "msda_backward launch");
   if (counted) {
     const bool fvec = aligned(grad_value, 16);
     switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_finalize<float>(p, fvec, sm_count(), st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_finalize<__half>(p, fvec, sm_count(), st); break;
-      default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, sm_count(), st); break;
+      case MSDA_DTYPE_F32: e = msda::launch_finalize<float>(p, fvec, fixed, sm_count(), st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_finalize<__half>(p, fvec, fixed, sm_count(), st); break;
+      default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, fixed, sm_count(), st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward finalize launch");
   }
@@ -432,6 +485,17 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
       default: e = msda::launch_owner<__nv_bfloat16>(p, plan, st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward grad_value launch");
+  }
+  if (algo == Algo::kScatterFixed) {
+    const int64_t n = s.B * s.S * s.M * s.D;
+    const bool cast_vec = aligned(grad_value, 16);
+    const long long* src = static_cast<const long long*>(target);
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = msda::launch_cast_fixed<float>(src, static_cast<float*>(grad_value), n, cast_vec, fixed_hdr, p.fixed_log2n, sm_count(), st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_cast_fixed<__half>(src, static_cast<__half*>(grad_value), n, cast_vec, fixed_hdr, p.fixed_log2n, sm_count(), st); break;
+      default: e = msda::launch_cast_fixed<__nv_bfloat16>(src, static_cast<__nv_bfloat16*>(grad_value), n, cast_vec, fixed_hdr, p.fixed_log2n, sm_count(), st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "msda_backward fixed-point downcast launch");
   }
   if (fp32_ws) {
     const int64_t n = s.B * s.S * s.M * s.D;

@@ -304,6 +304,89 @@ __device__ __forceinline__ void red_add_vec_hint(A* p, const float (&v)[VEC], ui
   }
 }
 
+// ---------------------------------------------------------------------------
+// Deterministic grad_value: 64-bit fixed-point accumulation.
+//
+// Every contribution c = a * w_c * g_d is rounded once to an integer multiple
+// of 2^-F and added with an integer `red.global.add.u64`. Integer addition is
+// associative, so the sum -- and the value rounded from it -- does not depend
+// on the order in which the reductions land: the result is a function of the
+// inputs alone (bitwise reproducible across runs, grids and streams).
+//
+// The scale 2^F comes from a 2-word header the backward's absmax pass fills:
+// hdr[0] = bit pattern of max|attention weight| (1.0 for the fused prologue's
+// softmax weights), hdr[1] = that of max|grad_out| (an atomicMax over |x|
+// bit patterns, which order like the magnitudes). With |a| < 2^ea,
+// |g| < 2^eg, |w_c| <= 1 and at most n = Q*K contributions per row (a row
+// belongs to one level; each point of it adds at most one corner there),
+//   F = 61 - ceil(log2 n) - ea - eg
+// bounds every partial sum by 2^61 < 2^63 (F up to 252, applied as two
+// exact power-of-two factors, so tiny gradients keep their precision; below
+// that every contribution is under fp32's smallest subnormal anyway). The
+// rounding error of one
+// contribution is at most 2^-(F+1): relative to the largest possible
+// contribution 2^-(62 - ceil(log2 n)), i.e. below 2^-45 for n <= 2^17,
+// far below fp32's 2^-24 per add. Inputs with a non-finite maximum (or so
+// large that a product could overflow fp32) set `ok` false; the scatter then
+// adds fp32 contributions to the low word of each 64-bit element with
+// ordinary float atomics, which propagates Inf / NaN as fp32 accumulation
+// would (and is not order-independent -- there is no finite value to keep).
+// ---------------------------------------------------------------------------
+// Accumulator type tag: A = long long selects the fixed-point scatter.
+template <typename A>
+struct IsFixed {
+  static constexpr bool value = false;
+};
+template <>
+struct IsFixed<long long> {
+  static constexpr bool value = true;
+};
+
+struct FixedScale {
+  float s1, s2;      // 2^F = s1 * s2 (each a normal fp32 power of two)
+  float inv1, inv2;  // 2^-F = inv1 * inv2
+  bool ok;           // false: fp32 fallback (non-finite or overflowing inputs)
+};
+
+__device__ __forceinline__ FixedScale fixed_scale(const unsigned* __restrict__ hdr, int clog2n) {
+  const unsigned ua = __ldcg(hdr), ug = __ldcg(hdr + 1);
+  FixedScale fx;
+  fx.ok = ua < 0x7f800000u && ug < 0x7f800000u;
+  int F = 0;
+  if (fx.ok && ua != 0u && ug != 0u) {
+    // |x| < 2^(E - 126) for biased exponent E (denormals: below 2^-125).
+    const int ea = max((int)(ua >> 23), 1) - 126;
+    const int eg = max((int)(ug >> 23), 1) - 126;
+    if (ea + eg + clog2n > 127) fx.ok = false;  // a (merged) product could overflow fp32
+    F = min(61 - clog2n - ea - eg, 252);        // >= -66 whenever ok
+  }
+  if (!fx.ok) F = 0;
+  const int F1 = min(F, 126), F2 = F - F1;      // F1 in [-66, 126], F2 in [0, 126]
+  fx.s1 = __int_as_float((F1 + 127) << 23);
+  fx.s2 = __int_as_float((F2 + 127) << 23);
+  fx.inv1 = __int_as_float((127 - F1) << 23);
+  fx.inv2 = __int_as_float((127 - F2) << 23);
+  return fx;
+}
+
+__device__ __forceinline__ void red_fixed(long long* p, float c, const FixedScale& fx, uint64_t pol) {
+  if (fx.ok) {
+    const long long v = __float2ll_rn(c * fx.s1 * fx.s2);  // exact scaling, one rounding
+    if (v != 0)
+      asm volatile("red.global.add.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol)
+                   : "memory");
+  } else {
+    atomicAdd(reinterpret_cast<float*>(p), c);
+  }
+}
+
+// A 64-bit accumulator element -> float: the integer rounded once to fp32,
+// then scaled by the powers of two (exact unless the result is subnormal),
+// or the fallback's fp32 low word.
+__device__ __forceinline__ float fixed_to_f32(long long v, const FixedScale& fx) {
+  return fx.ok ? __ll2float_rn(v) * fx.inv1 * fx.inv2 : __int_as_float((int)(unsigned)(unsigned long long)v);
+}
+
 // Read-only 16-byte load with an L2 policy (value rows in the scatter backward).
 __device__ __forceinline__ uint4 ldg16_hint(const void* p, uint64_t pol) {
   uint4 v;

@@ -37,7 +37,12 @@ struct OpParams {
   void* grad_loc;
   void* grad_attn;
   unsigned* counts;   // counted scatter: bilinear hits per (b, pixel, m) row
-  float* acc;         // counted scatter: fp32 rows of the multi-hit rows
+  void* acc;          // counted scatter: accumulator rows of the multi-hit rows
+  int acc_words;      // 32-bit words per accumulator element: 1 (fp32), 2 (64-bit fixed point)
+  // Deterministic grad_value (64-bit fixed point): the absmax header and
+  // ceil(log2(Q*K)), the bound on contributions per row.
+  const unsigned* fixed_hdr;
+  int fixed_log2n;
   // Fused prologue (fused != 0): `loc` holds sampling offsets in level
   // pixels, `attn` attention logits (softmaxed over a query-head's L*K
   // points), `ref` reference points (B, Q, 2); the sampling location of a
@@ -273,6 +278,10 @@ template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, 
 __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS)
     msda_bwd_kernel(const OpParams p) {
   constexpr bool SCATTER = MODE != kNoScatter;
+  // A = long long: deterministic grad_value in 64-bit fixed point (see
+  // fixed_scale); the scatter target (kScatter*) or the multi-hit rows
+  // (kCounted) hold fixed-point elements.
+  constexpr bool FIXED = IsFixed<A>::value;
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
   __shared__ float fused_ga[FUSED ? WARPS : 1][FUSED ? kFusedMaxLK : 1];  // fused: dL/da per point
@@ -290,7 +299,9 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   const int64_t head_base = (b * p.S * p.M + m) * D;
   const T* vb = reinterpret_cast<const T*>(p.value) + head_base;
   A* gvb = reinterpret_cast<A*>(p.grad_value) + head_base;
-  float* accb = p.acc + head_base;                     // kCounted only
+  T* gvt = reinterpret_cast<T*>(p.grad_value) + head_base;  // kCounted: one-hit rows
+  float* accb = reinterpret_cast<float*>(p.acc) + head_base;  // kCounted, fp32 rows
+  long long* faccb = reinterpret_cast<long long*>(p.acc) + head_base;  // kCounted, fixed point
   const unsigned* cnb = p.counts + (b * p.S * p.M + m);  // kCounted: row pix at cnb[pix * M]
   const int LK = p.L * p.K;
   const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
@@ -334,13 +345,27 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   // in reduction k (0, 1) lane `sub` adds channels (k*LPR + sub)*4 .. +3, so
   // neighbouring lanes fill one sector per instruction. gq holds grad_out in
   // that order.
-  constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 &&
+  constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 && !FIXED &&
                          (MODE == kCounted || (MODE != kNoScatter && sizeof(A) == 4));
   // Same-row merging (see the scatter below): one corner item per lane needs
   // the 4 corners of a group to fit in its LPR lanes, one point per group.
   // It pays where a query's points share rows (dense, local sampling such as
   // an encoder's) and costs where they do not, so the host selects it.
   constexpr bool COMBINE = MODE == kScatterMerge && LPR >= 4 && NB == 1;
+  // Fixed-point reductions are scalar 8-byte `red`s; in reduction k lane
+  // `sub` adds channel j*LPR*VEC + k*LPR + sub, so the LPR lanes of a group
+  // fill consecutive 8-byte words. gi holds grad_out in that order.
+  float gi[FIXED ? CPL : 1][FIXED ? VEC : 1];
+  if constexpr (FIXED) {
+    const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j)
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        const int ch = j * LPR * VEC + k * LPR + sub;
+        gi[j][k] = (live && ch < D) ? to_f32(gp[ch]) : 0.f;
+      }
+  }
   float gq[QUADS ? CPL : 1][2][4];
   if constexpr (QUADS) {
     const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
@@ -382,6 +407,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
     refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
     warp_softmax_stats(ap, LK, lane, smx, sinv);
   }
+  FixedScale fx{1.f, 1.f, 1.f, 1.f, true};
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -444,6 +470,9 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
     // The value gathers above need nothing from the kernel before this one
     // (the zero-fill or the hit count); the counts and the reduction target do.
     if constexpr (SCATTER) pdl_wait();
+    if constexpr (FIXED) {
+      if (s0 == 0) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);  // written by the absmax pass
+    }
 #pragma unroll
     for (int n = 0; n < NB; ++n)
 #pragma unroll
@@ -550,6 +579,19 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
 #pragma unroll
           for (int j = 0; j < CPL; ++j) {
             const int ch = (j * LPR + sub) * VEC;
+            if constexpr (FIXED) {
+              // Fixed-point reduction in interleaved channels (see gi); a
+              // counted one-hit row is stored in the natural layout.
+              if (MODE != kCounted || hits != 1u) {
+                long long* row = (MODE == kCounted ? faccb : reinterpret_cast<long long*>(gvb)) + pix * rs;
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) {
+                  const int ci = j * LPR * VEC + k * LPR + sub;
+                  if (ci < D) red_fixed(row + ci, wc * gi[j][k], fx, pol_keep);
+                }
+                continue;
+              }
+            }
             if constexpr (QUADS) {
               // fp32 reduction in interleaved quads (see gq); a counted
               // one-hit row is stored in the natural layout.
@@ -581,10 +623,10 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
                 // (rounded once, as fp32 accumulation would); rows with
                 // more hits accumulate in fp32.
                 if (hits == 1u)
-                  store_vec<T, VEC>(reinterpret_cast<T*>(gvb) + pix * rs + ch, contrib);
-                else
+                  store_vec<T, VEC>(gvt + pix * rs + ch, contrib);
+                else if constexpr (!FIXED)
                   red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
-              } else {
+              } else if constexpr (!FIXED) {
                 red_add_vec_hint<A, VEC>(gvb + pix * rs + ch, contrib, pol_keep);
               }
             }
@@ -1151,8 +1193,8 @@ __device__ __forceinline__ int64_t dense_pixel(const LevelInfo* lv, int L, int64
   return 0;  // unreachable for r < dense pixels per batch
 }
 
-// One warp per dense pixel row (the M*D floats of all heads of one pixel):
-// flag its M counts and zero its fp32 accumulator.
+// One warp per dense pixel row (the M*D accumulator elements of all heads of
+// one pixel): flag its M counts and zero its accumulator.
 __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelInfo* lv, int64_t warp,
                                                  int64_t nwarps) {
   int64_t per_batch = 0;
@@ -1160,14 +1202,14 @@ __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelI
     if (lv[l].dense) per_batch += (int64_t)lv[l].H * lv[l].W;
   if (per_batch == 0) return;
   const int lane = threadIdx.x & 31;
-  const int64_t row_floats = (int64_t)p.M * p.D;
+  const int64_t row_floats = (int64_t)p.M * p.D * p.acc_words;  // 32-bit words
   const bool vec = row_floats % 4 == 0 && (reinterpret_cast<uintptr_t>(p.acc) & 15) == 0;
   for (int64_t px = warp; px < p.B * per_batch; px += nwarps) {
     const int64_t b = px / per_batch;
     const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
     const int64_t row0 = (b * p.S + pix) * p.M;  // first (b, pix, m) row
     for (int m = lane; m < p.M; m += 32) atomicOr(p.counts + row0 + m, kDenseRow);
-    float* a = p.acc + row0 * p.D;
+    float* a = reinterpret_cast<float*>(p.acc) + row0 * p.D * p.acc_words;
     if (vec) {
       for (int64_t k = lane; k < row_floats / 4; k += 32)
         reinterpret_cast<float4*>(a)[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1229,23 +1271,27 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   // dense blocks.
 #pragma unroll
   for (int c = 0; c < 4; ++c)
-    if (((bl.valid >> c) & 1u) && old[c] == 1u) zero_row(p.acc + row[c] * p.D, p.D);
+    if (((bl.valid >> c) & 1u) && old[c] == 1u)
+      zero_row(reinterpret_cast<float*>(p.acc) + row[c] * p.D * p.acc_words, p.D * p.acc_words);
 }
 
 // Hit-counted scatter, pass 3: rows nothing hit become zeros; multi-hit and
 // dense-level rows (count > 1, or the kDenseRow flag) are rounded from their
-// fp32 accumulator (skipped when grad_value itself is the fp32 accumulator);
-// one-hit rows were already stored by the backward.
+// accumulator -- fp32, or 64-bit fixed point (FIXED) -- (skipped when
+// grad_value itself is the fp32 accumulator); one-hit rows were already
+// stored by the backward.
 // One thread per 4 consecutive rows x VEC elements (one 16-byte count load).
-template <typename T, int VEC>
+template <typename T, int VEC, bool FIXED = false>
 __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p) {
   const int D = p.D;
   const int per_row = D / VEC;
   const int64_t rows = p.B * p.S * p.M;
   const int64_t quads = (rows + 3) / 4;
-  const bool in_place = reinterpret_cast<const void*>(p.acc) == p.grad_value;
+  const bool in_place = !FIXED && reinterpret_cast<const void*>(p.acc) == p.grad_value;
   const bool quad_loads = (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0;
-  pdl_wait();  // counts and fp32 rows come from the count pass and the backward
+  pdl_wait();  // counts and accumulator rows come from the count pass and the backward
+  FixedScale fx{1.f, 1.f, 1.f, 1.f, true};
+  if constexpr (FIXED) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < quads * per_row;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t quad = t / per_row;  // rows 4*quad .. 4*quad+3
@@ -1266,10 +1312,23 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
       if (cnt[r] == 0u) {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+      } else if constexpr (FIXED) {
+        const long long* a = reinterpret_cast<const long long*>(p.acc) + e;
+        if constexpr (VEC % 2 == 0) {
+#pragma unroll
+          for (int k = 0; k < VEC; k += 2) {
+            const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(a + k));
+            v[k] = fixed_to_f32(f.x, fx);
+            v[k + 1] = fixed_to_f32(f.y, fx);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(a + k), fx);
+        }
       } else if constexpr (VEC % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < VEC; k += 4) {
-          const float4 f = __ldcs(reinterpret_cast<const float4*>(p.acc + e + k));
+          const float4 f = __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.acc) + e + k));
           v[k] = f.x;
           v[k + 1] = f.y;
           v[k + 2] = f.z;
@@ -1277,7 +1336,7 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) v[k] = __ldcs(p.acc + e + k);
+        for (int k = 0; k < VEC; ++k) v[k] = __ldcs(reinterpret_cast<const float*>(p.acc) + e + k);
       }
       store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
     }
@@ -1316,6 +1375,88 @@ __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict_
     } else {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) v[k] = __ldcs(src + i * VEC + k);
+    }
+    store_vec<T, VEC>(dst + i * VEC, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic grad_value, pass 0: the header fixed_scale reads --
+// hdr[0] = max |attention weight| (with `logits`, the weights are a softmax,
+// at most 1: 1.0 unless a logit is non-finite), hdr[1] = max |grad_out|, as
+// fp32 bit patterns of magnitudes (NaN and Inf sort above every finite
+// value). The header is zeroed by the kernel before this one.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ unsigned abs_bits(T x) {
+  return __float_as_uint(to_f32(x)) & 0x7fffffffu;
+}
+
+// max |x| bits over p[0, n), this thread's grid-stride share: 16-byte vectors,
+// four in flight per thread, when p is 16-byte aligned.
+template <typename T>
+__device__ __forceinline__ unsigned absmax_share(const T* __restrict__ p, int64_t n) {
+  constexpr int V = 16 / (int)sizeof(T);
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  unsigned m = 0u;
+  int64_t done = 0;
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const int64_t nv = n / V;
+    const uint4* pv = reinterpret_cast<const uint4*>(p);
+    for (int64_t i = tid; i < nv; i += 4 * stride) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) r[u] = i + u * stride < nv ? __ldcs(pv + i + u * stride) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&r[u]);
+#pragma unroll
+        for (int k = 0; k < V; ++k) m = max(m, abs_bits(e[k]));
+      }
+    }
+    done = nv * V;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) m = max(m, abs_bits(p[i]));
+  return m;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) msda_absmax_kernel(const T* __restrict__ attn, int64_t n_attn,
+                                                          int logits, const T* __restrict__ g,
+                                                          int64_t n_g, unsigned* hdr) {
+  pdl_trigger();
+  unsigned ma = __reduce_max_sync(kFullMask, absmax_share(attn, n_attn));
+  const unsigned mg = __reduce_max_sync(kFullMask, absmax_share(g, n_g));
+  if (logits) ma = ma >= 0x7f800000u ? ma : 0x3f800000u;  // softmax weights: |a| <= 1
+  pdl_wait();  // the header is zeroed by the kernel before this one
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(hdr, ma);
+    atomicMax(hdr + 1, mg);
+  }
+}
+
+// Deterministic scatter, last pass: 64-bit fixed-point accumulator -> value
+// dtype (or fp32), each element rounded once.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) msda_cast_fixed_kernel(const long long* __restrict__ src,
+                                                             T* __restrict__ dst, int64_t nvec,
+                                                             const unsigned* hdr, int clog2n) {
+  pdl_wait();  // the accumulator rows come from the backward
+  const FixedScale fx = fixed_scale(hdr, clog2n);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float v[VEC];
+    if constexpr (VEC % 2 == 0) {
+#pragma unroll
+      for (int k = 0; k < VEC; k += 2) {
+        const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(src + i * VEC + k));
+        v[k] = fixed_to_f32(f.x, fx);
+        v[k + 1] = fixed_to_f32(f.y, fx);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(src + i * VEC + k), fx);
     }
     store_vec<T, VEC>(dst + i * VEC, v);
   }

@@ -43,24 +43,42 @@ constexpr int kWarpsPerCta = 8;
 
 template <typename T>
 cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st);
+
+// Accumulator of the grad_value reductions.
+enum AccKind : int {
+  kAccNative = 0,  // the value dtype (packed f16x2 / bf16x2 `red`)
+  kAccF32 = 1,     // fp32
+  kAccFixed = 2,   // 64-bit fixed point (deterministic; needs p.fixed_hdr)
+};
+
 // Backward over sampling points: grad_loc / grad_attn, plus the grad_value
 // handling `mode` (ScatterMode): kScatter (kScatterMerge: after merging a
-// warp's same-row contributions; vector path only) adds with vector `red` into
-// p.grad_value (fp32 when fp32_scatter, else the value dtype); kCounted stores
-// one-hit rows and reduces multi-hit rows into p.acc (needs the counts).
-// `pdl`: the kernel before this one in the stream is our zero-fill or hit
-// count (the backward waits for it only before its first count read /
-// reduction).
+// warp's same-row contributions; vector path only) adds into p.grad_value
+// (accumulator `acc`: fp32 for fp32 values whatever `acc` says, unless
+// kAccFixed); kCounted stores one-hit rows and reduces multi-hit rows into
+// p.acc (fp32, or fixed point with kAccFixed; needs the counts).
+// `pdl`: the kernel before this one in the stream is our zero-fill, hit
+// count or absmax pass (the backward waits for it only before its first
+// count read / reduction).
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
-                            bool pdl, cudaStream_t st);
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, bool pdl,
+                            cudaStream_t st);
 // Hit-counted scatter passes 1 (count hits, zero the accumulators that will
 // be reduced into) and 3 (zeros / downcast). p.counts must be zeroed before
 // launch_count.
 template <typename T>
 cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st);
 template <typename T>
-cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st);
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, int num_sms, cudaStream_t st);
+// Deterministic grad_value: the absmax header (pass 0; `pdl` when the kernel
+// before it is our zero-fill) and the fixed-point -> dtype pass of the
+// deterministic scatter.
+template <typename T>
+cudaError_t launch_absmax(const void* attn, int64_t n_attn, bool logits, const void* grad_out,
+                          int64_t n_g, unsigned* hdr, int num_sms, bool pdl, cudaStream_t st);
+template <typename T>
+cudaError_t launch_cast_fixed(const long long* src, T* dst, int64_t n, bool vec_ok,
+                              const unsigned* hdr, int clog2n, int num_sms, cudaStream_t st);
 
 // grad_value by pixel-chunk ownership (see msda_bwd_value_owner_kernel).
 struct OwnerPlan {
@@ -142,9 +160,29 @@ cudaError_t launch_forward(const OpParams& p, const Cfg& c, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, bool fp32_scatter,
-                            bool pdl, cudaStream_t st) {
+cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, bool pdl,
+                            cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
+  const bool fp32_scatter = acc == kAccF32;
+  if (acc == kAccFixed) {
+    using F = long long;
+    if (mode == kNoScatter) return cudaErrorNotSupported;
+    if (p.fused) {  // vector path only
+      if (c.vec != V16) return cudaErrorNotSupported;
+      if (mode == kCounted) return bwd_by_shape<T, F, V16, kCounted, true>(p, c, pdl, st);
+      return mode == kScatterMerge ? bwd_by_shape<T, F, V16, kScatterMerge, true>(p, c, pdl, st)
+                                   : bwd_by_shape<T, F, V16, kScatter, true>(p, c, pdl, st);
+    }
+    if (c.vec == V16) {
+      if (mode == kCounted) return bwd_by_shape<T, F, V16, kCounted>(p, c, pdl, st);
+      return mode == kScatterMerge ? bwd_by_shape<T, F, V16, kScatterMerge>(p, c, pdl, st)
+                                   : bwd_by_shape<T, F, V16, kScatter>(p, c, pdl, st);
+    }
+    if (c.vec == 1)
+      return mode == kCounted ? bwd_by_shape<T, F, 1, kCounted>(p, c, pdl, st)
+                              : bwd_by_shape<T, F, 1, kScatter>(p, c, pdl, st);
+    return cudaErrorInvalidConfiguration;
+  }
   if (p.fused) {  // vector path only
     if (c.vec != V16 || mode == kNoScatter) return cudaErrorNotSupported;
     if (mode == kCounted) return bwd_by_shape<T, T, V16, kCounted, true>(p, c, pdl, st);
@@ -191,7 +229,7 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
 }
 
 template <typename T>
-cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStream_t st) {
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, int num_sms, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
   const int64_t rows = p.B * p.S * p.M;
   const int vec = (vec_ok && p.D % V16 == 0 && p.D % 4 == 0) ? V16 : 1;
@@ -202,8 +240,40 @@ cudaError_t launch_finalize(const OpParams& p, bool vec_ok, int num_sms, cudaStr
   const int64_t blocks = (n + 255) / 256;
   // The backward runs right before: overlap its tail (the finalize waits).
   const dim3 grid((unsigned)std::max<int64_t>(blocks, 1));
+  if (fixed) {
+    if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16, true>, grid, dim3(256), 0, st, true, p);
+    return launch_ex(msda_finalize_kernel<T, 1, true>, grid, dim3(256), 0, st, true, p);
+  }
   if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16>, grid, dim3(256), 0, st, true, p);
   return launch_ex(msda_finalize_kernel<T, 1>, grid, dim3(256), 0, st, true, p);
+}
+
+template <typename T>
+cudaError_t launch_absmax(const void* attn, int64_t n_attn, bool logits, const void* grad_out,
+                          int64_t n_g, unsigned* hdr, int num_sms, bool pdl, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  const int64_t longest = std::max(n_attn, n_g) / V16 + 1;
+  const int64_t blocks = std::min<int64_t>((int64_t)num_sms * 4, (longest + 255) / 256);
+  return launch_ex(msda_absmax_kernel<T>, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256), 0,
+                   st, pdl, static_cast<const T*>(attn), n_attn, logits ? 1 : 0,
+                   static_cast<const T*>(grad_out), n_g, hdr);
+}
+
+template <typename T>
+cudaError_t launch_cast_fixed(const long long* src, T* dst, int64_t n, bool vec_ok,
+                              const unsigned* hdr, int clog2n, int num_sms, cudaStream_t st) {
+  constexpr int V16 = 16 / (int)sizeof(T);
+  const int64_t max_blocks = (int64_t)num_sms * 8;
+  // The backward runs right before: overlap its tail (the pass waits).
+  if (vec_ok && n % V16 == 0) {
+    const int64_t nvec = n / V16;
+    const int64_t blocks = std::min<int64_t>(max_blocks, (nvec + 255) / 256);
+    return launch_ex(msda_cast_fixed_kernel<T, V16>, dim3((unsigned)std::max<int64_t>(blocks, 1)),
+                     dim3(256), 0, st, true, src, dst, nvec, hdr, clog2n);
+  }
+  const int64_t blocks = std::min<int64_t>(max_blocks, (n + 255) / 256);
+  return launch_ex(msda_cast_fixed_kernel<T, 1>, dim3((unsigned)std::max<int64_t>(blocks, 1)), dim3(256),
+                   0, st, true, src, dst, n, hdr, clog2n);
 }
 
 template <typename T, int OVEC, int DT>
@@ -260,9 +330,11 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
 #ifdef MSDA_LAUNCH_IMPL
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
-  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, bool, bool, cudaStream_t); \
+  template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, int, bool, cudaStream_t); \
   template cudaError_t launch_count<T>(const OpParams&, int, cudaStream_t);                         \
-  template cudaError_t launch_finalize<T>(const OpParams&, bool, int, cudaStream_t);              \
+  template cudaError_t launch_finalize<T>(const OpParams&, bool, bool, int, cudaStream_t);        \
+  template cudaError_t launch_absmax<T>(const void*, int64_t, bool, const void*, int64_t, unsigned*, int, bool, cudaStream_t); \
+  template cudaError_t launch_cast_fixed<T>(const long long*, T*, int64_t, bool, const unsigned*, int, int, cudaStream_t); \
   template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);
 

@@ -26,6 +26,7 @@ MSDA_BWD_FP32_ACCUM = 1
 MSDA_BWD_FORCE_SCATTER = 2
 MSDA_BWD_FORCE_OWNER = 4
 MSDA_BWD_FORCE_COUNTED = 8
+MSDA_BWD_DETERMINISTIC = 16
 
 # Every symbol include/msda_b200.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p

@@ -43,6 +43,21 @@ def _use_fp32_grad_accum(value: torch.Tensor) -> bool:
     return value.dtype != torch.float32
 
 
+def _use_deterministic(deterministic: bool | None) -> bool:
+    """``deterministic=None`` follows ``torch.use_deterministic_algorithms``:
+    when PyTorch is asked for deterministic algorithms the backward takes the
+    library's 64-bit fixed-point grad_value accumulation (bitwise
+    reproducible) instead of raising or silently using atomics."""
+    if deterministic is None:
+        return torch.are_deterministic_algorithms_enabled()
+    return bool(deterministic)
+
+
+def _bwd_flags(fp32_grad_accum: bool, deterministic: bool, algo_flags: int) -> int:
+    return ((_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0)
+            | (_lib.MSDA_BWD_DETERMINISTIC if deterministic else 0) | algo_flags)
+
+
 def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
@@ -73,7 +88,7 @@ def _forward(value, spatial_shapes, level_start_index, sampling_locations, atten
 
 
 def _backward(value, spatial_shapes, level_start_index, sampling_locations, attention_weights,
-              grad_out, fp32_grad_accum, algo_flags=0):
+              grad_out, fp32_grad_accum, algo_flags=0, deterministic=False):
     B, S, M, D = value.shape
     _, Q, _, L, K, _ = sampling_locations.shape
     grad_value = torch.empty_like(value)
@@ -81,7 +96,7 @@ def _backward(value, spatial_shapes, level_start_index, sampling_locations, atte
     grad_attn = torch.empty_like(attention_weights)
     lib = _lib.load()
     code = _DTYPE_CODE[value.dtype]
-    flags = (_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0) | algo_flags
+    flags = _bwd_flags(fp32_grad_accum, deterministic, algo_flags)
     ws_bytes = lib.msda_backward_workspace_size(B, S, Q, M, D, L, K, code, flags)
     workspace = (
         torch.empty(ws_bytes, dtype=torch.uint8, device=value.device) if ws_bytes else None
@@ -104,11 +119,12 @@ class _MSDAFunction(torch.autograd.Function):
     level_start_index, sampling_locations, attention_weights, fp32_grad_accum)``
     on contiguous CUDA tensors with int64 shapes on the same device, returning
     ``(B, Q, M*D)``; backward returns gradients for value, sampling_locations
-    and attention_weights only."""
+    and attention_weights only. An optional 7th argument ``deterministic``
+    (default False) selects the bitwise-reproducible grad_value accumulation."""
 
     @staticmethod
     def forward(ctx, value, spatial_shapes, level_start_index, sampling_locations,
-                attention_weights, fp32_grad_accum):
+                attention_weights, fp32_grad_accum, deterministic=False):
         B, S, M, D = value.shape
         Q = sampling_locations.shape[1]
         out = _forward(value, spatial_shapes, level_start_index, sampling_locations,
@@ -116,6 +132,7 @@ class _MSDAFunction(torch.autograd.Function):
         ctx.save_for_backward(value, spatial_shapes, level_start_index,
                               sampling_locations, attention_weights)
         ctx.fp32_grad_accum = bool(fp32_grad_accum)
+        ctx.deterministic = bool(deterministic)
         return out.view(B, Q, M * D)
 
     @staticmethod
@@ -129,9 +146,9 @@ class _MSDAFunction(torch.autograd.Function):
         grad_out = grad_out.reshape(B, Q, M, D).to(value.dtype).contiguous()
         grad_value, grad_loc, grad_attn = _backward(
             value, spatial_shapes, level_start_index, sampling_locations, attention_weights,
-            grad_out, ctx.fp32_grad_accum,
+            grad_out, ctx.fp32_grad_accum, deterministic=ctx.deterministic,
         )
-        return grad_value, None, None, grad_loc, grad_attn, None
+        return grad_value, None, None, grad_loc, grad_attn, None, None
 
 
 class MultiScaleDeformableAttnFunction(torch.autograd.Function):
@@ -140,7 +157,8 @@ class MultiScaleDeformableAttnFunction(torch.autograd.Function):
     im2col_step)`` (the call made at benchmarks/modal_benchmark.py:231-233 of
     the reference). ``im2col_step`` is accepted for signature compatibility
     and ignored: the kernels need no batch chunking. grad_value uses the
-    default accumulator policy of :func:`_use_fp32_grad_accum`."""
+    default accumulator policy of :func:`_use_fp32_grad_accum`, deterministic
+    when ``torch.use_deterministic_algorithms(True)`` is in effect."""
 
     @staticmethod
     def forward(ctx, value, value_spatial_shapes, value_level_start_index,
@@ -155,6 +173,7 @@ class MultiScaleDeformableAttnFunction(torch.autograd.Function):
         out = _forward(value, shapes, starts, sampling_locations, attention_weights)
         ctx.save_for_backward(value, shapes, starts, sampling_locations, attention_weights)
         ctx.fp32_grad_accum = _use_fp32_grad_accum(value)
+        ctx.deterministic = _use_deterministic(None)
         return out.view(B, Q, M * D)
 
     @staticmethod
@@ -166,7 +185,7 @@ class MultiScaleDeformableAttnFunction(torch.autograd.Function):
         grad_out = grad_out.reshape(B, Q, M, D).to(value.dtype).contiguous()
         grad_value, grad_loc, grad_attn = _backward(
             value, shapes, starts, sampling_locations, attention_weights, grad_out,
-            ctx.fp32_grad_accum,
+            ctx.fp32_grad_accum, deterministic=ctx.deterministic,
         )
         return grad_value, None, None, grad_loc, grad_attn, None
 
@@ -179,6 +198,7 @@ def multi_scale_deformable_attention(
     attention_weights: torch.Tensor,
     *,
     fp32_grad_accum: bool | None = None,
+    deterministic: bool | None = None,
 ) -> torch.Tensor:
     """Multi-scale deformable attention (Zhu et al. 2021, Eq. 1) on B200.
 
@@ -205,13 +225,18 @@ def multi_scale_deformable_attention(
             (``False``). ``None`` picks fp32 for fp16/bf16 (see
             :func:`_use_fp32_grad_accum`); fp32 inputs always accumulate in
             fp32.
+        deterministic: accumulate ``grad_value`` in 64-bit fixed point so
+            the backward is bitwise reproducible (no counterpart in the
+            reference; ``fp32_grad_accum`` is then moot). ``None`` follows
+            ``torch.are_deterministic_algorithms_enabled()``.
 
     Returns:
         ``(B, Q, M * D)`` output in ``value.dtype``.
 
     Note:
-        ``grad_value`` is accumulated with atomics, so the backward is not
-        bitwise deterministic from run to run.
+        Unless ``deterministic``, ``grad_value`` is accumulated with fp32 (or
+        native) atomics, so the backward is not bitwise deterministic from
+        run to run (as in the reference).
     """
     if value.dim() != 4:
         raise ValueError(f"value must be (B, S, M, D), got {tuple(value.shape)}")
@@ -267,6 +292,7 @@ def multi_scale_deformable_attention(
         sampling_locations.contiguous(),
         attention_weights.contiguous(),
         fp32_grad_accum,
+        _use_deterministic(deterministic),
     )
 
 
@@ -324,7 +350,7 @@ def _forward_fused(value, spatial_shapes, level_start_index, reference_points, s
 
 
 def _backward_fused(value, spatial_shapes, level_start_index, reference_points, sampling_offsets,
-                    attention_logits, grad_out, fp32_grad_accum, algo_flags=0):
+                    attention_logits, grad_out, fp32_grad_accum, algo_flags=0, deterministic=False):
     """(grad_value, grad_offsets, grad_logits) of the fused forward."""
     B, S, M, D = value.shape
     _, Q, _, L, K, _ = sampling_offsets.shape
@@ -333,7 +359,7 @@ def _backward_fused(value, spatial_shapes, level_start_index, reference_points, 
     grad_logits = torch.empty_like(attention_logits)
     lib = _lib.load()
     code = _DTYPE_CODE[value.dtype]
-    flags = (_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0) | algo_flags
+    flags = _bwd_flags(fp32_grad_accum, deterministic, algo_flags)
     ws_bytes = lib.msda_backward_workspace_size(B, S, Q, M, D, L, K, code, flags)
     workspace = (
         torch.empty(ws_bytes, dtype=torch.uint8, device=value.device) if ws_bytes else None
@@ -354,7 +380,7 @@ class _MSDAFusedFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, value, spatial_shapes, level_start_index, reference_points, sampling_offsets,
-                attention_logits, fp32_grad_accum):
+                attention_logits, fp32_grad_accum, deterministic=False):
         B, S, M, D = value.shape
         Q = sampling_offsets.shape[1]
         out = _forward_fused(value, spatial_shapes, level_start_index, reference_points,
@@ -362,6 +388,7 @@ class _MSDAFusedFunction(torch.autograd.Function):
         ctx.save_for_backward(value, spatial_shapes, level_start_index, reference_points,
                               sampling_offsets, attention_logits)
         ctx.fp32_grad_accum = bool(fp32_grad_accum)
+        ctx.deterministic = bool(deterministic)
         return out.view(B, Q, M * D)
 
     @staticmethod
@@ -374,14 +401,15 @@ class _MSDAFusedFunction(torch.autograd.Function):
         if grad_out.data_ptr() % 16:  # the fused kernels read 16-byte vectors
             grad_out = grad_out.clone()
         grad_value, grad_off, grad_logits = _backward_fused(
-            value, shapes, starts, ref, off, logits, grad_out, ctx.fp32_grad_accum)
+            value, shapes, starts, ref, off, logits, grad_out, ctx.fp32_grad_accum,
+            deterministic=ctx.deterministic)
         grad_ref = None
         if ctx.needs_input_grad[3]:
             # location = ref + offset / (W_l, H_l): d/dref = sum over (m, l, k)
             # of d/doffset * (W_l, H_l).
             wh = shapes.flip(-1).to(torch.float32)  # (L, 2)
             grad_ref = (grad_off.float() * wh[:, None, :]).sum(dim=(2, 3, 4)).to(ref.dtype)
-        return grad_value, None, None, grad_ref, grad_off, grad_logits, None
+        return grad_value, None, None, grad_ref, grad_off, grad_logits, None, None
 
 
 def multi_scale_deformable_attention_fused(
@@ -393,6 +421,7 @@ def multi_scale_deformable_attention_fused(
     attention_logits: torch.Tensor,
     *,
     fp32_grad_accum: bool | None = None,
+    deterministic: bool | None = None,
 ) -> torch.Tensor:
     """Multi-scale deformable attention with the Deformable-DETR layer's
     prologue fused in (the prologue of the reference's layer,
@@ -411,7 +440,8 @@ def multi_scale_deformable_attention_fused(
         sampling_offsets: ``(B, Q, M, L, K, 2)`` in pixels of each level.
         attention_logits: ``(B, Q, M, L, K)``, softmaxed jointly over
             ``(L, K)`` per query and head.
-        fp32_grad_accum: as in :func:`multi_scale_deformable_attention`.
+        fp32_grad_accum, deterministic: as in
+            :func:`multi_scale_deformable_attention`.
 
     Returns:
         ``(B, Q, M * D)`` in ``value.dtype``; differentiable with respect to
@@ -459,8 +489,10 @@ def multi_scale_deformable_attention_fused(
         locations = reference_points[:, :, None, None, None, :] + sampling_offsets / wh[:, None, :]
         weights = attention_logits.reshape(B, Q, M, L * K).softmax(-1).view(B, Q, M, L, K)
         return multi_scale_deformable_attention(value, spatial_shapes, level_start_index,
-                                                locations, weights, fp32_grad_accum=fp32_grad_accum)
+                                                locations, weights, fp32_grad_accum=fp32_grad_accum,
+                                                deterministic=deterministic)
     return _MSDAFusedFunction.apply(
         value.contiguous(), spatial_shapes, level_start_index, reference_points.contiguous(),
         sampling_offsets.contiguous(), attention_logits.contiguous(), fp32_grad_accum,
+        _use_deterministic(deterministic),
     )

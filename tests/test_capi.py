@@ -101,6 +101,54 @@ def test_abi_workspace_size():
     assert ws(1, 10, 20000, 1, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 10 * 8 * 4
 
 
+def test_abi_workspace_size_deterministic():
+    """Deterministic grad_value: a 256-byte absmax header, then 64-bit
+    fixed-point rows -- for every grad_value element (scatter, dense
+    sampling) or behind the per-row counts (hit-counted, sparse sampling),
+    whatever the dtype and fp32_grad_accum."""
+    lib = _lib.load()
+    d = _lib.MSDA_BWD_DETERMINISTIC
+    ws = lambda Q, dt, fl: lib.msda_backward_workspace_size(2, 10, Q, 3, 8, 1, 4, dt, fl)  # noqa: E731
+    elems = 2 * 10 * 3 * 8
+    scatter = 256 + elems * 8
+    counted = 256 + 256 + elems * 8
+    for dt in (_lib.MSDA_DTYPE_F32, _lib.MSDA_DTYPE_F16, _lib.MSDA_DTYPE_BF16):
+        for f in (0, _lib.MSDA_BWD_FP32_ACCUM):
+            assert ws(50, dt, d | f) == scatter
+            assert ws(2, dt, d | f) == counted
+            assert ws(2, dt, d | f | _lib.MSDA_BWD_FORCE_SCATTER) == scatter
+            assert ws(50, dt, d | f | _lib.MSDA_BWD_FORCE_COUNTED) == counted
+
+
+def test_abi_deterministic_flag_checks():
+    text = HEADER.read_text()
+    assert re.search(r"#define MSDA_BWD_DETERMINISTIC (\d+)u", text).group(1) == str(_lib.MSDA_BWD_DETERMINISTIC)
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    call = lambda flags, ws=0: lib.msda_backward(  # noqa: E731
+        vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16),
+        vp(ws), 0, 1, 4, 1, 1, 8, 1, 1, _lib.MSDA_DTYPE_BF16, flags, vp(0))
+    # The owner algorithm is not a deterministic one: the combination is refused.
+    assert call(_lib.MSDA_BWD_DETERMINISTIC | _lib.MSDA_BWD_FORCE_OWNER) == _lib.MSDA_ERR_UNSUPPORTED
+    assert b"exclusive" in lib.msda_last_error()
+    # The fixed-point accumulator lives in the workspace.
+    assert call(_lib.MSDA_BWD_DETERMINISTIC) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert b"deterministic" in lib.msda_last_error()
+
+
+def test_deterministic_option_follows_torch_flag():
+    from msda_triton_b200.ops import _use_deterministic
+    assert _use_deterministic(True) and not _use_deterministic(False)
+    before = torch.are_deterministic_algorithms_enabled()
+    try:
+        torch.use_deterministic_algorithms(True)
+        assert _use_deterministic(None)
+        torch.use_deterministic_algorithms(False)
+        assert not _use_deterministic(None)
+    finally:
+        torch.use_deterministic_algorithms(before)
+
+
 def test_abi_backward_needs_workspace_for_fp32_accumulation():
     lib = _lib.load()
     vp = ctypes.c_void_p
