@@ -319,18 +319,30 @@ __device__ __forceinline__ void red_add_vec_hint(A* p, const float (&v)[VEC], ui
 // bit patterns, which order like the magnitudes). With |a| < 2^ea,
 // |g| < 2^eg, |w_c| <= 1 and at most n = Q*K contributions per row (a row
 // belongs to one level; each point of it adds at most one corner there),
-//   F = 61 - ceil(log2 n) - ea - eg
-// bounds every partial sum by 2^61 < 2^63 (F up to 252, applied as two
-// exact power-of-two factors, so tiny gradients keep their precision; below
-// that every contribution is under fp32's smallest subnormal anyway). The
-// rounding error of one
-// contribution is at most 2^-(F+1): relative to the largest possible
-// contribution 2^-(62 - ceil(log2 n)), i.e. below 2^-45 for n <= 2^17,
-// far below fp32's 2^-24 per add. Inputs with a non-finite maximum (or so
-// large that a product could overflow fp32) set `ok` false; the scatter then
-// adds fp32 contributions to the low word of each 64-bit element with
-// ordinary float atomics, which propagates Inf / NaN as fp32 accumulation
-// would (and is not order-independent -- there is no finite value to keep).
+//   F = 49 - ceil(log2 n) - ea - eg
+// bounds every scaled contribution by 2^(49 - ceil(log2 n)) and every row
+// sum by 2^49.
+//
+// Rounding without a float-to-integer conversion: the weight a * w_c is
+// widened to fp64 and scaled by 2^F once per corner (exact in fp64's range),
+// and each element is one
+//   t = fma(a * w_c * 2^F, g, 1.5 * 2^52)
+// -- the exact product rounded once to an integer v (fp64's ulp is 1 on
+// [2^52, 2^53), and |product| < 2^51 keeps t there), read back as
+// v = bits(t) - bits(1.5 * 2^52). The rounding error of one contribution is
+// at most 2^-(F+1): relative to the largest possible contribution,
+// 2^-(50 - ceil(log2 n)), i.e. below 2^-33 for n <= 2^17 -- finer than one
+// fp32 add (2^-24), and of the exact product rather than an fp32-rounded
+// one. A row sum is rounded once to fp32 and scaled by 2^-F as two fp32
+// powers of two (exact unless the result is below fp32's normal range; an F
+// beyond 252, i.e. max|a| * max|g| < 2^-203, leaves only underflowing
+// results).
+//
+// Inputs with a non-finite maximum (or an attention weight so large that a
+// merged fp32 weight could overflow) set `ok` false: the scatter then adds
+// fp32 contributions to the low word of each 64-bit element with ordinary
+// float atomics, which puts Inf / NaN where fp32 accumulation would (and is
+// not order-independent -- there is no finite value to keep).
 // ---------------------------------------------------------------------------
 // Accumulator type tag: A = long long selects the fixed-point scatter.
 template <typename A>
@@ -342,8 +354,11 @@ struct IsFixed<long long> {
   static constexpr bool value = true;
 };
 
+constexpr double kFixedMagic = 6755399441055744.0;  // 1.5 * 2^52
+constexpr long long kFixedMagicBits = 0x4338000000000000ll;
+
 struct FixedScale {
-  float s1, s2;      // 2^F = s1 * s2 (each a normal fp32 power of two)
+  double scale;      // 2^F
   float inv1, inv2;  // 2^-F = inv1 * inv2
   bool ok;           // false: fp32 fallback (non-finite or overflowing inputs)
 };
@@ -357,34 +372,29 @@ __device__ __forceinline__ FixedScale fixed_scale(const unsigned* __restrict__ h
     // |x| < 2^(E - 126) for biased exponent E (denormals: below 2^-125).
     const int ea = max((int)(ua >> 23), 1) - 126;
     const int eg = max((int)(ug >> 23), 1) - 126;
-    if (ea + eg + clog2n > 127) fx.ok = false;  // a (merged) product could overflow fp32
-    F = min(61 - clog2n - ea - eg, 252);        // >= -66 whenever ok
+    if (ea + clog2n > 127) fx.ok = false;  // a merged fp32 weight sum could overflow
+    F = 49 - clog2n - ea - eg;             // in [-247, 300]: a normal fp64 power of two
   }
   if (!fx.ok) F = 0;
-  const int F1 = min(F, 126), F2 = F - F1;      // F1 in [-66, 126], F2 in [0, 126]
-  fx.s1 = __int_as_float((F1 + 127) << 23);
-  fx.s2 = __int_as_float((F2 + 127) << 23);
+  fx.scale = __longlong_as_double((long long)(1023 + F) << 52);
+  const int F1 = min(max(F, -126), 126), F2 = min(max(F - F1, -126), 126);
   fx.inv1 = __int_as_float((127 - F1) << 23);
   fx.inv2 = __int_as_float((127 - F2) << 23);
   return fx;
 }
 
-__device__ __forceinline__ void red_fixed(long long* p, float c, const FixedScale& fx, uint64_t pol) {
-  if (fx.ok) {
-    const long long v = __float2ll_rn(c * fx.s1 * fx.s2);  // exact scaling, one rounding
-    if (v != 0)
-      asm volatile("red.global.add.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol)
-                   : "memory");
-  } else {
-    atomicAdd(reinterpret_cast<float*>(p), c);
-  }
+// Adds round(wd * gd) to a 64-bit element (wd = the corner weight
+// a * w_c * 2^F in fp64, gd = g); zero contributions are skipped.
+__device__ __forceinline__ void red_fixed(long long* p, double wd, double gd, uint64_t pol) {
+  const long long v = __double_as_longlong(fma(wd, gd, kFixedMagic)) - kFixedMagicBits;
+  if (v != 0)
+    asm volatile("red.global.add.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol) : "memory");
 }
 
-// A 64-bit accumulator element -> float: the integer rounded once to fp32,
-// then scaled by the powers of two (exact unless the result is subnormal),
-// or the fallback's fp32 low word.
+// A 64-bit accumulator element -> float (or the fallback's fp32 low word).
 __device__ __forceinline__ float fixed_to_f32(long long v, const FixedScale& fx) {
-  return fx.ok ? __ll2float_rn(v) * fx.inv1 * fx.inv2 : __int_as_float((int)(unsigned)(unsigned long long)v);
+  if (!fx.ok) return __int_as_float((int)(unsigned)(unsigned long long)v);
+  return __ll2float_rn(v) * fx.inv1 * fx.inv2;
 }
 
 // Read-only 16-byte load with an L2 policy (value rows in the scatter backward).

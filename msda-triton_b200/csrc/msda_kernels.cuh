@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
     refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
     warp_softmax_stats(ap, LK, lane, smx, sinv);
   }
-  FixedScale fx{1.f, 1.f, 1.f, 1.f, true};
+  FixedScale fx{1.0, 1.f, 1.f, true};
 
   for (int s0 = 0; s0 < LK; s0 += G * NB) {
     Bilinear bl[NB];
@@ -584,10 +584,19 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
               // counted one-hit row is stored in the natural layout.
               if (MODE != kCounted || hits != 1u) {
                 long long* row = (MODE == kCounted ? faccb : reinterpret_cast<long long*>(gvb)) + pix * rs;
+                if (fx.ok) {
+                  const double wd = (double)wc * fx.scale;  // exact
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) {
-                  const int ci = j * LPR * VEC + k * LPR + sub;
-                  if (ci < D) red_fixed(row + ci, wc * gi[j][k], fx, pol_keep);
+                  for (int k = 0; k < VEC; ++k) {
+                    const int ci = j * LPR * VEC + k * LPR + sub;
+                    if (ci < D) red_fixed(row + ci, wd, (double)gi[j][k], pol_keep);
+                  }
+                } else {  // fp32 fallback into the low words
+#pragma unroll
+                  for (int k = 0; k < VEC; ++k) {
+                    const int ci = j * LPR * VEC + k * LPR + sub;
+                    if (ci < D) atomicAdd(reinterpret_cast<float*>(row + ci), wc * gi[j][k]);
+                  }
                 }
                 continue;
               }
@@ -1290,7 +1299,7 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
   const bool in_place = !FIXED && reinterpret_cast<const void*>(p.acc) == p.grad_value;
   const bool quad_loads = (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0;
   pdl_wait();  // counts and accumulator rows come from the count pass and the backward
-  FixedScale fx{1.f, 1.f, 1.f, 1.f, true};
+  FixedScale fx{1.0, 1.f, 1.f, true};
   if constexpr (FIXED) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < quads * per_row;
        t += (int64_t)gridDim.x * blockDim.x) {
