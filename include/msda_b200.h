@@ -224,6 +224,57 @@ MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_sha
                                    int32_t num_levels, int32_t num_points, int32_t dtype,
                                    void* stream);
 
+/*
+ * Sibling gathers (no counterpart in the reference, which names them as the
+ * operators its recipe transfers to, docs/course/08-exercises.md:39): the
+ * same channel-vector bilinear gathers and scatters, for grid_sample and
+ * ROI-Align. Channels-last (NHWC) layouts, all in `dtype` unless stated:
+ *   input        (N, H, W, C)
+ *   grid         (N, out_h, out_w, 2)   normalised (x, y) in [-1, 1]
+ *   output       (N, out_h, out_w, C)   grid_sample
+ *   rois         (num_rois, 5) fp32     (batch index, x1, y1, x2, y2)
+ *   output       (num_rois, pooled_height, pooled_width, C)   roi_align
+ * Backward flags: MSDA_BWD_FP32_ACCUM (fp32 workspace + downcast for
+ * fp16/bf16), MSDA_BWD_DETERMINISTIC (grid_sample only: 64-bit fixed-point
+ * accumulation, bitwise reproducible); the workspace size depends on them.
+ * grad_input need not be zeroed by the caller.
+ */
+
+/* torch.nn.functional.grid_sample(input, grid, mode="bilinear",
+ * padding_mode, align_corners) on NHWC data; padding_mode 0 = "zeros",
+ * 1 = "border" ("reflection" is not supported: MSDA_ERR_UNSUPPORTED). */
+MSDA_API int msda_grid_sample_forward(const void* input, const void* grid, void* output, int64_t N,
+                                      int64_t H, int64_t W, int64_t C, int64_t out_h, int64_t out_w,
+                                      int32_t padding_mode, int32_t align_corners, int32_t dtype,
+                                      void* stream);
+MSDA_API size_t msda_grid_sample_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                         int64_t out_h, int64_t out_w, int32_t dtype,
+                                                         uint32_t flags);
+/* grad_input (N, H, W, C) and grad_grid (N, out_h, out_w, 2). */
+MSDA_API int msda_grid_sample_backward(const void* input, const void* grid, const void* grad_output,
+                                       void* grad_input, void* grad_grid, void* workspace,
+                                       size_t workspace_bytes, int64_t N, int64_t H, int64_t W,
+                                       int64_t C, int64_t out_h, int64_t out_w, int32_t padding_mode,
+                                       int32_t align_corners, int32_t dtype, uint32_t flags,
+                                       void* stream);
+
+/* torchvision.ops.roi_align(input, rois, (pooled_height, pooled_width),
+ * spatial_scale, sampling_ratio, aligned) on NHWC data. An ROI whose batch
+ * index is outside [0, N) yields zeros. */
+MSDA_API int msda_roi_align_forward(const void* input, const float* rois, void* output, int64_t N,
+                                    int64_t H, int64_t W, int64_t C, int64_t num_rois,
+                                    int32_t pooled_height, int32_t pooled_width, float spatial_scale,
+                                    int32_t sampling_ratio, int32_t aligned, int32_t dtype,
+                                    void* stream);
+MSDA_API size_t msda_roi_align_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C,
+                                                       int32_t dtype, uint32_t flags);
+/* grad_input (N, H, W, C); the boxes get no gradient (as in torchvision). */
+MSDA_API int msda_roi_align_backward(const float* rois, const void* grad_output, void* grad_input,
+                                     void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
+                                     int64_t W, int64_t C, int64_t num_rois, int32_t pooled_height,
+                                     int32_t pooled_width, float spatial_scale, int32_t sampling_ratio,
+                                     int32_t aligned, int32_t dtype, uint32_t flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,47 +5,14 @@
 #include <string>
 
 #include "msda_b200.h"
+#include "msda_abi.cuh"
 #include "msda_launch.cuh"
 
 namespace {
 
+using namespace msda::abi;
+
 thread_local std::string g_last_error;
-
-int fail(int code, const char* fmt, ...) {
-  char buf[512];
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(buf, sizeof(buf), fmt, ap);
-  va_end(ap);
-  g_last_error = buf;
-  return code;
-}
-
-int succeed() {
-  g_last_error.clear();
-  return MSDA_OK;
-}
-
-int cuda_fail(cudaError_t e, const char* what) {
-  return fail(MSDA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
-}
-
-int elem_size(int32_t dtype) {
-  switch (dtype) {
-    case MSDA_DTYPE_F32: return 4;
-    case MSDA_DTYPE_F16: return 2;
-    case MSDA_DTYPE_BF16: return 2;
-    default: return 0;
-  }
-}
-
-bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
-
-int next_pow2(int x) {
-  int p = 1;
-  while (p < x) p <<= 1;
-  return p;
-}
 
 // Largest pixel-index range the kernels address with 32-bit level arithmetic.
 constexpr int64_t kMaxS = int64_t(1) << 30;
@@ -70,26 +37,6 @@ int check_shape(const Shape& s, int32_t dtype) {
   // Grid (ceil(Q / 8), M, B): y and z are limited to 65535.
   if (s.B > 65535 || s.M > 65535)
     return fail(MSDA_ERR_UNSUPPORTED, "batch (%lld) and num_heads (%d) must be <= 65535", (long long)s.B, s.M);
-  return MSDA_OK;
-}
-
-// Picks the lane layout for a head dim. `vec_ptrs_aligned` says whether every
-// buffer read or written in D-chunks is 16-byte aligned.
-int choose_cfg(int32_t D, int es, bool vec_ptrs_aligned, msda::Cfg* c) {
-  const int v16 = 16 / es;
-  c->short_grid = false;
-  if ((D % v16) == 0 && vec_ptrs_aligned) {
-    c->vec = v16;
-  } else {
-    c->vec = 1;
-  }
-  const int nc = D / c->vec;
-  c->lpr = next_pow2(nc < 32 ? nc : 32);
-  c->cpl = (nc + c->lpr - 1) / c->lpr;
-  if (c->cpl == 3) c->cpl = 4;
-  if (c->cpl > 4)
-    return fail(MSDA_ERR_UNSUPPORTED, "head_dim=%d too large for the %s path (max %d)", D,
-                c->vec > 1 ? "vector" : "scalar", 128 * c->vec);
   return MSDA_OK;
 }
 
@@ -137,7 +84,6 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
   return scatter;
 }
 
-size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Deterministic (fixed-point) algorithms: the workspace starts with the
 // absmax header (2 words, padded).
@@ -157,19 +103,6 @@ size_t counted_ws_bytes(const Shape& s, int32_t dtype, bool fixed, size_t* count
   if (fixed) return head + counts + rows * (size_t)s.D * sizeof(long long);
   if (dtype == MSDA_DTYPE_F32) return counts;
   return counts + rows * (size_t)s.D * sizeof(float);
-}
-
-// ceil(log2(n)) for n >= 1.
-int ceil_log2(int64_t n) {
-  int r = 0;
-  while (r < 62 && ((int64_t)1 << r) < n) ++r;
-  return r;
-}
-
-int sm_count() {
-  int dev = 0, n = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n;
 }
 
 }  // namespace

@@ -64,6 +64,28 @@ SIGNATURES = {
         [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
          _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _VP],
     ),
+    # Sibling gathers on NHWC data: grid_sample and ROI-Align.
+    "msda_grid_sample_forward": (
+        ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _VP]),
+    "msda_grid_sample_backward_workspace_size": (
+        ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64, _I32, ctypes.c_uint32]),
+    "msda_grid_sample_backward": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64, _I64,
+         _I32, _I32, _I32, ctypes.c_uint32, _VP],
+    ),
+    "msda_roi_align_forward": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I32, _I32, ctypes.c_float, _I32, _I32,
+         _I32, _VP],
+    ),
+    "msda_roi_align_backward_workspace_size": (
+        ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I32, ctypes.c_uint32]),
+    "msda_roi_align_backward": (
+        ctypes.c_int,
+        [_VP, _VP, _VP, _VP, ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
+         ctypes.c_float, _I32, _I32, _I32, ctypes.c_uint32, _VP],
+    ),
 }
 
 # Size of the static scratch behind msda_backward_noalloc

@@ -1,0 +1,251 @@
+"""Sibling gathers on the B200 kernels: ``grid_sample`` and ``roi_align``.
+
+The reference names these as the operators its recipe transfers to
+(docs/course/08-exercises.md:39: "ROI-Align, grid_sample itself ... share
+MSDA's anatomy: data-dependent bilinear gathers forward, atomic scatters
+backward"). Both run on the MSDA kernel skeleton in channels-last layout
+(csrc/msda_gather.cuh) through the C ABI of include/msda_b200.h, and are
+drop-ins for the public operators they replace:
+
+* :func:`grid_sample` for ``torch.nn.functional.grid_sample`` (4-D input,
+  ``mode="bilinear"``, ``padding_mode`` "zeros" or "border");
+* :func:`roi_align` for ``torchvision.ops.roi_align``.
+
+The kernels read and write NHWC: an input already in ``torch.channels_last``
+memory format is used as is (otherwise it is copied once), and the outputs
+are returned as channels-last NCHW tensors (same shape and values as the
+replaced operators, a different memory format). There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from . import _lib
+from .ops import _DTYPE_CODE, _FLOAT_DTYPES, _device_guard, _ptr, _stream, _use_deterministic
+
+_PADDING = {"zeros": 0, "border": 1}
+
+
+def _nhwc(x: torch.Tensor) -> torch.Tensor:
+    """(N, C, H, W) -> contiguous (N, H, W, C) (a view for channels_last input)."""
+    return x.permute(0, 2, 3, 1).contiguous()
+
+
+def _bwd_flags(dtype, fp32_grad_accum, deterministic):
+    if fp32_grad_accum is None:
+        fp32_grad_accum = dtype != torch.float32
+    return ((_lib.MSDA_BWD_FP32_ACCUM if fp32_grad_accum else 0)
+            | (_lib.MSDA_BWD_DETERMINISTIC if deterministic else 0))
+
+
+def _workspace(nbytes, device):
+    return torch.empty(nbytes, dtype=torch.uint8, device=device) if nbytes else None
+
+
+# ---------------------------------------------------------------------------
+# grid_sample
+# ---------------------------------------------------------------------------
+class _GridSampleFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, grid, padding, align, flags):
+        N, H, W, C = x.shape
+        _, Ho, Wo, _ = grid.shape
+        out = x.new_empty(N, Ho, Wo, C)
+        lib = _lib.load()
+        with _device_guard(x.device):
+            rc = lib.msda_grid_sample_forward(_ptr(x), _ptr(grid), _ptr(out), N, H, W, C, Ho, Wo,
+                                              padding, int(align), _DTYPE_CODE[x.dtype],
+                                              _stream(x.device))
+        _lib.check("msda_grid_sample_forward", rc)
+        ctx.save_for_backward(x, grid)
+        ctx.cfg = (padding, align, flags)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_out):
+        x, grid = ctx.saved_tensors
+        padding, align, flags = ctx.cfg
+        N, H, W, C = x.shape
+        _, Ho, Wo, _ = grid.shape
+        grad_out = grad_out.to(x.dtype).contiguous()
+        grad_in = torch.empty_like(x)
+        grad_grid = torch.empty_like(grid)
+        lib = _lib.load()
+        code = _DTYPE_CODE[x.dtype]
+        nbytes = lib.msda_grid_sample_backward_workspace_size(N, H, W, C, Ho, Wo, code, flags)
+        ws = _workspace(nbytes, x.device)
+        with _device_guard(x.device):
+            rc = lib.msda_grid_sample_backward(
+                _ptr(x), _ptr(grid), _ptr(grad_out), _ptr(grad_in), _ptr(grad_grid), _ptr(ws), nbytes,
+                N, H, W, C, Ho, Wo, padding, int(align), code, flags, _stream(x.device))
+        _lib.check("msda_grid_sample_backward", rc)
+        return grad_in, grad_grid, None, None, None
+
+
+def grid_sample(
+    input: torch.Tensor,
+    grid: torch.Tensor,
+    mode: str = "bilinear",
+    padding_mode: str = "zeros",
+    align_corners: bool | None = None,
+    *,
+    fp32_grad_accum: bool | None = None,
+    deterministic: bool | None = None,
+) -> torch.Tensor:
+    """``torch.nn.functional.grid_sample`` for 4-D input on B200.
+
+    Args:
+        input: ``(N, C, H, W)``; channels-last memory avoids a copy.
+        grid: ``(N, H_out, W_out, 2)`` normalised ``(x, y)`` in ``[-1, 1]``.
+        mode: ``"bilinear"`` (``"nearest"`` / ``"bicubic"`` are not built).
+        padding_mode: ``"zeros"`` or ``"border"`` (``"reflection"`` is not
+            built).
+        align_corners: as in torch; ``None`` means ``False``.
+        fp32_grad_accum: accumulate the input gradient in fp32 (default for
+            fp16/bf16) or with native half-precision atomics.
+        deterministic: bitwise-reproducible input gradient (64-bit
+            fixed-point accumulation); ``None`` follows
+            ``torch.are_deterministic_algorithms_enabled()``.
+
+    Returns:
+        ``(N, C, H_out, W_out)`` in ``input.dtype``, channels-last memory.
+    """
+    if input.dim() != 4:
+        raise ValueError(f"grid_sample: only 4-D input (N, C, H, W) is supported, got {input.dim()}-D")
+    if grid.dim() != 4 or grid.shape[-1] != 2 or grid.shape[0] != input.shape[0]:
+        raise ValueError(f"grid_sample: grid must be (N, H_out, W_out, 2) with N={input.shape[0]}, "
+                         f"got {tuple(grid.shape)}")
+    if mode not in ("bilinear", "nearest", "bicubic"):
+        raise ValueError(f"grid_sample: expected mode to be 'bilinear', 'nearest' or 'bicubic', got '{mode}'")
+    if mode != "bilinear":
+        raise NotImplementedError(f"grid_sample: mode='{mode}' is not built (bilinear only)")
+    if padding_mode not in ("zeros", "border", "reflection"):
+        raise ValueError("grid_sample: expected padding_mode to be 'zeros', 'border' or 'reflection', "
+                         f"got '{padding_mode}'")
+    if padding_mode == "reflection":
+        raise NotImplementedError("grid_sample: padding_mode='reflection' is not built")
+    if input.dtype != grid.dtype:
+        raise ValueError(f"grid_sample: input and grid dtypes must match, got {input.dtype}/{grid.dtype}")
+    if input.dtype not in _FLOAT_DTYPES:
+        raise ValueError(f"grid_sample: unsupported dtype {input.dtype}; use fp32, fp16 or bf16")
+    if input.device.type != "cuda" or grid.device != input.device:
+        raise ValueError("grid_sample: input and grid must be CUDA tensors on the same device")
+    if input.shape[2] < 1 or input.shape[3] < 1 or input.shape[1] < 1:
+        raise ValueError(f"grid_sample: empty input {tuple(input.shape)}")
+    _lib.load()
+    flags = _bwd_flags(input.dtype, fp32_grad_accum, _use_deterministic(deterministic))
+    out = _GridSampleFunction.apply(_nhwc(input), grid.contiguous(), _PADDING[padding_mode],
+                                    bool(align_corners), flags)
+    return out.permute(0, 3, 1, 2)
+
+
+# ---------------------------------------------------------------------------
+# roi_align
+# ---------------------------------------------------------------------------
+def _check_boxes(boxes) -> None:
+    if isinstance(boxes, (list, tuple)):
+        for b in boxes:
+            if b.dim() != 2 or b.shape[1] != 4:
+                raise ValueError(f"roi_align: each box tensor must be (L, 4), got {tuple(b.shape)}")
+    elif boxes.dim() != 2 or boxes.shape[1] != 5:
+        raise ValueError(f"roi_align: boxes must be a (K, 5) tensor or a list of (L, 4) tensors, "
+                         f"got {tuple(boxes.shape)}")
+
+
+def _rois(boxes, device) -> torch.Tensor:
+    """torchvision's box formats -> (K, 5) fp32 (batch index, x1, y1, x2, y2)."""
+    if isinstance(boxes, (list, tuple)):
+        parts = [torch.cat([torch.full((b.shape[0], 1), float(i), dtype=torch.float32, device=b.device),
+                            b.float()], 1) for i, b in enumerate(boxes)]
+        rois = torch.cat(parts, 0) if parts else torch.zeros(0, 5)
+    else:
+        rois = boxes.float()
+    return rois.to(device).contiguous()
+
+
+class _RoiAlignFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, rois, out_hw, spatial_scale, sampling_ratio, aligned, flags):
+        N, H, W, C = x.shape
+        K = rois.shape[0]
+        PH, PW = out_hw
+        out = x.new_empty(K, PH, PW, C)
+        lib = _lib.load()
+        with _device_guard(x.device):
+            rc = lib.msda_roi_align_forward(_ptr(x), _ptr(rois), _ptr(out), N, H, W, C, K, PH, PW,
+                                            float(spatial_scale), int(sampling_ratio), int(aligned),
+                                            _DTYPE_CODE[x.dtype], _stream(x.device))
+        _lib.check("msda_roi_align_forward", rc)
+        ctx.save_for_backward(rois)
+        ctx.cfg = (tuple(x.shape), x.dtype, out_hw, spatial_scale, sampling_ratio, aligned, flags)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_out):
+        (rois,) = ctx.saved_tensors
+        shape, dtype, (PH, PW), spatial_scale, sampling_ratio, aligned, flags = ctx.cfg
+        if torch.are_deterministic_algorithms_enabled():
+            raise RuntimeError("roi_align backward has no deterministic implementation (as in "
+                               "torchvision); disable torch.use_deterministic_algorithms for it")
+        N, H, W, C = shape
+        grad_out = grad_out.to(dtype).contiguous()
+        grad_in = grad_out.new_empty(shape)
+        lib = _lib.load()
+        code = _DTYPE_CODE[dtype]
+        nbytes = lib.msda_roi_align_backward_workspace_size(N, H, W, C, code, flags)
+        ws = _workspace(nbytes, grad_out.device)
+        with _device_guard(grad_out.device):
+            rc = lib.msda_roi_align_backward(
+                _ptr(rois), _ptr(grad_out), _ptr(grad_in), _ptr(ws), nbytes, N, H, W, C, rois.shape[0],
+                PH, PW, float(spatial_scale), int(sampling_ratio), int(aligned), code, flags,
+                _stream(grad_out.device))
+        _lib.check("msda_roi_align_backward", rc)
+        return grad_in, None, None, None, None, None, None
+
+
+def roi_align(
+    input: torch.Tensor,
+    boxes,
+    output_size,
+    spatial_scale: float = 1.0,
+    sampling_ratio: int = -1,
+    aligned: bool = False,
+    *,
+    fp32_grad_accum: bool | None = None,
+) -> torch.Tensor:
+    """``torchvision.ops.roi_align`` on B200.
+
+    Args:
+        input: ``(N, C, H, W)``; channels-last memory avoids a copy.
+        boxes: ``(K, 5)`` tensor of ``(batch index, x1, y1, x2, y2)`` or a
+            list of per-image ``(L, 4)`` tensors (torchvision's formats);
+            coordinates are used in fp32.
+        output_size: ``int`` or ``(height, width)`` of the pooled output.
+        spatial_scale, sampling_ratio, aligned: as in torchvision.
+        fp32_grad_accum: accumulate the input gradient in fp32 (default for
+            fp16/bf16) or with native half-precision atomics.
+
+    Returns:
+        ``(K, C, height, width)`` in ``input.dtype``, channels-last memory.
+        Differentiable with respect to ``input`` only.
+    """
+    if input.dim() != 4:
+        raise ValueError(f"roi_align: input must be (N, C, H, W), got {input.dim()}-D")
+    _check_boxes(boxes)
+    if input.dtype not in _FLOAT_DTYPES:
+        raise ValueError(f"roi_align: unsupported dtype {input.dtype}; use fp32, fp16 or bf16")
+    if input.device.type != "cuda":
+        raise ValueError("roi_align: input must be a CUDA tensor")
+    out_hw = (output_size, output_size) if isinstance(output_size, int) else tuple(int(v) for v in output_size)
+    if len(out_hw) != 2 or min(out_hw) < 1:
+        raise ValueError(f"roi_align: output_size must be an int or (height, width) >= 1, got {output_size}")
+    _lib.load()
+    rois = _rois(boxes, input.device)
+    flags = _bwd_flags(input.dtype, fp32_grad_accum, False)
+    out = _RoiAlignFunction.apply(_nhwc(input), rois, out_hw, float(spatial_scale), int(sampling_ratio),
+                                  bool(aligned), flags)
+    return out.permute(0, 3, 1, 2)

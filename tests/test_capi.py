@@ -28,7 +28,11 @@ def test_header_declares_the_abi():
     assert set(_declared()) == {"msda_version", "msda_last_error", "msda_forward",
                                 "msda_backward_workspace_size", "msda_backward",
                                 "msda_backward_noalloc", "msda_forward_fused",
-                                "msda_backward_fused"}
+                                "msda_backward_fused", "msda_grid_sample_forward",
+                                "msda_grid_sample_backward_workspace_size",
+                                "msda_grid_sample_backward", "msda_roi_align_forward",
+                                "msda_roi_align_backward_workspace_size",
+                                "msda_roi_align_backward"}
 
 
 def test_library_exports_every_declared_symbol():
@@ -149,6 +153,61 @@ def test_deterministic_option_follows_torch_flag():
         torch.use_deterministic_algorithms(before)
 
 
+def test_gather_abi_checks_before_any_device_work():
+    """grid_sample / roi_align entry points: argument checks on the host,
+    workspace sizes, and empty work as a no-op (no device touched)."""
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    gs = lambda **o: lib.msda_grid_sample_forward(  # noqa: E731
+        vp(o.get("x", 16)), vp(o.get("g", 16)), vp(o.get("y", 16)), o.get("N", 1), o.get("H", 4),
+        o.get("W", 4), o.get("C", 8), o.get("Ho", 2), o.get("Wo", 2), o.get("pad", 0), 0,
+        o.get("dtype", 0), vp(0))
+    assert gs(dtype=9) == _lib.MSDA_ERR_UNSUPPORTED
+    assert gs(pad=2) == _lib.MSDA_ERR_UNSUPPORTED  # reflection is not built
+    assert b"padding_mode" in lib.msda_last_error()
+    assert gs(H=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert gs(C=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert gs(x=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert gs(g=6, dtype=0) == _lib.MSDA_ERR_INVALID_ARGUMENT  # grid needs 8-byte alignment for fp32
+    assert gs(Ho=0) == _lib.MSDA_OK and gs(N=0, x=0, g=0, y=0) == _lib.MSDA_OK
+    ws = lib.msda_grid_sample_backward_workspace_size
+    n = 2 * 5 * 6 * 8
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_BF16, _lib.MSDA_BWD_FP32_ACCUM) == n * 4
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_F32, _lib.MSDA_BWD_FP32_ACCUM) == 0
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_BF16, 0) == 0
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_F32, _lib.MSDA_BWD_DETERMINISTIC) == 256 + n * 8
+    rws = lib.msda_roi_align_backward_workspace_size
+    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, _lib.MSDA_BWD_FP32_ACCUM) == n * 4
+    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, _lib.MSDA_BWD_DETERMINISTIC) == 0
+    ra = lambda **o: lib.msda_roi_align_forward(  # noqa: E731
+        vp(16), vp(16), vp(16), 1, 4, 4, 8, o.get("K", 3), o.get("ph", 2), 2, 1.0, -1, 0, 0, vp(0))
+    assert ra(ph=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert ra(K=0) == _lib.MSDA_OK
+    rc = lib.msda_roi_align_backward(vp(16), vp(16), vp(16), vp(0), 0, 1, 4, 4, 8, 3, 2, 2, 1.0, -1, 0,
+                                     0, _lib.MSDA_BWD_DETERMINISTIC, vp(0))
+    assert rc == _lib.MSDA_ERR_UNSUPPORTED
+
+
+def test_gather_op_validation():
+    from msda_triton_b200 import grid_sample, roi_align
+    x = torch.zeros(1, 4, 5, 5)
+    g = torch.zeros(1, 3, 3, 2)
+    with pytest.raises(ValueError, match="mode"):
+        grid_sample(x, g, mode="linear")
+    with pytest.raises(NotImplementedError, match="nearest"):
+        grid_sample(x, g, mode="nearest")
+    with pytest.raises(NotImplementedError, match="reflection"):
+        grid_sample(x, g, padding_mode="reflection")
+    with pytest.raises(ValueError, match="grid"):
+        grid_sample(x, torch.zeros(2, 3, 3, 2))
+    with pytest.raises(ValueError, match="CUDA"):
+        grid_sample(x, g)
+    with pytest.raises(ValueError, match="boxes"):
+        roi_align(x, torch.zeros(3, 4), 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        roi_align(x, torch.zeros(3, 5), 2)
+
+
 def test_abi_backward_needs_workspace_for_fp32_accumulation():
     lib = _lib.load()
     vp = ctypes.c_void_p
@@ -196,10 +255,11 @@ def test_package_surface():
     import msda_triton_b200 as pkg
 
     # The reference's export (src/msda_triton/__init__.py:9-12) plus the
-    # mmcv-style Function and the layer around the operator.
+    # mmcv-style Function, the layer around the operator and the sibling gathers.
     assert pkg.__all__[0] == "multi_scale_deformable_attention"
     assert set(pkg.__all__) == {"multi_scale_deformable_attention", "MultiScaleDeformableAttnFunction",
-                                "MSDACrossAttention", "multi_scale_deformable_attention_fused"}
+                                "MSDACrossAttention", "multi_scale_deformable_attention_fused",
+                                "grid_sample", "roi_align"}
     assert callable(MultiScaleDeformableAttnFunction.apply)
 
 

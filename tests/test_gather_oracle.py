@@ -1,0 +1,66 @@
+"""The sibling-gather oracle (oracle/gather_oracle.py) pinned to the public
+operators it restates -- torch.nn.functional.grid_sample and
+torchvision.ops.roi_align -- on CPU in float64, forward and backward (CPU
+only: no GPU needed)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import gather_oracle as go
+
+torchvision = pytest.importorskip("torchvision")
+
+
+def _grid_inputs(seed, N=2, C=5, H=7, W=9, Ho=6, Wo=8, lo=-1.2, hi=1.2):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(N, C, H, W, generator=g, dtype=torch.float64)
+    grid = lo + (hi - lo) * torch.rand(N, Ho, Wo, 2, generator=g, dtype=torch.float64)
+    return x, grid
+
+
+@pytest.mark.parametrize("align", [False, True])
+@pytest.mark.parametrize("padding", ["zeros", "border"])
+def test_grid_sample_restatement_matches_torch(padding, align):
+    x, grid = _grid_inputs(0)
+    a = [t.clone().requires_grad_(True) for t in (x, grid)]
+    b = [t.clone().requires_grad_(True) for t in (x, grid)]
+    out = go.grid_sample_bilinear(*a, padding_mode=padding, align_corners=align)
+    ref = F.grid_sample(*b, mode="bilinear", padding_mode=padding, align_corners=align)
+    torch.testing.assert_close(out, ref, rtol=1e-12, atol=1e-12)
+    g = torch.randn_like(ref)
+    out.backward(g)
+    ref.backward(g)
+    torch.testing.assert_close(a[0].grad, b[0].grad, rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(a[1].grad, b[1].grad, rtol=1e-10, atol=1e-10)
+
+
+def _boxes(seed, K=6, N=2, H=20, W=24, scale=0.5):
+    g = torch.Generator().manual_seed(seed)
+    xy = torch.rand(K, 2, generator=g) * torch.tensor([W, H]) / scale
+    wh = torch.rand(K, 2, generator=g) * torch.tensor([W, H]) / scale * 0.6
+    idx = torch.randint(0, N, (K, 1), generator=g).float()
+    boxes = torch.cat([idx, xy - 0.2 * wh, xy + wh], 1)  # some boxes cross the border
+    return boxes
+
+
+@pytest.mark.parametrize("aligned", [False, True])
+@pytest.mark.parametrize("sampling_ratio", [-1, 2])
+def test_roi_align_restatement_matches_torchvision(sampling_ratio, aligned):
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 4, 20, 24, generator=g, dtype=torch.float64)
+    boxes = _boxes(4)
+    a = x.clone().requires_grad_(True)
+    b = x.clone().requires_grad_(True)
+    out = go.roi_align(a, boxes.double(), (5, 4), 0.5, sampling_ratio, aligned, box_dtype=torch.float64)
+    ref = torchvision.ops.roi_align(b, boxes.double(), (5, 4), 0.5, sampling_ratio, aligned)
+    torch.testing.assert_close(out, ref, rtol=1e-12, atol=1e-12)
+    gout = torch.randn_like(ref)
+    out.backward(gout)
+    ref.backward(gout)
+    torch.testing.assert_close(a.grad, b.grad, rtol=1e-12, atol=1e-12)
+    # fp32 box arithmetic (the kernels') moves sample positions by ~1e-6 px.
+    out32 = go.roi_align(x, boxes, (5, 4), 0.5, sampling_ratio, aligned)
+    torch.testing.assert_close(out32, ref.detach(), rtol=1e-4, atol=1e-5)

@@ -1,0 +1,250 @@
+"""Parity of the sibling gathers (grid_sample, ROI-Align) with the operators
+they replace -- torch.nn.functional.grid_sample and torchvision.ops.roi_align
+run on the CPU in float64 on the same (dtype-rounded) inputs -- and with the
+restated oracle (oracle/gather_oracle.py), forward and backward (GPU only).
+
+Tolerances: the strict bar of the MSDA suite (cases.STRICT_TOL) on outputs
+and input gradients; grid gradients in pixel units with the bilinear kinks
+excluded for fp32 grids (as for the MSDA location gradients).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cases
+from cases import REF_BWD_TOL, STRICT_TOL
+from msda_triton_b200 import _lib as _clib
+from msda_triton_b200 import grid_sample, roi_align
+from oracle import gather_oracle as go
+
+torchvision = pytest.importorskip("torchvision")
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+DTYPES = [torch.float32, torch.float16, torch.bfloat16]
+
+
+@pytest.fixture(autouse=True)
+def _lib_loaded(cuda_lib):
+    yield
+
+
+def close(actual, expected, tol, what=""):
+    torch.testing.assert_close(actual.double().cpu(), expected.double().cpu(), **tol,
+                               msg=lambda m: f"{what}: {m}")
+
+
+def _bitwise_equal(a, b):
+    as_int = {2: torch.int16, 4: torch.int32}[a.element_size()]
+    return torch.equal(a.contiguous().view(as_int), b.contiguous().view(as_int))
+
+
+# ---------------------------------------------------------------------------
+# grid_sample
+# ---------------------------------------------------------------------------
+GS_CASES = [
+    ("c32", dict(N=2, C=32, H=24, W=31, Ho=20, Wo=17)),
+    ("c3_scalar", dict(N=2, C=3, H=16, W=16, Ho=9, Wo=11)),
+    ("c256", dict(N=1, C=256, H=12, W=10, Ho=8, Wo=8)),
+    ("c96", dict(N=2, C=96, H=9, W=13, Ho=7, Wo=5)),
+    ("c512_cpl2", dict(N=1, C=512, H=6, W=7, Ho=5, Wo=4)),
+]
+
+
+def _gs_inputs(kw, dtype, seed=0, lo=-1.15, hi=1.15):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(kw["N"], kw["C"], kw["H"], kw["W"], generator=g)
+    grid = lo + (hi - lo) * torch.rand(kw["N"], kw["Ho"], kw["Wo"], 2, generator=g)
+    gout = torch.randn(kw["N"], kw["C"], kw["Ho"], kw["Wo"], generator=g)
+    return (x.to(DEV, dtype), grid.to(DEV, dtype), gout.to(DEV, dtype))
+
+
+def _gs_reference(x, grid, gout, padding, align):
+    """torch's CPU grid_sample in float64 on the same rounded inputs, with autograd."""
+    xr = x.detach().double().cpu().requires_grad_(True)
+    gr = grid.detach().double().cpu().requires_grad_(True)
+    out = F.grid_sample(xr, gr, mode="bilinear", padding_mode=padding, align_corners=align)
+    out.backward(gout.double().cpu())
+    return out.detach(), xr.grad, gr.grad
+
+
+def _gs_kinks(grid, H, W, align, eps):
+    """Grid points whose pixel coordinate lies within eps of an integer."""
+    g = grid.detach().double().cpu()
+    size = torch.tensor([W, H], dtype=torch.float64)
+    px = ((g + 1) / 2) * (size - 1) if align else ((g + 1) * size - 1) / 2
+    return ((px - px.round()).abs() < eps).any(-1)
+
+
+def _run_gs(x, grid, gout, padding, align, **kw):
+    xl = x.clone().requires_grad_(True)
+    gl = grid.clone().requires_grad_(True)
+    out = grid_sample(xl, gl, mode="bilinear", padding_mode=padding, align_corners=align, **kw)
+    out.backward(gout)
+    return out.detach(), xl.grad, gl.grad
+
+
+@pytest.mark.parametrize("align", [False, True], ids=["ac0", "ac1"])
+@pytest.mark.parametrize("padding", ["zeros", "border"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,kw", GS_CASES, ids=[c[0] for c in GS_CASES])
+def test_grid_sample_matches_torch(name, kw, dtype, padding, align):
+    x, grid, gout = _gs_inputs(kw, dtype)
+    out, gx, gg = _run_gs(x, grid, gout, padding, align)
+    assert out.shape == (kw["N"], kw["C"], kw["Ho"], kw["Wo"]) and out.dtype == dtype
+    ref, gx_r, gg_r = _gs_reference(x, grid, gout, padding, align)
+    tol = STRICT_TOL[dtype]
+    close(out, ref, tol, "out")
+    close(gx, gx_r, tol, "grad_input")
+    # grad_grid in pixel units. fp32 grids: points within 1e-3 px of a
+    # bilinear kink are excluded (the fp32 and float64 pixel coordinates may
+    # floor differently there). 16-bit grids give pixel coordinates that are
+    # exact in fp32, so both sides take the same one-sided derivative and
+    # nothing is excluded.
+    scale = torch.tensor([kw["W"], kw["H"]], dtype=torch.float64) / 2
+    if dtype == torch.float32:
+        keep = ~_gs_kinks(grid, kw["H"], kw["W"], align, 1e-3)
+        assert keep.double().mean() > 0.98
+    else:
+        keep = torch.ones(grid.shape[:-1], dtype=torch.bool)
+    torch.testing.assert_close((gg.double().cpu() / scale)[keep], (gg_r / scale)[keep], **tol)
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_grid_sample_matches_the_oracle(dtype):
+    x, grid, gout = _gs_inputs(GS_CASES[0][1], dtype, seed=3)
+    out, gx, _ = _run_gs(x, grid, gout, "zeros", False)
+    xr = x.double().cpu().requires_grad_(True)
+    ref = go.grid_sample_bilinear(xr, grid.double().cpu(), "zeros", False)
+    ref.backward(gout.double().cpu())
+    close(out, ref.detach(), STRICT_TOL[dtype], "out")
+    close(gx, xr.grad, STRICT_TOL[dtype], "grad_input")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=str)
+def test_grid_sample_native_accumulation(dtype):
+    x, grid, gout = _gs_inputs(GS_CASES[0][1], dtype, seed=4)
+    _, gx, _ = _run_gs(x, grid, gout, "zeros", False, fp32_grad_accum=False)
+    _, gx_r, _ = _gs_reference(x, grid, gout, "zeros", False)
+    close(gx, gx_r, REF_BWD_TOL[dtype], "grad_input (native atomics)")
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,kw", GS_CASES[:3], ids=[c[0] for c in GS_CASES[:3]])
+def test_grid_sample_deterministic(name, kw, dtype):
+    """The fixed-point input gradient is bitwise invariant to the order of
+    the output pixels (a permutation of the grid reorders every atomic)."""
+    # A zoomed-out grid: many output pixels share input pixels.
+    x, grid, gout = _gs_inputs(kw, dtype, seed=5, lo=-0.3, hi=0.3)
+    _, gx, gg = _run_gs(x, grid, gout, "zeros", False, deterministic=True)
+    _, gx2, _ = _run_gs(x, grid, gout, "zeros", False, deterministic=True)
+    assert _bitwise_equal(gx, gx2)
+    N, Ho, Wo = kw["N"], kw["Ho"], kw["Wo"]
+    perm = torch.randperm(Ho * Wo, generator=torch.Generator().manual_seed(1)).to(DEV)
+    gridp = grid.reshape(N, Ho * Wo, 2)[:, perm].reshape(N, Ho, Wo, 2)
+    goutp = gout.reshape(N, -1, Ho * Wo)[:, :, perm].reshape(N, -1, Ho, Wo)
+    _, gxp, ggp = _run_gs(x, gridp, goutp, "zeros", False, deterministic=True)
+    assert _bitwise_equal(gx, gxp)
+    assert _bitwise_equal(gg.reshape(N, Ho * Wo, 2)[:, perm], ggp.reshape(N, Ho * Wo, 2))
+    _, gx_r, _ = _gs_reference(x, grid, gout, "zeros", False)
+    close(gx, gx_r, STRICT_TOL[dtype], "grad_input (deterministic)")
+
+
+def test_grid_sample_channels_last_input_and_edges():
+    kw = GS_CASES[0][1]
+    x, grid, gout = _gs_inputs(kw, torch.bfloat16, seed=6)
+    a = grid_sample(x, grid, align_corners=False)
+    b = grid_sample(x.contiguous(memory_format=torch.channels_last), grid, align_corners=False)
+    assert torch.equal(a, b)
+    assert a.is_contiguous(memory_format=torch.channels_last)
+    # Empty output grid; grid points far outside (zeros padding) give zeros.
+    empty = grid_sample(x, grid[:, :0], align_corners=False)
+    assert empty.shape == (kw["N"], kw["C"], 0, kw["Wo"])
+    far = torch.full_like(grid, 7.0)
+    assert (grid_sample(x, far) == 0).all()
+    nan = torch.full_like(grid, float("nan"))
+    assert torch.isfinite(grid_sample(x, nan)).all()
+
+
+# ---------------------------------------------------------------------------
+# ROI-Align
+# ---------------------------------------------------------------------------
+def _roi_inputs(dtype, C, seed=0, N=2, H=28, W=33, K=12, scale=0.25):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(N, C, H, W, generator=g)
+    xy = torch.rand(K, 2, generator=g) * torch.tensor([W, H]) / scale
+    wh = (0.05 + torch.rand(K, 2, generator=g)) * torch.tensor([W, H]) / scale * 0.5
+    idx = torch.randint(0, N, (K, 1), generator=g).float()
+    boxes = torch.cat([idx, xy - 0.3 * wh, xy + wh], 1)  # some boxes cross the border
+    return x.to(DEV, dtype), boxes, scale
+
+
+ROI_CASES = [("c32", 32), ("c3_scalar", 3), ("c256", 256), ("c64", 64)]
+
+
+@pytest.mark.parametrize("aligned", [False, True], ids=["unaligned", "aligned"])
+@pytest.mark.parametrize("sampling_ratio", [-1, 2], ids=["adaptive", "sr2"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,C", ROI_CASES, ids=[c[0] for c in ROI_CASES])
+def test_roi_align_matches_torchvision(name, C, dtype, sampling_ratio, aligned):
+    x, boxes, scale = _roi_inputs(dtype, C)
+    xl = x.clone().requires_grad_(True)
+    out = roi_align(xl, boxes.to(DEV), (7, 6), scale, sampling_ratio, aligned)
+    assert out.shape == (boxes.shape[0], C, 7, 6) and out.dtype == dtype
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(9)).to(DEV, dtype)
+    out.backward(gout)
+    # The kernels compute box geometry in fp32: the oracle with fp32 box
+    # arithmetic is the tight reference, torchvision (float64 boxes) the
+    # public one (sample positions differ by ~1e-6 px).
+    xr = x.double().cpu().requires_grad_(True)
+    ref = go.roi_align(xr, boxes, (7, 6), scale, sampling_ratio, aligned)
+    ref.backward(gout.double().cpu())
+    close(out, ref.detach(), STRICT_TOL[dtype], "out")
+    close(xl.grad, xr.grad, STRICT_TOL[dtype], "grad_input")
+    tv = torchvision.ops.roi_align(x.double().cpu(), boxes.double(), (7, 6), scale, sampling_ratio, aligned)
+    close(out, tv, REF_BWD_TOL[dtype] if dtype != torch.float32 else dict(rtol=1e-4, atol=1e-4), "out vs torchvision")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=str)
+def test_roi_align_native_accumulation_and_box_lists(dtype):
+    x, boxes, scale = _roi_inputs(dtype, 32, seed=2)
+    # torchvision's list-of-boxes format gives the same result as (K, 5).
+    per_image = [boxes[boxes[:, 0] == i, 1:].to(DEV) for i in range(x.shape[0])]
+    order = torch.cat([torch.nonzero(boxes[:, 0] == i).flatten() for i in range(x.shape[0])])
+    a = roi_align(x, boxes.to(DEV), 5, scale, 2)
+    b = roi_align(x, per_image, 5, scale, 2)
+    assert torch.equal(a[order.to(DEV)], b)
+    xl = x.clone().requires_grad_(True)
+    out = roi_align(xl, boxes.to(DEV), 5, scale, 2, fp32_grad_accum=False)
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(3)).to(DEV, dtype)
+    out.backward(gout)
+    xr = x.double().cpu().requires_grad_(True)
+    go.roi_align(xr, boxes, 5, scale, 2).backward(gout.double().cpu())
+    close(xl.grad, xr.grad, REF_BWD_TOL[dtype], "grad_input (native atomics)")
+
+
+def test_roi_align_edges():
+    x, boxes, scale = _roi_inputs(torch.float32, 32, seed=5)
+    # No boxes; a box on a missing batch item; a degenerate aligned box.
+    assert roi_align(x, torch.zeros(0, 5, device=DEV), 3, scale).shape == (0, 32, 3, 3)
+    bad = torch.tensor([[7.0, 1.0, 1.0, 20.0, 20.0], [0.0, 5.0, 5.0, 5.0, 5.0]], device=DEV)
+    out = roi_align(x, bad, 3, 1.0, -1, True)
+    assert (out[0] == 0).all()
+    ref = torchvision.ops.roi_align(x.double().cpu(), bad[1:].double().cpu(), 3, 1.0, -1, True)
+    close(out[1:], ref, dict(rtol=1e-5, atol=1e-6), "degenerate box")
+    # The backward refuses deterministic mode, as torchvision's does.
+    xl = x.clone().requires_grad_(True)
+    before = torch.are_deterministic_algorithms_enabled()
+    try:
+        torch.use_deterministic_algorithms(True)
+        out = roi_align(xl, boxes.to(DEV), 3, scale)
+        with pytest.raises(RuntimeError, match="deterministic"):
+            out.sum().backward()
+    finally:
+        torch.use_deterministic_algorithms(before)
+    with pytest.raises(_clib.MSDALibraryError):
+        _clib.check("msda_roi_align_backward", _clib.load().msda_roi_align_backward(
+            None, None, None, None, 0, 1, 4, 4, 8, 1, 2, 2, 1.0, -1, 0, 0, _clib.MSDA_BWD_DETERMINISTIC, None))
