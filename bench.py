@@ -394,6 +394,140 @@ def load_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+# ---------------------------------------------------------------------------
+# Sibling gathers (--op grid_sample / roi_align): their own workloads, timed
+# like the MSDA device leg (L2 flushed before every step, CUDA events around
+# forward + backward through the public op), next to the operators they
+# replace (torch's grid_sample, torchvision's roi_align) on the same GPU.
+# ---------------------------------------------------------------------------
+GATHER_WORKLOADS = {
+    # A feature-map warp: N=8, C=128, 128x128 -> 128x128, bf16, an affine grid
+    # (rotation, zoom, shift) with small jitter, so neighbouring outputs share
+    # input pixels.
+    "grid_sample": dict(N=8, C=128, H=128, W=128, Ho=128, Wo=128, dtype=torch.bfloat16),
+    # Mask R-CNN box head on the stride-4 level of an 800x1216 image pair:
+    # N=2, C=256, 200x304, 1024 boxes of 32-400 px, 7x7 bins, sampling_ratio 2,
+    # aligned; fp32 (torchvision's kernel takes boxes in the input's dtype and
+    # runs fp32 under autocast).
+    "roi_align": dict(N=2, C=256, H=200, W=304, K=1024, P=7, sr=2, scale=0.25, dtype=torch.float32),
+}
+
+
+def _gather_inputs(op):
+    w = GATHER_WORKLOADS[op]
+    g = torch.Generator().manual_seed(0)
+    dt = w["dtype"]
+    x = torch.randn(w["N"], w["C"], w["H"], w["W"], generator=g).to("cuda", dt)
+    if op == "grid_sample":
+        ang = torch.rand(w["N"], generator=g) * 0.35 - 0.175
+        zoom = 0.8 + 0.3 * torch.rand(w["N"], generator=g)
+        theta = torch.zeros(w["N"], 2, 3)
+        theta[:, 0, 0] = zoom * torch.cos(ang)
+        theta[:, 0, 1] = -zoom * torch.sin(ang)
+        theta[:, 1, 0] = zoom * torch.sin(ang)
+        theta[:, 1, 1] = zoom * torch.cos(ang)
+        theta[:, :, 2] = 0.1 * torch.randn(w["N"], 2, generator=g)
+        grid = torch.nn.functional.affine_grid(theta, (w["N"], w["C"], w["Ho"], w["Wo"]), align_corners=False)
+        grid = grid + 0.01 * torch.randn(grid.shape, generator=g)
+        gout = torch.randn(w["N"], w["C"], w["Ho"], w["Wo"], generator=g).to("cuda", dt)
+        return w, x, grid.to("cuda", dt), gout
+    K = w["K"]
+    img = torch.tensor([w["W"], w["H"]]) / w["scale"]
+    wh = 32 + 368 * torch.rand(K, 2, generator=g)
+    xy = torch.rand(K, 2, generator=g) * (img - wh).clamp(min=1)
+    boxes = torch.cat([torch.randint(0, w["N"], (K, 1), generator=g).float(), xy, xy + wh], 1)
+    gout = torch.randn(K, w["C"], w["P"], w["P"], generator=g).to("cuda", dt)
+    return w, x, boxes.to("cuda"), gout
+
+
+def _gather_call(op, impl, x, coords, w):
+    if op == "grid_sample":
+        if impl == "b200":
+            from msda_triton_b200 import grid_sample
+            return grid_sample(x, coords, align_corners=False)
+        return torch.nn.functional.grid_sample(x, coords, mode="bilinear", padding_mode="zeros",
+                                               align_corners=False)
+    if impl == "b200":
+        from msda_triton_b200 import roi_align
+        return roi_align(x, coords, w["P"], w["scale"], w["sr"], True)
+    import torchvision
+    return torchvision.ops.roi_align(x, coords, w["P"], w["scale"], w["sr"], True)
+
+
+def _gather_time(op, impl, x, coords, gout, w, steps, warmup):
+    """Mean (forward ms, backward ms) per step; L2 flushed before each step."""
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    drain = torch.ones(L2_DRAIN_BYTES // 4, dtype=torch.float32, device="cuda")
+    xl = x.clone().requires_grad_(True)
+    cl = coords.clone().requires_grad_(op == "grid_sample")
+    fwd, bwd = [], []
+    for i in range(warmup + steps):
+        flush.fill_(1)
+        drain.sum()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record()
+        out = _gather_call(op, impl, xl, cl, w)
+        e[1].record()
+        out.backward(gout)
+        e[2].record()
+        torch.cuda.synchronize()
+        xl.grad = None
+        cl.grad = None
+        if i >= warmup:
+            fwd.append(e[0].elapsed_time(e[1]))
+            bwd.append(e[1].elapsed_time(e[2]))
+    return statistics.fmean(fwd), statistics.fmean(bwd)
+
+
+def gather_algorithmic_bytes(op, w):
+    """Per step, counted like the MSDA model: every corner row gathered or
+    reduced, parameters, outputs and gradients once, the input gradient
+    zero-filled once."""
+    e, C = w["dtype"].itemsize, w["C"]
+    inp = w["N"] * w["H"] * w["W"] * C * e
+    if op == "grid_sample":
+        P = w["N"] * w["Ho"] * w["Wo"]
+        fwd = P * (4 * C * e + 2 * e + C * e)
+        bwd = P * (4 * C * e + 4 * C * e + C * e + 2 * e + 2 * e) + inp
+        return fwd, bwd, P
+    bins = w["K"] * w["P"] * w["P"]
+    samples = bins * w["sr"] * w["sr"]
+    fwd = samples * 4 * C * e + bins * C * e + w["K"] * 20
+    bwd = samples * 4 * C * e + bins * C * e + w["K"] * 20 + inp
+    return fwd, bwd, w["K"]
+
+
+def run_gather_bench(args):
+    op = args.op
+    w, x, coords, gout = _gather_inputs(op)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        f_ms, b_ms = _gather_time(op, "b200", x, coords, gout, w, args.steps, args.warmup)
+    rf_ms, rb_ms = _gather_time(op, "torch", x, coords, gout, w, args.steps, args.warmup)
+    fwd_b, bwd_b, units = gather_algorithmic_bytes(op, w)
+    peak, peak_kind = load_peaks()
+    ms = f_ms + b_ms
+    unit = "output pixels/s" if op == "grid_sample" else "rois/s"
+    achieved = (fwd_b + bwd_b) / (ms / 1e3) / 1e9
+    line = {
+        "metric": f"{op} fwd+bwd {unit}", "value": units / (ms / 1e3), "unit": unit, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": str(w["dtype"]).replace("torch.", ""), "data": "synthetic",
+        "config": {"workload": op, **{k: v for k, v in w.items() if k != "dtype"},
+                   "l2": "flushed before every step"},
+        "fwd_us": f_ms * 1e3, "bwd_us": b_ms * 1e3,
+        "replaced_operator": {"impl": "torch.nn.functional.grid_sample" if op == "grid_sample"
+                              else "torchvision.ops.roi_align", "fwd_us": rf_ms * 1e3, "bwd_us": rb_ms * 1e3,
+                              "value": units / ((rf_ms + rb_ms) / 1e3)},
+        "roofline": {"kernel": "forward + backward calls, CUDA-event time", "bound": "hbm",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes": fwd_b + bwd_b, "traffic": None},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def load_traffic(config_name):
     p = REPO / "profiles" / "traffic.json"
     if not p.exists():
@@ -449,6 +583,9 @@ def main(argv=None) -> int:
     ap.add_argument("--config", default="decoder", choices=sorted(presets.PRESETS))
     ap.add_argument("--dtype", default=None, choices=["bf16", "fp16", "fp32"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--op", default="msda", choices=["msda", "grid_sample", "roi_align"],
+                    help="msda (default): the headline benchmark; grid_sample / roi_align: the "
+                         "sibling gathers on their own workloads, next to torch / torchvision (1 GPU)")
     ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
     ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner", "counted"],
                     help="force the grad_value algorithm of the device leg (default: automatic)")
@@ -464,6 +601,11 @@ def main(argv=None) -> int:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
+    if args.op != "msda":
+        if args.gpus != 1 or args.impl != "b200":
+            ap.error("--op grid_sample / roi_align run on one GPU, b200 arm only")
+        torch.cuda.set_device(0)
+        return run_gather_bench(args)
     preset = presets.get(args.config)
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32,
              None: preset.dtype}[args.dtype]
