@@ -71,6 +71,65 @@ __device__ __forceinline__ bool query_block_of(const OpParams& p, int warps, int
   return q < p.Q;
 }
 
+// Sums the G lane groups' partial rows of a warp and stores the output row
+// (shared by the forward kernels).
+template <typename T, int VEC, int LPR, int CPL>
+__device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&acc)[CPL][VEC]) {
+  constexpr int G = 32 / LPR;
+  const int grp = lane / LPR, sub = lane % LPR;
+  if constexpr (CPL == 1 && G > 1 && VEC >= 2) {
+    // Reduce-scatter across the G groups: each xor stage halves the values a
+    // lane keeps (it keeps the half its partner sends it the other of), so
+    // log2(VEC) stages cost VEC-1 shuffles instead of VEC*log2(G); once a lane
+    // holds one value the remaining stages are plain xor-sums.
+    constexpr int STAGES = __builtin_ctz(G);
+    int base = 0;
+#pragma unroll
+    for (int st = 0; st < STAGES; ++st) {
+      const int off = LPR << st;
+      const int n = VEC >> st;  // live values before this stage (compile time after unrolling)
+      if (n > 1) {
+        const bool upper = (lane & off) != 0;
+        const int half = n / 2;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = upper ? acc[0][i] : acc[0][half + i];
+          const float keep = upper ? acc[0][half + i] : acc[0][i];
+          acc[0][i] = keep + __shfl_xor_sync(kFullMask, send, off);
+        }
+        if (upper) base += half;
+      } else {
+        acc[0][0] += __shfl_xor_sync(kFullMask, acc[0][0], off);
+      }
+    }
+    constexpr int NF = (VEC >> STAGES) > 0 ? (VEC >> STAGES) : 1;  // values left per lane
+    constexpr int HALVINGS = __builtin_ctz(VEC) < STAGES ? __builtin_ctz(VEC) : STAGES;
+    // Lanes that only replicated a value in the plain xor stages skip the store.
+    const int rep_mask = ((G - 1) << __builtin_ctz(LPR)) & ~(((1 << HALVINGS) - 1) << __builtin_ctz(LPR));
+    const int ch = sub * VEC + base;
+    if ((lane & rep_mask) == 0 && sub * VEC < D) {
+      float outv[NF];
+#pragma unroll
+      for (int i = 0; i < NF; ++i) outv[i] = acc[0][i];
+      store_vec<T, NF>(op + ch, outv);
+    }
+  } else {
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+      for (int j = 0; j < CPL; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], off);
+    if (grp == 0) {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int ch = (j * LPR + sub) * VEC;
+        if (ch < D) store_vec<T, VEC>(op + ch, acc[j]);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Forward: out[b,q,m,:] = sum_{l,k} a * sum_c w_c * value[b, pix_c, m, :]
 // (src/msda_triton/kernels.py:100-163)
@@ -186,58 +245,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpPara
       for (int e = 0; e < NP; ++e) f2_unpack(acc2[j][e], acc[j][2 * e], acc[j][2 * e + 1]);
   }
 
-  T* op = reinterpret_cast<T*>(p.out) + qm * D;
-  if constexpr (CPL == 1 && G > 1 && VEC >= 2) {
-    // Reduce-scatter across the G groups: each xor stage halves the values a
-    // lane keeps (it keeps the half its partner sends it the other of), so
-    // log2(VEC) stages cost VEC-1 shuffles instead of VEC*log2(G); once a lane
-    // holds one value the remaining stages are plain xor-sums.
-    constexpr int STAGES = __builtin_ctz(G);
-    int base = 0;
-#pragma unroll
-    for (int st = 0; st < STAGES; ++st) {
-      const int off = LPR << st;
-      const int n = VEC >> st;  // live values before this stage (compile time after unrolling)
-      if (n > 1) {
-        const bool upper = (lane & off) != 0;
-        const int half = n / 2;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-          const float send = upper ? acc[0][i] : acc[0][half + i];
-          const float keep = upper ? acc[0][half + i] : acc[0][i];
-          acc[0][i] = keep + __shfl_xor_sync(kFullMask, send, off);
-        }
-        if (upper) base += half;
-      } else {
-        acc[0][0] += __shfl_xor_sync(kFullMask, acc[0][0], off);
-      }
-    }
-    constexpr int NF = (VEC >> STAGES) > 0 ? (VEC >> STAGES) : 1;  // values left per lane
-    constexpr int HALVINGS = __builtin_ctz(VEC) < STAGES ? __builtin_ctz(VEC) : STAGES;
-    // Lanes that only replicated a value in the plain xor stages skip the store.
-    const int rep_mask = ((G - 1) << __builtin_ctz(LPR)) & ~(((1 << HALVINGS) - 1) << __builtin_ctz(LPR));
-    const int ch = sub * VEC + base;
-    if ((lane & rep_mask) == 0 && sub * VEC < D) {
-      float outv[NF];
-#pragma unroll
-      for (int i = 0; i < NF; ++i) outv[i] = acc[0][i];
-      store_vec<T, NF>(op + ch, outv);
-    }
-  } else {
-#pragma unroll
-    for (int off = LPR; off < 32; off <<= 1)
-#pragma unroll
-      for (int j = 0; j < CPL; ++j)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], off);
-    if (grp == 0) {
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        const int ch = (j * LPR + sub) * VEC;
-        if (ch < D) store_vec<T, VEC>(op + ch, acc[j]);
-      }
-    }
-  }
+  fwd_store_row<T, VEC, LPR, CPL>(reinterpret_cast<T*>(p.out) + qm * D, D, lane, acc);
 }
 
 // ---------------------------------------------------------------------------
