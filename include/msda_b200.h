@@ -240,6 +240,12 @@ MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_sha
  * grad_input need not be zeroed by the caller.
  */
 
+/* Layout conversion for the NHWC kernels: dst[n][c][r] = src[n][r][c] for
+ * (N, R, C) -> (N, C, R) -- NCHW -> NHWC with (R, C) = (C, H*W), and back
+ * with (R, C) = (H*W, C). */
+MSDA_API int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, int32_t dtype,
+                            void* stream);
+
 /* torch.nn.functional.grid_sample(input, grid, mode="bilinear",
  * padding_mode, align_corners) on NHWC data; padding_mode 0 = "zeros",
  * 1 = "border" ("reflection" is not supported: MSDA_ERR_UNSUPPORTED). */

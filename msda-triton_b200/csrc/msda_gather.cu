@@ -215,6 +215,39 @@ int forward(const char* fn, Op op, GatherParams& p, const Dims& d, int32_t dtype
 
 extern "C" {
 
+int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, int32_t dtype,
+                   void* stream) {
+  const char* fn = "msda_transpose";
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MSDA_ERR_UNSUPPORTED, "%s: unsupported dtype code %d", fn, dtype);
+  if (N < 0 || R < 0 || C < 0) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: negative size", fn);
+  if (N == 0 || R == 0 || C == 0) return succeed();
+  if (!src || !dst) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
+  if (!aligned(src, es) || !aligned(dst, es)) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer", fn);
+  constexpr int TL = msda::kTransposeTile;
+  const int64_t gx = (C + TL - 1) / TL, gy = (R + TL - 1) / TL;
+  if (gx > 0x7fffffff || gy > 65535 || N > 65535)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: sizes too large (N <= 65535, R <= %d)", fn, 65535 * TL);
+  const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)N);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (R % 4 == 0 && C % 4 == 0 && R * C < (int64_t(1) << 31) && aligned(src, 4 * es) && aligned(dst, 4 * es)) {
+    if (es == 4)
+      msda::transpose4_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst),
+                                                          (int)R, (int)C);
+    else
+      msda::transpose4_kernel<unsigned short><<<grid, 256, 0, st>>>(
+          static_cast<const unsigned short*>(src), static_cast<unsigned short*>(dst), (int)R, (int)C);
+  } else if (es == 4) {
+    msda::transpose_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst), R, C);
+  } else {
+    msda::transpose_kernel<unsigned short><<<grid, 256, 0, st>>>(static_cast<const unsigned short*>(src),
+                                                               static_cast<unsigned short*>(dst), R, C);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "transpose launch");
+  return succeed();
+}
+
 int msda_grid_sample_forward(const void* input, const void* grid, void* output, int64_t N, int64_t H,
                              int64_t W, int64_t C, int64_t out_h, int64_t out_w, int32_t padding_mode,
                              int32_t align_corners, int32_t dtype, void* stream) {

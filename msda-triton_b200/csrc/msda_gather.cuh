@@ -470,4 +470,75 @@ __global__ void __launch_bounds__(kGatherWarps * 32) roi_bwd_kernel(const Gather
     }
 }
 
+// ---------------------------------------------------------------------------
+// Layout conversion on either side of the channels-last kernels:
+// dst[n][c][r] = src[n][r][c] for (N, R, C) -> (N, C, R) (NCHW <-> NHWC with
+// R or C = H*W). A 64 x 64 tile goes through shared memory (a row pitch of
+// an odd number of 4-byte words keeps the column reads conflict-free), so
+// both the loads and the stores are coalesced along the contiguous axis of
+// their tensor.
+// ---------------------------------------------------------------------------
+constexpr int kTransposeTile = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                        int64_t R, int64_t C) {
+  constexpr int TL = kTransposeTile;
+  __shared__ T tile[TL][TL + 4 / sizeof(T)];
+  const int64_t n = blockIdx.z;
+  const int64_t r0 = (int64_t)blockIdx.y * TL, c0 = (int64_t)blockIdx.x * TL;
+  const T* s = src + n * R * C;
+  T* d = dst + n * R * C;
+  const int tx = threadIdx.x & (TL - 1), ty = threadIdx.x / TL;  // 64 x 4 threads
+#pragma unroll
+  for (int k = 0; k < TL; k += 4) {
+    const int64_t r = r0 + ty + k, c = c0 + tx;
+    if (r < R && c < C) tile[ty + k][tx] = s[r * C + c];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < TL; k += 4) {
+    const int64_t c = c0 + ty + k, r = r0 + tx;
+    if (c < C && r < R) d[c * R + r] = tile[tx][ty + k];
+  }
+}
+
+// Vector variant (R and C multiples of 4, 4-element aligned buffers, a batch
+// slice below 2^31 elements): every global access moves 4 elements (8 bytes
+// for 16-bit types, 16 for fp32), 16 lanes cover one 64-element tile row on
+// either side, and offsets are 32-bit.
+template <typename T>
+__global__ void __launch_bounds__(256) transpose4_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                         int R, int C) {
+  constexpr int TL = kTransposeTile;
+  using V4 = typename RawVec<4 * sizeof(T)>::type;  // 4 elements
+  __shared__ T tile[TL][TL + 1];
+  const int64_t n = blockIdx.z;
+  const int r0 = blockIdx.y * TL, c0 = blockIdx.x * TL;
+  const T* s = src + n * (int64_t)R * C;
+  T* d = dst + n * (int64_t)R * C;
+  const int lo = threadIdx.x & 15, hi = threadIdx.x >> 4;  // 16 x 16 threads
+#pragma unroll
+  for (int k = 0; k < TL; k += 16) {
+    const int r = r0 + hi + k, c = c0 + 4 * lo;
+    if (r < R && c < C) {
+      union { V4 v; T e[4]; } u;
+      u.v = __ldcs(reinterpret_cast<const V4*>(s + r * C + c));
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[hi + k][4 * lo + e] = u.e[e];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < TL; k += 16) {
+    const int c = c0 + hi + k, r = r0 + 4 * lo;
+    if (c < C && r < R) {
+      union { V4 v; T e[4]; } u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) u.e[e] = tile[4 * lo + e][hi + k];
+      *reinterpret_cast<V4*>(d + c * R + r) = u.v;
+    }
+  }
+}
+
 }  // namespace msda

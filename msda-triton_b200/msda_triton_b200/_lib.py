@@ -64,7 +64,8 @@ SIGNATURES = {
         [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
          _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _VP],
     ),
-    # Sibling gathers on NHWC data: grid_sample and ROI-Align.
+    # Sibling gathers on NHWC data: grid_sample and ROI-Align; the layout conversion.
+    "msda_transpose": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I32, _VP]),
     "msda_grid_sample_forward": (
         ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _VP]),
     "msda_grid_sample_backward_workspace_size": (

@@ -11,10 +11,12 @@ drop-ins for the public operators they replace:
   ``mode="bilinear"``, ``padding_mode`` "zeros" or "border");
 * :func:`roi_align` for ``torchvision.ops.roi_align``.
 
-The kernels read and write NHWC: an input already in ``torch.channels_last``
-memory format is used as is (otherwise it is copied once), and the outputs
-are returned as channels-last NCHW tensors (same shape and values as the
-replaced operators, a different memory format). There is no CPU path.
+The kernels read and write NHWC. An input already in ``torch.channels_last``
+memory format is used as is; an NCHW-contiguous input (and an NCHW output
+gradient) is converted by the library's tiled transpose kernel
+(``msda_transpose``), and the input gradient is returned in the input's
+layout. The outputs are channels-last NCHW tensors (same shape and values as
+the replaced operators, a different memory format). There is no CPU path.
 """
 
 from __future__ import annotations
@@ -28,9 +30,52 @@ from .ops import _DTYPE_CODE, _FLOAT_DTYPES, _device_guard, _ptr, _stream, _use_
 _PADDING = {"zeros": 0, "border": 1}
 
 
+def _transpose(src: torch.Tensor, N: int, R: int, C: int) -> torch.Tensor:
+    """(N, R, C) contiguous -> (N, C, R) contiguous, on the device."""
+    dst = src.new_empty(N, C, R)
+    lib = _lib.load()
+    with _device_guard(src.device):
+        rc = lib.msda_transpose(_ptr(src), _ptr(dst), N, R, C, _DTYPE_CODE[src.dtype], _stream(src.device))
+    _lib.check("msda_transpose", rc)
+    return dst
+
+
+class _ToNHWC(torch.autograd.Function):
+    """NCHW -> contiguous NHWC with the transpose kernel; the gradient goes
+    back to contiguous NCHW the same way."""
+
+    @staticmethod
+    def forward(ctx, x):
+        N, C, H, W = x.shape
+        return _transpose(x.contiguous(), N, C, H * W).view(N, H, W, C)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        N, H, W, C = g.shape
+        return _transpose(_nhwc_contiguous(g), N, H * W, C).view(N, C, H, W)
+
+
 def _nhwc(x: torch.Tensor) -> torch.Tensor:
-    """(N, C, H, W) -> contiguous (N, H, W, C) (a view for channels_last input)."""
-    return x.permute(0, 2, 3, 1).contiguous()
+    """(N, C, H, W) -> contiguous (N, H, W, C): a view of a channels_last
+    tensor, else one transpose kernel."""
+    v = x.permute(0, 2, 3, 1)
+    if v.is_contiguous():
+        return v
+    return _ToNHWC.apply(x)
+
+
+def _nhwc_contiguous(t: torch.Tensor) -> torch.Tensor:
+    """An (N, H, W, C)-shaped tensor as contiguous NHWC: itself, one
+    transpose kernel when it is an NCHW-contiguous tensor seen through a
+    permute (an output gradient from an NCHW consumer), else a copy."""
+    if t.is_contiguous():
+        return t
+    N, H, W, C = t.shape
+    nchw = t.permute(0, 3, 1, 2)
+    if nchw.is_contiguous() and t.dtype in _DTYPE_CODE:
+        return _transpose(nchw, N, C, H * W).view(N, H, W, C)
+    return t.contiguous()
 
 
 def _bwd_flags(dtype, fp32_grad_accum, deterministic):
@@ -70,7 +115,7 @@ class _GridSampleFunction(torch.autograd.Function):
         padding, align, flags = ctx.cfg
         N, H, W, C = x.shape
         _, Ho, Wo, _ = grid.shape
-        grad_out = grad_out.to(x.dtype).contiguous()
+        grad_out = _nhwc_contiguous(grad_out.to(x.dtype))
         grad_in = torch.empty_like(x)
         grad_grid = torch.empty_like(grid)
         lib = _lib.load()
@@ -192,7 +237,7 @@ class _RoiAlignFunction(torch.autograd.Function):
             raise RuntimeError("roi_align backward has no deterministic implementation (as in "
                                "torchvision); disable torch.use_deterministic_algorithms for it")
         N, H, W, C = shape
-        grad_out = grad_out.to(dtype).contiguous()
+        grad_out = _nhwc_contiguous(grad_out.to(dtype))
         grad_in = grad_out.new_empty(shape)
         lib = _lib.load()
         code = _DTYPE_CODE[dtype]

@@ -32,7 +32,7 @@ def test_header_declares_the_abi():
                                 "msda_grid_sample_backward_workspace_size",
                                 "msda_grid_sample_backward", "msda_roi_align_forward",
                                 "msda_roi_align_backward_workspace_size",
-                                "msda_roi_align_backward"}
+                                "msda_roi_align_backward", "msda_transpose"}
 
 
 def test_library_exports_every_declared_symbol():

@@ -248,3 +248,45 @@ def test_roi_align_edges():
     with pytest.raises(_clib.MSDALibraryError):
         _clib.check("msda_roi_align_backward", _clib.load().msda_roi_align_backward(
             None, None, None, None, 0, 1, 4, 4, 8, 1, 2, 2, 1.0, -1, 0, 0, _clib.MSDA_BWD_DETERMINISTIC, None))
+
+
+# ---------------------------------------------------------------------------
+# Layout conversion (msda_transpose) and the layouts of inputs and gradients
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("N,R,C", [(1, 1, 1), (2, 3, 130), (3, 64, 64), (2, 200, 77), (1, 4096, 33),
+                                   (2, 100, 132), (1, 256, 4096)])
+def test_transpose_is_exact(N, R, C, dtype):
+    """Both kernels: the scalar one (ragged sizes) and the 4-element vector
+    one (R and C multiples of 4)."""
+    from msda_triton_b200.gather import _transpose
+    x = torch.randn(N, R, C, generator=torch.Generator().manual_seed(R * C)).to(DEV, dtype)
+    y = _transpose(x, N, R, C)
+    assert torch.equal(y, x.transpose(1, 2).contiguous())
+    assert torch.equal(_transpose(y, N, C, R), x)
+
+
+@pytest.mark.parametrize("channels_last", [False, True], ids=["nchw", "channels_last"])
+def test_gather_ops_keep_the_input_layout(channels_last):
+    """An NCHW input gets an NCHW-contiguous gradient (and a channels_last one
+    a channels_last gradient), for NCHW and channels_last output gradients
+    alike; values match the references."""
+    kw = GS_CASES[0][1]
+    x, grid, gout = _gs_inputs(kw, torch.bfloat16, seed=8)
+    fmt = torch.channels_last if channels_last else torch.contiguous_format
+    xl = x.detach().contiguous(memory_format=fmt).requires_grad_(True)
+    _, gx_r, _ = _gs_reference(x, grid, gout, "zeros", False)
+    for g in (gout, gout.contiguous(memory_format=torch.channels_last)):
+        xl.grad = None
+        out = grid_sample(xl, grid, align_corners=False)
+        out.backward(g)
+        assert xl.grad.is_contiguous(memory_format=fmt)
+        close(xl.grad, gx_r, STRICT_TOL[torch.bfloat16], "grad_input")
+    xr, boxes, scale = _roi_inputs(torch.float32, 32, seed=4)
+    xl = xr.detach().contiguous(memory_format=fmt).requires_grad_(True)
+    out = roi_align(xl, boxes.to(DEV), 4, scale, 2)
+    out.backward(torch.ones_like(out))
+    assert xl.grad.is_contiguous(memory_format=fmt)
+    xd = xr.detach().double().cpu().requires_grad_(True)
+    go.roi_align(xd, boxes, 4, scale, 2).backward(torch.ones(out.shape, dtype=torch.float64))
+    close(xl.grad, xd.grad, STRICT_TOL[torch.float32], "roi grad_input")
