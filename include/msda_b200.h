@@ -246,13 +246,14 @@ MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_sha
 MSDA_API int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, int32_t dtype,
                             void* stream);
 
-/* torch.nn.functional.grid_sample(input, grid, mode="bilinear",
- * padding_mode, align_corners) on NHWC data; padding_mode 0 = "zeros",
- * 1 = "border" ("reflection" is not supported: MSDA_ERR_UNSUPPORTED). */
+/* torch.nn.functional.grid_sample(input, grid, mode, padding_mode,
+ * align_corners) on NHWC data; mode 0 = "bilinear", 1 = "nearest"
+ * ("bicubic" is not supported: MSDA_ERR_UNSUPPORTED); padding_mode
+ * 0 = "zeros", 1 = "border", 2 = "reflection". */
 MSDA_API int msda_grid_sample_forward(const void* input, const void* grid, void* output, int64_t N,
                                       int64_t H, int64_t W, int64_t C, int64_t out_h, int64_t out_w,
-                                      int32_t padding_mode, int32_t align_corners, int32_t dtype,
-                                      void* stream);
+                                      int32_t mode, int32_t padding_mode, int32_t align_corners,
+                                      int32_t dtype, void* stream);
 MSDA_API size_t msda_grid_sample_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C,
                                                          int64_t out_h, int64_t out_w, int32_t dtype,
                                                          uint32_t flags);
@@ -260,9 +261,9 @@ MSDA_API size_t msda_grid_sample_backward_workspace_size(int64_t N, int64_t H, i
 MSDA_API int msda_grid_sample_backward(const void* input, const void* grid, const void* grad_output,
                                        void* grad_input, void* grad_grid, void* workspace,
                                        size_t workspace_bytes, int64_t N, int64_t H, int64_t W,
-                                       int64_t C, int64_t out_h, int64_t out_w, int32_t padding_mode,
-                                       int32_t align_corners, int32_t dtype, uint32_t flags,
-                                       void* stream);
+                                       int64_t C, int64_t out_h, int64_t out_w, int32_t mode,
+                                       int32_t padding_mode, int32_t align_corners, int32_t dtype,
+                                       uint32_t flags, void* stream);
 
 /* torchvision.ops.roi_align(input, rois, (pooled_height, pooled_width),
  * spatial_scale, sampling_ratio, aligned) on NHWC data. An ROI whose batch

@@ -249,14 +249,16 @@ int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, 
 }
 
 int msda_grid_sample_forward(const void* input, const void* grid, void* output, int64_t N, int64_t H,
-                             int64_t W, int64_t C, int64_t out_h, int64_t out_w, int32_t padding_mode,
-                             int32_t align_corners, int32_t dtype, void* stream) {
+                             int64_t W, int64_t C, int64_t out_h, int64_t out_w, int32_t mode,
+                             int32_t padding_mode, int32_t align_corners, int32_t dtype, void* stream) {
   const char* fn = "msda_grid_sample_forward";
   const Dims d{N, H, W, C, N, out_h * out_w};
   if (out_h < 0 || out_w < 0) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: negative output size", fn);
   if (int rc = check_dims(fn, d, dtype)) return rc;
-  if (padding_mode != 0 && padding_mode != 1)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: padding_mode %d not supported (0 = zeros, 1 = border)", fn, padding_mode);
+  if (padding_mode < 0 || padding_mode > 2)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: padding_mode %d not supported (0 = zeros, 1 = border, 2 = reflection)", fn, padding_mode);
+  if (mode != 0 && mode != 1)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: mode %d not supported (0 = bilinear, 1 = nearest)", fn, mode);
   if (d.R * d.Q == 0) return succeed();
   const int es = elem_size(dtype);
   if (!input || !grid || !output) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
@@ -268,7 +270,8 @@ int msda_grid_sample_forward(const void* input, const void* grid, void* output, 
   p.out = output;
   p.N = N; p.R = N; p.Q = d.Q;
   p.H = (int)H; p.W = (int)W; p.C = (int)C;
-  p.border = padding_mode == 1;
+  p.padding = padding_mode;
+  p.nearest = mode == 1;
   p.align = align_corners != 0;
   return forward(fn, Op::kGridSample, p, d, dtype, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -281,14 +284,17 @@ size_t msda_grid_sample_backward_workspace_size(int64_t N, int64_t H, int64_t W,
 
 int msda_grid_sample_backward(const void* input, const void* grid, const void* grad_output, void* grad_input,
                               void* grad_grid, void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
-                              int64_t W, int64_t C, int64_t out_h, int64_t out_w, int32_t padding_mode,
-                              int32_t align_corners, int32_t dtype, uint32_t flags, void* stream) {
+                              int64_t W, int64_t C, int64_t out_h, int64_t out_w, int32_t mode,
+                              int32_t padding_mode, int32_t align_corners, int32_t dtype, uint32_t flags,
+                              void* stream) {
   const char* fn = "msda_grid_sample_backward";
   const Dims d{N, H, W, C, N, out_h * out_w};
   if (out_h < 0 || out_w < 0) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: negative output size", fn);
   if (int rc = check_dims(fn, d, dtype)) return rc;
-  if (padding_mode != 0 && padding_mode != 1)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: padding_mode %d not supported (0 = zeros, 1 = border)", fn, padding_mode);
+  if (padding_mode < 0 || padding_mode > 2)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: padding_mode %d not supported (0 = zeros, 1 = border, 2 = reflection)", fn, padding_mode);
+  if (mode != 0 && mode != 1)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: mode %d not supported (0 = bilinear, 1 = nearest)", fn, mode);
   if (N == 0) return succeed();
   const int es = elem_size(dtype);
   if (!grad_input || (d.Q > 0 && (!input || !grid || !grad_output || !grad_grid)))
@@ -303,7 +309,8 @@ int msda_grid_sample_backward(const void* input, const void* grid, const void* g
   p.grad_grid = grad_grid;
   p.N = N; p.R = N; p.Q = d.Q;
   p.H = (int)H; p.W = (int)W; p.C = (int)C;
-  p.border = padding_mode == 1;
+  p.padding = padding_mode;
+  p.nearest = mode == 1;
   p.align = align_corners != 0;
   return backward(fn, Op::kGridSample, p, d, grad_input, workspace, workspace_bytes, dtype, flags,
                   reinterpret_cast<cudaStream_t>(stream));

@@ -13,11 +13,16 @@
 // 32 / LPR groups each.
 //
 // Semantics follow the public operators they replace:
-// * grid_sample: torch.nn.functional.grid_sample(mode="bilinear",
-//   padding_mode in {"zeros", "border"}, align_corners) on NHWC data; the
-//   source coordinate is ((g + 1) * size - 1) / 2 (align_corners=False) or
-//   (g + 1) / 2 * (size - 1) (True); "border" clips it to [0, size - 1] and
-//   zeroes the grid gradient where it clips; "zeros" samples 0 outside.
+// * grid_sample: torch.nn.functional.grid_sample(mode "bilinear" or
+//   "nearest", padding_mode "zeros", "border" or "reflection",
+//   align_corners) on NHWC data; the source coordinate is
+//   ((g + 1) * size - 1) / 2 (align_corners=False) or (g + 1) / 2 * (size - 1)
+//   (True); "border" clips it to [0, size - 1] and zeroes the grid gradient
+//   where it clips; "reflection" first reflects it about the borders (at
+//   -0.5 and size - 0.5, or at 0 and size - 1 with align_corners; the grid
+//   gradient flips sign on reflected segments), then clips; "zeros"
+//   samples 0 outside. "nearest" reads the pixel at the coordinate rounded
+//   half to even; its grid gradient is zero.
 // * ROI-Align: torchvision.ops.roi_align (Mask R-CNN's RoIAlign): each
 //   output bin averages a grid of sampling points (sampling_ratio per bin
 //   side, or ceil(roi size / bins) when sampling_ratio <= 0); a point more
@@ -44,7 +49,8 @@ struct GatherParams {
   int64_t R, Q;        // output items (grid_sample: N; roi_align: ROIs), output rows per item
   int H, W, C;
   // grid_sample
-  int border;          // padding_mode == "border"
+  int padding;         // 0 "zeros", 1 "border", 2 "reflection"
+  int nearest;         // mode == "nearest" (else bilinear)
   int align;           // align_corners
   // roi_align
   int PH, PW;          // output bins (Q = PH * PW)
@@ -61,11 +67,46 @@ struct GatherParams {
 // ---------------------------------------------------------------------------
 struct GridPoint {
   Bilinear bl;
-  float dx, dy;  // d(pixel coordinate) / d(grid coordinate), 0 where border clips
+  float dx, dy;  // d(pixel coordinate) / d(grid coordinate); 0 where a border clips
 };
 
-// torch's source-index computation (unnormalise, then clip for "border").
-__device__ __forceinline__ float gs_source(float g, int size, int align, int border, float& d) {
+// Clip to [0, size - 1]; the gradient through a clipped coordinate is 0.
+__device__ __forceinline__ float gs_clip(float x, int size, float& d) {
+  const float hi = (float)(size - 1);
+  if (x <= 0.f) {
+    d = 0.f;
+    return 0.f;
+  }
+  if (x >= hi) {
+    d = 0.f;
+    return hi;
+  }
+  return x;
+}
+
+// Reflect about the borders at twice_lo / 2 and twice_hi / 2 (a coordinate
+// past one border comes back from it); d flips sign on reflected segments.
+__device__ __forceinline__ float gs_reflect(float x, int twice_lo, int twice_hi, float& d) {
+  if (twice_lo == twice_hi) {
+    d = 0.f;
+    return 0.f;
+  }
+  const float lo = (float)twice_lo * 0.5f, span = (float)(twice_hi - twice_lo) * 0.5f;
+  x -= lo;
+  if (x < 0.f) {
+    d = -d;
+    x = -x;
+  }
+  const float extra = fmodf(x, span);
+  const int flips = (int)floorf(x / span);
+  if (flips % 2 == 0) return extra + lo;
+  d = -d;
+  return span - extra + lo;
+}
+
+// torch's source-index computation: unnormalise, then clip ("border") or
+// reflect and clip ("reflection"). d = d(coordinate) / d(grid value).
+__device__ __forceinline__ float gs_source(float g, int size, int align, int padding, float& d) {
   float x;
   if (align) {
     x = ((g + 1.f) * 0.5f) * (float)(size - 1);
@@ -74,15 +115,16 @@ __device__ __forceinline__ float gs_source(float g, int size, int align, int bor
     x = ((g + 1.f) * (float)size - 1.f) * 0.5f;
     d = 0.5f * (float)size;
   }
-  if (border) {
-    const float hi = (float)(size - 1);
-    if (x <= 0.f) {
-      x = 0.f;
-      d = 0.f;
-    } else if (x >= hi) {
-      x = hi;
-      d = 0.f;
-    }
+  if (padding == 2) {
+    // A NaN coordinate stays NaN (the bilinear / nearest resolution sends it
+    // outside: it samples nothing); |x| <= 1e9 keeps the reflection's flip
+    // count within int range (span >= 1 pixel whenever size > 1).
+    if (!(x == x)) return x;
+    x = fminf(fmaxf(x, -1.0e9f), 1.0e9f);
+    x = align ? gs_reflect(x, 0, 2 * (size - 1), d) : gs_reflect(x, -1, 2 * size - 1, d);
+    x = gs_clip(x, size, d);
+  } else if (padding == 1) {
+    x = gs_clip(x, size, d);
   }
   return x;
 }
@@ -91,8 +133,22 @@ template <typename T>
 __device__ __forceinline__ GridPoint grid_point(const GatherParams& p, int64_t row) {
   const float2 g = load_pair(reinterpret_cast<const T*>(p.coords) + 2 * row);
   GridPoint r;
-  const float x = gs_source(g.x, p.W, p.align, p.border, r.dx);
-  const float y = gs_source(g.y, p.H, p.align, p.border, r.dy);
+  const float x = gs_source(g.x, p.W, p.align, p.padding, r.dx);
+  const float y = gs_source(g.y, p.H, p.align, p.padding, r.dy);
+  if (p.nearest) {
+    // The pixel at the coordinate rounded half to even, as one corner of
+    // weight 1 (the clamp keeps the integer conversion defined for NaN /
+    // huge coordinates, all of which land outside).
+    const float xr = rintf(fminf(fmaxf(x, -2.0f), (float)p.W + 1.0f));
+    const float yr = rintf(fminf(fmaxf(y, -2.0f), (float)p.H + 1.0f));
+    const int xi = (int)xr, yi = (int)yr;
+    r.bl = empty_slot();
+    r.bl.valid = ((unsigned)xi < (unsigned)p.W && (unsigned)yi < (unsigned)p.H) ? 1u : 0u;
+    r.bl.pix[0] = r.bl.valid ? yi * p.W + xi : 0;
+    r.bl.w[0] = 1.f;
+    r.dx = r.dy = 0.f;  // piecewise constant in the grid
+    return r;
+  }
   LevelInfo L;
   L.H = p.H;
   L.W = p.W;

@@ -67,13 +67,13 @@ SIGNATURES = {
     # Sibling gathers on NHWC data: grid_sample and ROI-Align; the layout conversion.
     "msda_transpose": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I32, _VP]),
     "msda_grid_sample_forward": (
-        ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _VP]),
+        ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _VP]),
     "msda_grid_sample_backward_workspace_size": (
         ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I64, _I64, _I32, ctypes.c_uint32]),
     "msda_grid_sample_backward": (
         ctypes.c_int,
         [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64, _I64,
-         _I32, _I32, _I32, ctypes.c_uint32, _VP],
+         _I32, _I32, _I32, _I32, ctypes.c_uint32, _VP],
     ),
     "msda_roi_align_forward": (
         ctypes.c_int,

@@ -8,7 +8,8 @@ backward"). Both run on the MSDA kernel skeleton in channels-last layout
 drop-ins for the public operators they replace:
 
 * :func:`grid_sample` for ``torch.nn.functional.grid_sample`` (4-D input,
-  ``mode="bilinear"``, ``padding_mode`` "zeros" or "border");
+  ``mode`` "bilinear" or "nearest", ``padding_mode`` "zeros", "border" or
+  "reflection");
 * :func:`roi_align` for ``torchvision.ops.roi_align``.
 
 The kernels read and write NHWC. An input already in ``torch.channels_last``
@@ -27,7 +28,8 @@ from torch.autograd.function import once_differentiable
 from . import _lib
 from .ops import _DTYPE_CODE, _FLOAT_DTYPES, _device_guard, _ptr, _stream, _use_deterministic
 
-_PADDING = {"zeros": 0, "border": 1}
+_PADDING = {"zeros": 0, "border": 1, "reflection": 2}
+_MODE = {"bilinear": 0, "nearest": 1}
 
 
 def _transpose(src: torch.Tensor, N: int, R: int, C: int) -> torch.Tensor:
@@ -94,25 +96,25 @@ def _workspace(nbytes, device):
 # ---------------------------------------------------------------------------
 class _GridSampleFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, grid, padding, align, flags):
+    def forward(ctx, x, grid, mode, padding, align, flags):
         N, H, W, C = x.shape
         _, Ho, Wo, _ = grid.shape
         out = x.new_empty(N, Ho, Wo, C)
         lib = _lib.load()
         with _device_guard(x.device):
             rc = lib.msda_grid_sample_forward(_ptr(x), _ptr(grid), _ptr(out), N, H, W, C, Ho, Wo,
-                                              padding, int(align), _DTYPE_CODE[x.dtype],
+                                              mode, padding, int(align), _DTYPE_CODE[x.dtype],
                                               _stream(x.device))
         _lib.check("msda_grid_sample_forward", rc)
         ctx.save_for_backward(x, grid)
-        ctx.cfg = (padding, align, flags)
+        ctx.cfg = (mode, padding, align, flags)
         return out
 
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_out):
         x, grid = ctx.saved_tensors
-        padding, align, flags = ctx.cfg
+        mode, padding, align, flags = ctx.cfg
         N, H, W, C = x.shape
         _, Ho, Wo, _ = grid.shape
         grad_out = _nhwc_contiguous(grad_out.to(x.dtype))
@@ -125,9 +127,9 @@ class _GridSampleFunction(torch.autograd.Function):
         with _device_guard(x.device):
             rc = lib.msda_grid_sample_backward(
                 _ptr(x), _ptr(grid), _ptr(grad_out), _ptr(grad_in), _ptr(grad_grid), _ptr(ws), nbytes,
-                N, H, W, C, Ho, Wo, padding, int(align), code, flags, _stream(x.device))
+                N, H, W, C, Ho, Wo, mode, padding, int(align), code, flags, _stream(x.device))
         _lib.check("msda_grid_sample_backward", rc)
-        return grad_in, grad_grid, None, None, None
+        return grad_in, grad_grid, None, None, None, None
 
 
 def grid_sample(
@@ -145,9 +147,8 @@ def grid_sample(
     Args:
         input: ``(N, C, H, W)``; channels-last memory avoids a copy.
         grid: ``(N, H_out, W_out, 2)`` normalised ``(x, y)`` in ``[-1, 1]``.
-        mode: ``"bilinear"`` (``"nearest"`` / ``"bicubic"`` are not built).
-        padding_mode: ``"zeros"`` or ``"border"`` (``"reflection"`` is not
-            built).
+        mode: ``"bilinear"`` or ``"nearest"`` (``"bicubic"`` is not built).
+        padding_mode: ``"zeros"``, ``"border"`` or ``"reflection"``.
         align_corners: as in torch; ``None`` means ``False``.
         fp32_grad_accum: accumulate the input gradient in fp32 (default for
             fp16/bf16) or with native half-precision atomics.
@@ -165,13 +166,11 @@ def grid_sample(
                          f"got {tuple(grid.shape)}")
     if mode not in ("bilinear", "nearest", "bicubic"):
         raise ValueError(f"grid_sample: expected mode to be 'bilinear', 'nearest' or 'bicubic', got '{mode}'")
-    if mode != "bilinear":
-        raise NotImplementedError(f"grid_sample: mode='{mode}' is not built (bilinear only)")
+    if mode == "bicubic":
+        raise NotImplementedError("grid_sample: mode='bicubic' is not built (bilinear and nearest are)")
     if padding_mode not in ("zeros", "border", "reflection"):
         raise ValueError("grid_sample: expected padding_mode to be 'zeros', 'border' or 'reflection', "
                          f"got '{padding_mode}'")
-    if padding_mode == "reflection":
-        raise NotImplementedError("grid_sample: padding_mode='reflection' is not built")
     if input.dtype != grid.dtype:
         raise ValueError(f"grid_sample: input and grid dtypes must match, got {input.dtype}/{grid.dtype}")
     if input.dtype not in _FLOAT_DTYPES:
@@ -182,7 +181,7 @@ def grid_sample(
         raise ValueError(f"grid_sample: empty input {tuple(input.shape)}")
     _lib.load()
     flags = _bwd_flags(input.dtype, fp32_grad_accum, _use_deterministic(deterministic))
-    out = _GridSampleFunction.apply(_nhwc(input), grid.contiguous(), _PADDING[padding_mode],
+    out = _GridSampleFunction.apply(_nhwc(input), grid.contiguous(), _MODE[mode], _PADDING[padding_mode],
                                     bool(align_corners), flags)
     return out.permute(0, 3, 1, 2)
 

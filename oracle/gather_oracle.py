@@ -9,11 +9,14 @@ Neither operator lives in /root/reference; their published definitions are
 those of the third-party operators the B200 versions replace, installed in
 this image and used to pin the restatements (tests/test_gather_oracle.py):
 
-* :func:`grid_sample_bilinear` restates ``torch.nn.functional.grid_sample``
-  (torch 2.11.0; mode="bilinear", padding_mode "zeros" / "border",
-  align_corners): source index ((g + 1) * size - 1) / 2 or
-  (g + 1) / 2 * (size - 1), clipped to [0, size - 1] for "border", bilinear
-  weights of the four neighbours, zero outside the map.
+* :func:`grid_sample` restates ``torch.nn.functional.grid_sample``
+  (torch 2.11.0; mode "bilinear" / "nearest", padding_mode "zeros" /
+  "border" / "reflection", align_corners): source index
+  ((g + 1) * size - 1) / 2 or (g + 1) / 2 * (size - 1), clipped to
+  [0, size - 1] for "border", reflected about the borders (at -0.5 and
+  size - 0.5, or 0 and size - 1 with align_corners) and then clipped for
+  "reflection"; bilinear weights of the four neighbours, or the neighbour at
+  the coordinate rounded half to even for "nearest"; zero outside the map.
 * :func:`roi_align` restates ``torchvision.ops.roi_align`` (torchvision
   0.26.0; the RoIAlign of Mask R-CNN, He et al. 2017): per output bin, the
   mean over a grid of sampling points (sampling_ratio per side, or
@@ -32,8 +35,19 @@ import math
 import torch
 
 
-def grid_sample_bilinear(input: torch.Tensor, grid: torch.Tensor, padding_mode: str = "zeros",
-                         align_corners: bool = False) -> torch.Tensor:
+def _reflect(x: torch.Tensor, twice_lo: int, twice_hi: int) -> torch.Tensor:
+    """x reflected about twice_lo / 2 and twice_hi / 2 until it lies between them."""
+    if twice_lo == twice_hi:
+        return torch.zeros_like(x)
+    lo, span = twice_lo / 2, (twice_hi - twice_lo) / 2
+    d = (x - lo).abs()
+    extra = torch.fmod(d, span)
+    flips = torch.floor(d / span)
+    return torch.where(torch.fmod(flips, 2) == 0, extra + lo, span - extra + lo)
+
+
+def grid_sample(input: torch.Tensor, grid: torch.Tensor, mode: str = "bilinear",
+                padding_mode: str = "zeros", align_corners: bool = False) -> torch.Tensor:
     """(N, C, H, W), (N, Ho, Wo, 2) -> (N, C, Ho, Wo)."""
     N, C, H, W = input.shape
 
@@ -42,15 +56,23 @@ def grid_sample_bilinear(input: torch.Tensor, grid: torch.Tensor, padding_mode: 
             x = ((g + 1) / 2) * (size - 1)
         else:
             x = ((g + 1) * size - 1) / 2
-        if padding_mode == "border":
+        if padding_mode == "reflection":
+            x = _reflect(x, 0, 2 * (size - 1)) if align_corners else _reflect(x, -1, 2 * size - 1)
+        if padding_mode in ("border", "reflection"):
             x = x.clamp(0, size - 1)
         return x
 
     x = source(grid[..., 0], W)
     y = source(grid[..., 1], H)
+    img = input.permute(0, 2, 3, 1)  # (N, H, W, C)
+    if mode == "nearest":
+        xi, yi = x.detach().round(), y.detach().round()  # half to even
+        valid = (xi >= 0) & (xi < W) & (yi >= 0) & (yi < H)
+        n = torch.arange(N).view(N, 1, 1).expand_as(xi)
+        v = img[n, yi.clamp(0, H - 1).long(), xi.clamp(0, W - 1).long()]
+        return (v * valid[..., None]).permute(0, 3, 1, 2)
     x0, y0 = x.detach().floor(), y.detach().floor()
     lx, ly = x - x0, y - y0
-    img = input.permute(0, 2, 3, 1)  # (N, H, W, C)
     n = torch.arange(N).view(N, 1, 1).expand_as(x0)
     out = 0
     for dy, dx, w in ((0, 0, (1 - lx) * (1 - ly)), (0, 1, lx * (1 - ly)),

@@ -160,11 +160,13 @@ def test_gather_abi_checks_before_any_device_work():
     vp = ctypes.c_void_p
     gs = lambda **o: lib.msda_grid_sample_forward(  # noqa: E731
         vp(o.get("x", 16)), vp(o.get("g", 16)), vp(o.get("y", 16)), o.get("N", 1), o.get("H", 4),
-        o.get("W", 4), o.get("C", 8), o.get("Ho", 2), o.get("Wo", 2), o.get("pad", 0), 0,
+        o.get("W", 4), o.get("C", 8), o.get("Ho", 2), o.get("Wo", 2), o.get("mode", 0), o.get("pad", 0), 0,
         o.get("dtype", 0), vp(0))
     assert gs(dtype=9) == _lib.MSDA_ERR_UNSUPPORTED
-    assert gs(pad=2) == _lib.MSDA_ERR_UNSUPPORTED  # reflection is not built
+    assert gs(pad=3) == _lib.MSDA_ERR_UNSUPPORTED
     assert b"padding_mode" in lib.msda_last_error()
+    assert gs(mode=2) == _lib.MSDA_ERR_UNSUPPORTED  # bicubic is not built
+    assert b"mode" in lib.msda_last_error()
     assert gs(H=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert gs(C=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert gs(x=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
@@ -194,10 +196,10 @@ def test_gather_op_validation():
     g = torch.zeros(1, 3, 3, 2)
     with pytest.raises(ValueError, match="mode"):
         grid_sample(x, g, mode="linear")
-    with pytest.raises(NotImplementedError, match="nearest"):
-        grid_sample(x, g, mode="nearest")
-    with pytest.raises(NotImplementedError, match="reflection"):
-        grid_sample(x, g, padding_mode="reflection")
+    with pytest.raises(NotImplementedError, match="bicubic"):
+        grid_sample(x, g, mode="bicubic")
+    with pytest.raises(ValueError, match="padding_mode"):
+        grid_sample(x, g, padding_mode="wrap")
     with pytest.raises(ValueError, match="grid"):
         grid_sample(x, torch.zeros(2, 3, 3, 2))
     with pytest.raises(ValueError, match="CUDA"):

@@ -22,19 +22,23 @@ def _grid_inputs(seed, N=2, C=5, H=7, W=9, Ho=6, Wo=8, lo=-1.2, hi=1.2):
 
 
 @pytest.mark.parametrize("align", [False, True])
-@pytest.mark.parametrize("padding", ["zeros", "border"])
-def test_grid_sample_restatement_matches_torch(padding, align):
-    x, grid = _grid_inputs(0)
+@pytest.mark.parametrize("padding", ["zeros", "border", "reflection"])
+@pytest.mark.parametrize("mode", ["bilinear", "nearest"])
+def test_grid_sample_restatement_matches_torch(mode, padding, align):
+    # Grids reaching well past the borders, so that reflection folds more than once.
+    x, grid = _grid_inputs(0, lo=-3.2, hi=3.2)
     a = [t.clone().requires_grad_(True) for t in (x, grid)]
     b = [t.clone().requires_grad_(True) for t in (x, grid)]
-    out = go.grid_sample_bilinear(*a, padding_mode=padding, align_corners=align)
-    ref = F.grid_sample(*b, mode="bilinear", padding_mode=padding, align_corners=align)
+    out = go.grid_sample(*a, mode=mode, padding_mode=padding, align_corners=align)
+    ref = F.grid_sample(*b, mode=mode, padding_mode=padding, align_corners=align)
     torch.testing.assert_close(out, ref, rtol=1e-12, atol=1e-12)
     g = torch.randn_like(ref)
     out.backward(g)
     ref.backward(g)
     torch.testing.assert_close(a[0].grad, b[0].grad, rtol=1e-12, atol=1e-12)
-    torch.testing.assert_close(a[1].grad, b[1].grad, rtol=1e-10, atol=1e-10)
+    # "nearest" is piecewise constant in the grid: no gradient (torch: zeros).
+    ga = a[1].grad if a[1].grad is not None else torch.zeros_like(grid)
+    torch.testing.assert_close(ga, b[1].grad, rtol=1e-10, atol=1e-10)
 
 
 def _boxes(seed, K=6, N=2, H=20, W=24, scale=0.5):

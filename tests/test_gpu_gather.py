@@ -62,11 +62,11 @@ def _gs_inputs(kw, dtype, seed=0, lo=-1.15, hi=1.15):
     return (x.to(DEV, dtype), grid.to(DEV, dtype), gout.to(DEV, dtype))
 
 
-def _gs_reference(x, grid, gout, padding, align):
+def _gs_reference(x, grid, gout, padding, align, mode="bilinear"):
     """torch's CPU grid_sample in float64 on the same rounded inputs, with autograd."""
     xr = x.detach().double().cpu().requires_grad_(True)
     gr = grid.detach().double().cpu().requires_grad_(True)
-    out = F.grid_sample(xr, gr, mode="bilinear", padding_mode=padding, align_corners=align)
+    out = F.grid_sample(xr, gr, mode=mode, padding_mode=padding, align_corners=align)
     out.backward(gout.double().cpu())
     return out.detach(), xr.grad, gr.grad
 
@@ -88,11 +88,13 @@ def _run_gs(x, grid, gout, padding, align, **kw):
 
 
 @pytest.mark.parametrize("align", [False, True], ids=["ac0", "ac1"])
-@pytest.mark.parametrize("padding", ["zeros", "border"])
+@pytest.mark.parametrize("padding", ["zeros", "border", "reflection"])
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
 @pytest.mark.parametrize("name,kw", GS_CASES, ids=[c[0] for c in GS_CASES])
 def test_grid_sample_matches_torch(name, kw, dtype, padding, align):
-    x, grid, gout = _gs_inputs(kw, dtype)
+    # Reflection: grids reaching well past the borders (several folds).
+    span = 2.6 if padding == "reflection" else 1.15
+    x, grid, gout = _gs_inputs(kw, dtype, lo=-span, hi=span)
     out, gx, gg = _run_gs(x, grid, gout, padding, align)
     assert out.shape == (kw["N"], kw["C"], kw["Ho"], kw["Wo"]) and out.dtype == dtype
     ref, gx_r, gg_r = _gs_reference(x, grid, gout, padding, align)
@@ -113,12 +115,38 @@ def test_grid_sample_matches_torch(name, kw, dtype, padding, align):
     torch.testing.assert_close((gg.double().cpu() / scale)[keep], (gg_r / scale)[keep], **tol)
 
 
+@pytest.mark.parametrize("align", [False, True], ids=["ac0", "ac1"])
+@pytest.mark.parametrize("padding", ["zeros", "border", "reflection"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("name,kw", GS_CASES[:3], ids=[c[0] for c in GS_CASES[:3]])
+def test_grid_sample_nearest_matches_torch(name, kw, dtype, padding, align):
+    """mode="nearest": the pixel at the coordinate rounded half to even.
+    Grid values are bf16-representable for every dtype, so the pixel
+    coordinate is exact in fp32 and ties round the same way on both sides."""
+    x, grid, gout = _gs_inputs(kw, dtype, seed=2, lo=-1.6, hi=1.6)
+    grid = grid.to(torch.bfloat16).to(dtype)
+    xl = x.clone().requires_grad_(True)
+    gl = grid.clone().requires_grad_(True)
+    out = grid_sample(xl, gl, mode="nearest", padding_mode=padding, align_corners=align)
+    out.backward(gout)
+    ref, gx_r, _ = _gs_reference(x, grid, gout, padding, align, mode="nearest")
+    tol = STRICT_TOL[dtype]
+    close(out, ref, tol, "out")
+    close(xl.grad, gx_r, tol, "grad_input")
+    assert (gl.grad == 0).all()
+    # The deterministic accumulation gives the same input gradient.
+    xd = x.clone().requires_grad_(True)
+    grid_sample(xd, grid, mode="nearest", padding_mode=padding, align_corners=align,
+                deterministic=True).backward(gout)
+    close(xd.grad, gx_r, tol, "grad_input (deterministic)")
+
+
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
 def test_grid_sample_matches_the_oracle(dtype):
     x, grid, gout = _gs_inputs(GS_CASES[0][1], dtype, seed=3)
     out, gx, _ = _run_gs(x, grid, gout, "zeros", False)
     xr = x.double().cpu().requires_grad_(True)
-    ref = go.grid_sample_bilinear(xr, grid.double().cpu(), "zeros", False)
+    ref = go.grid_sample(xr, grid.double().cpu(), "bilinear", "zeros", False)
     ref.backward(gout.double().cpu())
     close(out, ref.detach(), STRICT_TOL[dtype], "out")
     close(gx, xr.grad, STRICT_TOL[dtype], "grad_input")
