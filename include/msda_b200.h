@@ -235,8 +235,8 @@ MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_sha
  *   rois         (num_rois, 5) fp32     (batch index, x1, y1, x2, y2)
  *   output       (num_rois, pooled_height, pooled_width, C)   roi_align
  * Backward flags: MSDA_BWD_FP32_ACCUM (fp32 workspace + downcast for
- * fp16/bf16), MSDA_BWD_DETERMINISTIC (grid_sample only: 64-bit fixed-point
- * accumulation, bitwise reproducible); the workspace size depends on them.
+ * fp16/bf16), MSDA_BWD_DETERMINISTIC (64-bit fixed-point accumulation,
+ * bitwise reproducible); the workspace size depends on them.
  * grad_input need not be zeroed by the caller.
  */
 

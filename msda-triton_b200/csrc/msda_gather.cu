@@ -81,7 +81,9 @@ cudaError_t launch_fwd(bool roi, const GatherParams& p, const msda::Cfg& c, cuda
 template <typename T>
 cudaError_t launch_bwd(bool roi, const GatherParams& p, const msda::Cfg& c, Acc acc, bool pdl, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
-  if (roi) {  // no fixed-point variant
+  if (roi) {
+    if (acc == Acc::kFixed)
+      return c.vec == V16 ? roi_bwd<T, long long, V16>(p, c, pdl, st) : roi_bwd<T, long long, 1>(p, c, pdl, st);
     if (acc == Acc::kF32 || sizeof(T) == 4)
       return c.vec == V16 ? roi_bwd<T, float, V16>(p, c, pdl, st) : roi_bwd<T, float, 1>(p, c, pdl, st);
     return c.vec == V16 ? roi_bwd<T, T, V16>(p, c, pdl, st) : roi_bwd<T, T, 1>(p, c, pdl, st);
@@ -122,8 +124,6 @@ size_t workspace_bytes_for(const Dims& d, int32_t dtype, uint32_t flags) {
 int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_input, void* workspace,
              size_t ws_bytes, int32_t dtype, uint32_t flags, cudaStream_t st) {
   const bool fixed = (flags & MSDA_BWD_DETERMINISTIC) != 0;
-  if (fixed && op == Op::kRoiAlign)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_DETERMINISTIC is not offered for roi_align", fn);
   const bool f32_ws = !fixed && (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
   const int es = elem_size(dtype);
   const size_t need = workspace_bytes_for(d, dtype, flags);
@@ -153,7 +153,11 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
   p.grad_in = target;
   if (fixed) {
     p.fixed_hdr = static_cast<const unsigned*>(workspace);
-    p.fixed_log2n = ceil_log2(std::max<int64_t>(d.Q, 1));
+    // Bound on the terms of one input pixel's sum, each at most max|grad_out|
+    // (interpolation weights <= 1): grid_sample, the output pixels of its
+    // image; ROI-Align, every output bin (a bin's sampling weights average
+    // to 1, so its contributions to one pixel sum to at most max|grad_out|).
+    p.fixed_log2n = ceil_log2(std::max<int64_t>(op == Op::kRoiAlign ? d.R * d.Q : d.Q, 1));
     const int64_t ng = d.R * d.Q * d.C;
     unsigned* hdr = static_cast<unsigned*>(workspace);
     switch (dtype) {
@@ -349,7 +353,6 @@ int msda_roi_align_forward(const void* input, const float* rois, void* output, i
 size_t msda_roi_align_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C, int32_t dtype,
                                               uint32_t flags) {
   if (elem_size(dtype) == 0 || N < 0 || H < 1 || W < 1 || C < 1) return 0;
-  if (flags & MSDA_BWD_DETERMINISTIC) return 0;  // not offered
   return workspace_bytes_for(Dims{N, H, W, C, 0, 0}, dtype, flags);
 }
 
@@ -361,8 +364,6 @@ int msda_roi_align_backward(const float* rois, const void* grad_output, void* gr
   const char* fn = "msda_roi_align_backward";
   const Dims d{N, H, W, C, num_rois, (int64_t)pooled_height * pooled_width};
   if (int rc = roi_checks(fn, d, pooled_height, pooled_width, dtype)) return rc;
-  if (flags & MSDA_BWD_DETERMINISTIC)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_DETERMINISTIC is not offered for roi_align", fn);
   if (N == 0) return succeed();
   const int es = elem_size(dtype);
   if (!grad_input || (num_rois > 0 && (!rois || !grad_output)))

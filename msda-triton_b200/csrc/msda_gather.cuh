@@ -514,7 +514,8 @@ __global__ void __launch_bounds__(kGatherWarps * 32) roi_bwd_kernel(const Gather
   const RoiBin b = roi_bin(p, row);
   RowScatter<T, A, VEC, LPR, CPL> sc;
   sc.load(reinterpret_cast<const T*>(p.grad_out) + row * p.C, true, sub, p.C);
-  pdl_wait();  // the zero-fill of the scatter target
+  pdl_wait();  // the zero-fill (and absmax header) of the scatter target
+  sc.set_scale(p.fixed_hdr, p.fixed_log2n);
   if (b.n < 0 || b.n >= p.N) return;
   A* gb = reinterpret_cast<A*>(p.grad_in) + (int64_t)b.n * p.H * p.W * p.C;
   for (int iy = 0; iy < b.gh; ++iy)

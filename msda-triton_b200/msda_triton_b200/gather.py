@@ -232,9 +232,6 @@ class _RoiAlignFunction(torch.autograd.Function):
     def backward(ctx, grad_out):
         (rois,) = ctx.saved_tensors
         shape, dtype, (PH, PW), spatial_scale, sampling_ratio, aligned, flags = ctx.cfg
-        if torch.are_deterministic_algorithms_enabled():
-            raise RuntimeError("roi_align backward has no deterministic implementation (as in "
-                               "torchvision); disable torch.use_deterministic_algorithms for it")
         N, H, W, C = shape
         grad_out = _nhwc_contiguous(grad_out.to(dtype))
         grad_in = grad_out.new_empty(shape)
@@ -260,6 +257,7 @@ def roi_align(
     aligned: bool = False,
     *,
     fp32_grad_accum: bool | None = None,
+    deterministic: bool | None = None,
 ) -> torch.Tensor:
     """``torchvision.ops.roi_align`` on B200.
 
@@ -272,6 +270,9 @@ def roi_align(
         spatial_scale, sampling_ratio, aligned: as in torchvision.
         fp32_grad_accum: accumulate the input gradient in fp32 (default for
             fp16/bf16) or with native half-precision atomics.
+        deterministic: bitwise-reproducible input gradient (64-bit
+            fixed-point accumulation; torchvision's backward has none);
+            ``None`` follows ``torch.are_deterministic_algorithms_enabled()``.
 
     Returns:
         ``(K, C, height, width)`` in ``input.dtype``, channels-last memory.
@@ -289,7 +290,7 @@ def roi_align(
         raise ValueError(f"roi_align: output_size must be an int or (height, width) >= 1, got {output_size}")
     _lib.load()
     rois = _rois(boxes, input.device)
-    flags = _bwd_flags(input.dtype, fp32_grad_accum, False)
+    flags = _bwd_flags(input.dtype, fp32_grad_accum, _use_deterministic(deterministic))
     out = _RoiAlignFunction.apply(_nhwc(input), rois, out_hw, float(spatial_scale), int(sampling_ratio),
                                   bool(aligned), flags)
     return out.permute(0, 3, 1, 2)

@@ -180,14 +180,15 @@ def test_gather_abi_checks_before_any_device_work():
     assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_F32, _lib.MSDA_BWD_DETERMINISTIC) == 256 + n * 8
     rws = lib.msda_roi_align_backward_workspace_size
     assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, _lib.MSDA_BWD_FP32_ACCUM) == n * 4
-    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, _lib.MSDA_BWD_DETERMINISTIC) == 0
+    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, _lib.MSDA_BWD_DETERMINISTIC) == 256 + n * 8
     ra = lambda **o: lib.msda_roi_align_forward(  # noqa: E731
         vp(16), vp(16), vp(16), 1, 4, 4, 8, o.get("K", 3), o.get("ph", 2), 2, 1.0, -1, 0, 0, vp(0))
     assert ra(ph=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert ra(K=0) == _lib.MSDA_OK
+    # The deterministic backward needs its fixed-point workspace.
     rc = lib.msda_roi_align_backward(vp(16), vp(16), vp(16), vp(0), 0, 1, 4, 4, 8, 3, 2, 2, 1.0, -1, 0,
                                      0, _lib.MSDA_BWD_DETERMINISTIC, vp(0))
-    assert rc == _lib.MSDA_ERR_UNSUPPORTED
+    assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
 
 
 def test_gather_op_validation():

@@ -16,7 +16,6 @@ import torch.nn.functional as F
 
 import cases
 from cases import REF_BWD_TOL, STRICT_TOL
-from msda_triton_b200 import _lib as _clib
 from msda_triton_b200 import grid_sample, roi_align
 from oracle import gather_oracle as go
 
@@ -263,19 +262,36 @@ def test_roi_align_edges():
     assert (out[0] == 0).all()
     ref = torchvision.ops.roi_align(x.double().cpu(), bad[1:].double().cpu(), 3, 1.0, -1, True)
     close(out[1:], ref, dict(rtol=1e-5, atol=1e-6), "degenerate box")
-    # The backward refuses deterministic mode, as torchvision's does.
-    xl = x.clone().requires_grad_(True)
+
+
+@pytest.mark.parametrize("sampling_ratio", [-1, 2], ids=["adaptive", "sr2"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+def test_roi_align_deterministic(dtype, sampling_ratio):
+    """The fixed-point input gradient: within the strict bar of the oracle,
+    bitwise equal across runs, under a permutation of the boxes (which
+    reorders every atomic), and under torch.use_deterministic_algorithms
+    (where torchvision's backward raises)."""
+    x, boxes, scale = _roi_inputs(dtype, 32, seed=6, K=24)
+    gout = torch.randn(24, 32, 5, 4, generator=torch.Generator().manual_seed(4)).to(DEV, dtype)
+
+    def grad(b, g, **kw):
+        xl = x.clone().requires_grad_(True)
+        roi_align(xl, b.to(DEV), (5, 4), scale, sampling_ratio, True, **kw).backward(g)
+        return xl.grad
+
+    g1 = grad(boxes, gout, deterministic=True)
+    assert _bitwise_equal(g1, grad(boxes, gout, deterministic=True))
+    perm = torch.randperm(24, generator=torch.Generator().manual_seed(8))
+    assert _bitwise_equal(g1, grad(boxes[perm], gout[perm.to(DEV)], deterministic=True))
     before = torch.are_deterministic_algorithms_enabled()
     try:
         torch.use_deterministic_algorithms(True)
-        out = roi_align(xl, boxes.to(DEV), 3, scale)
-        with pytest.raises(RuntimeError, match="deterministic"):
-            out.sum().backward()
+        assert _bitwise_equal(g1, grad(boxes, gout))
     finally:
         torch.use_deterministic_algorithms(before)
-    with pytest.raises(_clib.MSDALibraryError):
-        _clib.check("msda_roi_align_backward", _clib.load().msda_roi_align_backward(
-            None, None, None, None, 0, 1, 4, 4, 8, 1, 2, 2, 1.0, -1, 0, 0, _clib.MSDA_BWD_DETERMINISTIC, None))
+    xr = x.double().cpu().requires_grad_(True)
+    go.roi_align(xr, boxes, (5, 4), scale, sampling_ratio, True).backward(gout.double().cpu())
+    close(g1, xr.grad, STRICT_TOL[dtype], "grad_input (deterministic)")
 
 
 # ---------------------------------------------------------------------------
