@@ -588,9 +588,12 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
           for (int j = 0; j < CPL; ++j) {
             const int ch = (j * LPR + sub) * VEC;
             if constexpr (FIXED) {
-              // Fixed-point reduction in interleaved channels (see gi); a
-              // counted one-hit row is stored in the natural layout.
-              if (MODE != kCounted || hits != 1u) {
+              // Fixed-point reduction in interleaved channels (see gi). In
+              // the counted mode a one-hit row is stored and a two-hit row
+              // reduced in fp32 (below): fp32 addition is commutative, so
+              // 0 + a + b == 0 + b + a bitwise and two terms need no fixed
+              // point; three or more (and dense-level rows) do.
+              if (MODE != kCounted || hits > 2u) {
                 long long* row = (MODE == kCounted ? faccb : reinterpret_cast<long long*>(gvb)) + pix * rs;
                 if (fx.ok) {
                   const double wd = (double)wc * fx.scale;  // exact
@@ -643,6 +646,9 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
                   store_vec<T, VEC>(gvt + pix * rs + ch, contrib);
                 else if constexpr (!FIXED)
                   red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
+                else  // two hits: fp32 in the first half of the 64-bit row
+                  red_add_vec_hint<float, VEC>(reinterpret_cast<float*>(faccb + pix * rs) + ch, contrib,
+                                               pol_keep);
               } else if constexpr (!FIXED) {
                 red_add_vec_hint<A, VEC>(gvb + pix * rs + ch, contrib, pol_keep);
               }
@@ -1331,7 +1337,11 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
         for (int k = 0; k < VEC; ++k) v[k] = 0.f;
       } else if constexpr (FIXED) {
         const long long* a = reinterpret_cast<const long long*>(p.acc) + e;
-        if constexpr (VEC % 2 == 0) {
+        if (cnt[r] == 2u) {  // two hits: an fp32 row at the start of the 64-bit row
+          const float* f = reinterpret_cast<const float*>(a - chunk * VEC) + chunk * VEC;
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[k] = __ldcs(f + k);
+        } else if constexpr (VEC % 2 == 0) {
 #pragma unroll
           for (int k = 0; k < VEC; k += 2) {
             const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(a + k));
