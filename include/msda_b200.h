@@ -87,7 +87,9 @@ typedef enum msda_status {
  * contributions a * w_c * g are rounded once to 64-bit fixed point and
  * accumulated with integer reductions, whose sum does not depend on the
  * order the atomics land in, then each element is rounded once to the
- * value dtype. Results are bitwise reproducible from run to run for the same
+ * value dtype (the hit-counted algorithm stores rows hit once and reduces
+ * rows hit exactly twice in fp32: two commutative adds into zero are
+ * order-independent too). Results are bitwise reproducible from run to run for the same
  * inputs. The fixed-point scale is set on the device from max|attention
  * weight| (1 for the fused prologue's softmax weights) and max|grad_output|
  * so that no row sum can overflow; one contribution's rounding error is below
