@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config decoder]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
     python bench.py --impl reference ...   # the reference's CPU implementation
+    python bench.py --op grid_sample|roi_align   # the sibling gathers (1 GPU)
 
 A step is one forward + backward of the multi-scale deformable attention op
 over one batch of the configured operating point (default: the
@@ -29,6 +30,11 @@ Reported (one JSON line on rank 0):
   cpu_baseline  the reference's CPU implementation (grid_sample forward +
              autograd backward, restated in oracle/msda_oracle.py) on the
              host cores, rank 0 at N=1.
+
+With --op grid_sample / roi_align the line covers the sibling gathers on
+their own workloads (GATHER_WORKLOADS), next to the operators they replace
+(torch's grid_sample, torchvision's roi_align) timed the same way on the
+same GPU; the headline benchmark is the default (--op msda).
 """
 
 from __future__ import annotations
