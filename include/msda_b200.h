@@ -192,9 +192,9 @@ MSDA_API int msda_backward(const void* value, const int64_t* spatial_shapes, con
  * the reference, which always allocates its fp32 buffer with torch).
  *
  * A caller that plans all device memory ahead of time and may not call
- * cudaMalloc while it runs (a TensorRT-style plugin's enqueue, code running
- * under CUDA graph capture in a mode that makes allocation an error, an
- * embedder without a device allocator) cannot hand msda_backward the fp32
+ * cudaMalloc while it runs (a TensorRT-style plugin's enqueue, which must
+ * not allocate outside its planned buffers; an embedder without a device
+ * allocator of its own) cannot hand msda_backward the fp32
  * workspace it needs for fp32 accumulation of fp16/bf16 gradients. This entry
  * point computes the same three gradients as msda_backward with
  * MSDA_BWD_FP32_ACCUM | MSDA_BWD_FORCE_SCATTER, taking that workspace from a

@@ -3,9 +3,7 @@
 // Some callers have no way to obtain a scratch buffer at the moment they run
 // the backward: a runtime that plans every device buffer ahead of time and
 // forbids cudaMalloc on its execution path (a TensorRT-style plugin's enqueue,
-// for instance), code that runs while a CUDA graph is being captured in a
-// mode that makes allocation an error, or an embedder with no device
-// allocator of its own. msda_backward needs an fp32 workspace from its caller
+// for instance), or an embedder with no device allocator of its own. msda_backward needs an fp32 workspace from its caller
 // whenever it accumulates fp16/bf16 gradients in fp32 with the scatter
 // kernel; msda_backward_noalloc runs that same kernel sequence with the
 // workspace taken from a fixed-size array compiled into the library.

@@ -2,8 +2,8 @@
 
 msda_backward_noalloc exists for callers that may not call cudaMalloc while
 they run -- a runtime that plans all device memory ahead of time (a
-TensorRT-style plugin's enqueue), code under CUDA graph capture in a mode that
-makes allocation an error, an embedder without a device allocator. Instead of
+TensorRT-style plugin's enqueue), an embedder without a device allocator of
+its own. Instead of
 a caller-provided fp32 workspace it uses a static device array inside the
 library (16 MiB). These tests call it through the C ABI and check it against
 msda_backward, the regular entry point, on two calls in a row: the shared
