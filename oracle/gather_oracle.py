@@ -5,7 +5,7 @@ MSDA (docs/course/08-exercises.md:39), used as the checkers of the sm_100a
 grid_sample and ROI-Align kernels. Only ``tests/`` may import this module;
 the product path (``msda_triton_b200``) never does.
 
-Neither operator lives in /root/reference; their published definitions are
+Neither operator is part of the reference; their published definitions are
 those of the third-party operators the B200 versions replace, installed in
 this image and used to pin the restatements (tests/test_gather_oracle.py):
 
