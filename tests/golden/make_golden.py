@@ -1,7 +1,8 @@
 """Generate the golden vectors under tests/golden/ from the REFERENCE's own code.
 
-Runs only where the reference checkout is present (default
-/root/reference, override with MSDA_REFERENCE). It imports, by file path:
+Runs only where the reference checkout is present (its path in
+MSDA_REFERENCE; the default is the read-only checkout the committed vectors
+were made from). It imports, by file path:
 
 * tests/reference_impls.py -- ``msda_reference`` (grid_sample) and
   ``msda_naive`` (loops), the reference's CPU implementations;
