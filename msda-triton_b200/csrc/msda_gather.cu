@@ -229,23 +229,28 @@ int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, 
   if (!src || !dst) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   if (!aligned(src, es) || !aligned(dst, es)) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer", fn);
   constexpr int TL = msda::kTransposeTile;
-  const int64_t gx = (C + TL - 1) / TL, gy = (R + TL - 1) / TL;
+  const int64_t tc = (C + TL - 1) / TL, tr = (R + TL - 1) / TL;  // column / row tiles
+  // The larger tile count goes on gridDim.x (2^31 - 1); the other must fit
+  // gridDim.y (65535).
+  const int r_in_x = tr > 65535 ? 1 : 0;
+  const int64_t gx = r_in_x ? tr : tc, gy = r_in_x ? tc : tr;
   if (gx > 0x7fffffff || gy > 65535 || N > 65535)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: sizes too large (N <= 65535, R <= %d)", fn, 65535 * TL);
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: sizes too large (N <= 65535, min(R, C) <= %d)", fn, 65535 * TL);
   const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)N);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (R % 4 == 0 && C % 4 == 0 && R * C < (int64_t(1) << 31) && aligned(src, 4 * es) && aligned(dst, 4 * es)) {
     if (es == 4)
       msda::transpose4_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst),
-                                                          (int)R, (int)C);
+                                                          (int)R, (int)C, r_in_x);
     else
       msda::transpose4_kernel<unsigned short><<<grid, 256, 0, st>>>(
-          static_cast<const unsigned short*>(src), static_cast<unsigned short*>(dst), (int)R, (int)C);
+          static_cast<const unsigned short*>(src), static_cast<unsigned short*>(dst), (int)R, (int)C, r_in_x);
   } else if (es == 4) {
-    msda::transpose_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst), R, C);
+    msda::transpose_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst), R, C,
+                                                        r_in_x);
   } else {
     msda::transpose_kernel<unsigned short><<<grid, 256, 0, st>>>(static_cast<const unsigned short*>(src),
-                                                               static_cast<unsigned short*>(dst), R, C);
+                                                               static_cast<unsigned short*>(dst), R, C, r_in_x);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "transpose launch");

@@ -533,17 +533,19 @@ __global__ void __launch_bounds__(kGatherWarps * 32) roi_bwd_kernel(const Gather
 // R or C = H*W). A 64 x 64 tile goes through shared memory (a row pitch of
 // an odd number of 4-byte words keeps the column reads conflict-free), so
 // both the loads and the stores are coalesced along the contiguous axis of
-// their tensor.
+// their tensor. The grid is (column tiles, row tiles, N), or (row tiles,
+// column tiles, N) with `r_in_x` when the row tiles exceed gridDim.y's limit.
 // ---------------------------------------------------------------------------
 constexpr int kTransposeTile = 64;
 
 template <typename T>
 __global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                        int64_t R, int64_t C) {
+                                                        int64_t R, int64_t C, int r_in_x) {
   constexpr int TL = kTransposeTile;
   __shared__ T tile[TL][TL + 4 / sizeof(T)];
   const int64_t n = blockIdx.z;
-  const int64_t r0 = (int64_t)blockIdx.y * TL, c0 = (int64_t)blockIdx.x * TL;
+  const int64_t r0 = (int64_t)(r_in_x ? blockIdx.x : blockIdx.y) * TL;
+  const int64_t c0 = (int64_t)(r_in_x ? blockIdx.y : blockIdx.x) * TL;
   const T* s = src + n * R * C;
   T* d = dst + n * R * C;
   const int tx = threadIdx.x & (TL - 1), ty = threadIdx.x / TL;  // 64 x 4 threads
@@ -566,12 +568,12 @@ __global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ sr
 // either side, and offsets are 32-bit.
 template <typename T>
 __global__ void __launch_bounds__(256) transpose4_kernel(const T* __restrict__ src, T* __restrict__ dst,
-                                                         int R, int C) {
+                                                         int R, int C, int r_in_x) {
   constexpr int TL = kTransposeTile;
   using V4 = typename RawVec<4 * sizeof(T)>::type;  // 4 elements
   __shared__ T tile[TL][TL + 1];
   const int64_t n = blockIdx.z;
-  const int r0 = blockIdx.y * TL, c0 = blockIdx.x * TL;
+  const int r0 = (r_in_x ? blockIdx.x : blockIdx.y) * TL, c0 = (r_in_x ? blockIdx.y : blockIdx.x) * TL;
   const T* s = src + n * (int64_t)R * C;
   T* d = dst + n * (int64_t)R * C;
   const int lo = threadIdx.x & 15, hi = threadIdx.x >> 4;  // 16 x 16 threads

@@ -299,7 +299,9 @@ def test_roi_align_deterministic(dtype, sampling_ratio):
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
 @pytest.mark.parametrize("N,R,C", [(1, 1, 1), (2, 3, 130), (3, 64, 64), (2, 200, 77), (1, 4096, 33),
-                                   (2, 100, 132), (1, 256, 4096)])
+                                   (2, 100, 132), (1, 256, 4096),
+                                   # more than 65535 row tiles (an NHWC image above 2048 x 2048)
+                                   (1, 64 * 65536 + 5, 3), (1, 64 * 65536 + 4, 8)])
 def test_transpose_is_exact(N, R, C, dtype):
     """Both kernels: the scalar one (ragged sizes) and the 4-element vector
     one (R and C multiples of 4)."""
