@@ -17,9 +17,18 @@ constexpr int64_t kMaxPixels = int64_t(1) << 30;
 #define MSDA_GATHER_SHAPES(X) \
   X(1, 1) X(2, 1) X(4, 1) X(8, 1) X(16, 1) X(32, 1) X(32, 2) X(32, 4)
 
-dim3 gather_grid(const GatherParams& p, const msda::Cfg& c) {
+int64_t gather_ctas(int64_t rows, const msda::Cfg& c) {
   const int64_t rows_per_cta = (int64_t)msda::kGatherWarps * (32 / c.lpr);
-  return dim3((unsigned)((p.R * p.Q + rows_per_cta - 1) / rows_per_cta));
+  return (rows + rows_per_cta - 1) / rows_per_cta;
+}
+
+// One-dimensional grid over the output rows; its size is checked against
+// gridDim.x's limit by `grid_fits` before any launch.
+dim3 gather_grid(const GatherParams& p, const msda::Cfg& c) { return dim3((unsigned)gather_ctas(p.R * p.Q, c)); }
+
+int grid_fits(const char* fn, int64_t rows, const msda::Cfg& c) {
+  if (gather_ctas(rows, c) > 0x7fffffff) return fail(MSDA_ERR_UNSUPPORTED, "%s: too many output rows for one grid", fn);
+  return MSDA_OK;
 }
 
 template <typename T, int VEC>
@@ -136,6 +145,12 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
   void* target = fixed ? static_cast<void*>(static_cast<char*>(workspace) + 256) : f32_ws ? workspace : grad_input;
   void* zdst = fixed ? workspace : target;
   const size_t zbytes = need ? need : gi_bytes;
+  msda::Cfg cfg;
+  if (d.R * d.Q > 0) {  // every check before the first launch
+    const bool vec_ok = aligned(p.input ? p.input : p.grad_out, 16) && aligned(p.grad_out, 16) && aligned(target, 16);
+    if (int rc = choose_cfg((int32_t)d.C, es, vec_ok, &cfg)) return rc;
+    if (int rc = grid_fits(fn, d.R * d.Q, cfg)) return rc;
+  }
   cudaError_t e;
   bool pdl = false;
   if (zbytes % 16 == 0 && aligned(zdst, 16)) {
@@ -147,9 +162,6 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
   if (e != cudaSuccess) return cuda_fail(e, "zero-fill");
   // Nothing to scatter and no accumulator to round: grad_input is the zeros.
   if (d.R * d.Q == 0 && !need) return succeed();
-  msda::Cfg cfg;
-  const bool vec_ok = aligned(p.input ? p.input : p.grad_out, 16) && aligned(p.grad_out, 16) && aligned(target, 16);
-  if (int rc = choose_cfg((int32_t)d.C, es, vec_ok, &cfg)) return rc;
   p.grad_in = target;
   if (fixed) {
     p.fixed_hdr = static_cast<const unsigned*>(workspace);
@@ -203,6 +215,7 @@ int forward(const char* fn, Op op, GatherParams& p, const Dims& d, int32_t dtype
   const int es = elem_size(dtype);
   msda::Cfg cfg;
   if (int rc = choose_cfg((int32_t)d.C, es, aligned(p.input, 16) && aligned(p.out, 16), &cfg)) return rc;
+  if (int rc = grid_fits(fn, d.R * d.Q, cfg)) return rc;
   cudaError_t e;
   const bool roi = op == Op::kRoiAlign;
   switch (dtype) {
@@ -211,7 +224,6 @@ int forward(const char* fn, Op op, GatherParams& p, const Dims& d, int32_t dtype
     default: e = launch_fwd<__nv_bfloat16>(roi, p, cfg, st); break;
   }
   if (e != cudaSuccess) return cuda_fail(e, "forward launch");
-  (void)fn;
   return succeed();
 }
 
