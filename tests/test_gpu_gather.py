@@ -264,6 +264,32 @@ def test_roi_align_edges():
     close(out[1:], ref, dict(rtol=1e-5, atol=1e-6), "degenerate box")
 
 
+@pytest.mark.parametrize("deterministic", [False, True], ids=["fp32", "fixed"])
+@pytest.mark.parametrize("sampling_ratio", [-1, 2, 5], ids=["adaptive", "sr2", "sr5"])
+def test_roi_align_reversed_and_tiny_boxes(sampling_ratio, deterministic):
+    """Boxes with x2 < x1 or y2 < y1 (aligned=True keeps the negative bin
+    size, so the samples run backwards), sub-pixel boxes whose samples share
+    pixels, and boxes hanging over the border, forward and backward."""
+    x, boxes, scale = _roi_inputs(torch.float32, 64, seed=11, K=16)
+    rev = boxes.clone()
+    rev[:8, [1, 3]] = boxes[:8, [3, 1]]        # x reversed
+    rev[4:12, [2, 4]] = boxes[4:12, [4, 2]]    # y reversed (4 boxes both)
+    rev[12:, 3:] = rev[12:, 1:3] + 0.7 / scale  # under one pixel per side
+    rev[15, 1:] = torch.tensor([-3.0, -2.0, 0.5, 0.8]) / scale  # mostly outside
+    xl = x.clone().requires_grad_(True)
+    out = roi_align(xl, rev.to(DEV), (4, 3), scale, sampling_ratio, True, deterministic=deterministic)
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(12)).to(DEV)
+    out.backward(gout)
+    xr = x.double().cpu().requires_grad_(True)
+    ref = go.roi_align(xr, rev, (4, 3), scale, sampling_ratio, True)
+    ref.backward(gout.double().cpu())
+    close(out, ref.detach(), STRICT_TOL[torch.float32], "out")
+    close(xl.grad, xr.grad, STRICT_TOL[torch.float32], "grad_input")
+    if sampling_ratio > 0:  # torchvision's CPU kernel rejects an adaptive grid on a reversed box
+        tv = torchvision.ops.roi_align(x.double().cpu(), rev.double(), (4, 3), scale, sampling_ratio, True)
+        close(out, tv, dict(rtol=1e-4, atol=1e-4), "out vs torchvision")
+
+
 @pytest.mark.parametrize("sampling_ratio", [-1, 2], ids=["adaptive", "sr2"])
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
 def test_roi_align_deterministic(dtype, sampling_ratio):
