@@ -18,9 +18,10 @@
  *
  * Ownership: the caller allocates every buffer, including the optional
  * backward workspace; the library never allocates device memory.
- * Threading: the library is stateless apart from a thread-local error string;
- * all work is enqueued on the given stream with no host synchronisation, so
- * the calls may be captured in a CUDA graph.
+ * Threading: apart from a thread-local error string and the static scratch
+ * array of msda_backward_noalloc (described there), the library holds no
+ * state; every call enqueues its work on the given stream with no host
+ * synchronisation.
  * Errors: every entry point returns an msda_status (0 = success); the message
  * of the last failure on the calling thread is available from
  * msda_last_error(). A CUDA launch error is reported as MSDA_ERR_CUDA.
@@ -101,6 +102,15 @@ typedef enum msda_status {
  * one. MSDA_BWD_FP32_ACCUM is implied; MSDA_BWD_FORCE_OWNER is rejected.
  * Needs a workspace (msda_backward_workspace_size with this flag). */
 #define MSDA_BWD_DETERMINISTIC 16u
+/* Sibling gathers only (msda_grid_sample_backward, msda_roi_align_backward;
+ * msda_backward rejects it): grad_input is written (N, C, H, W) contiguous
+ * instead of (N, H, W, C). The reductions then always go into the NHWC
+ * workspace (fp32, 64-bit fixed point, or the data type when neither
+ * MSDA_BWD_FP32_ACCUM nor MSDA_BWD_DETERMINISTIC applies), and one pass
+ * converts and transposes it into grad_input: the NCHW gradient of an NCHW
+ * input without a separate msda_transpose call. The workspace size queries
+ * take the same flag. */
+#define MSDA_BWD_GRAD_INPUT_NCHW 32u
 
 /* Library version string, e.g. "msda_b200 0.1.0 sm_100a". */
 MSDA_API const char* msda_version(void);
@@ -238,7 +248,8 @@ MSDA_API int msda_backward_noalloc(const void* value, const int64_t* spatial_sha
  *   output       (num_rois, pooled_height, pooled_width, C)   roi_align
  * Backward flags: MSDA_BWD_FP32_ACCUM (fp32 workspace + downcast for
  * fp16/bf16), MSDA_BWD_DETERMINISTIC (64-bit fixed-point accumulation,
- * bitwise reproducible); the workspace size depends on them.
+ * bitwise reproducible), MSDA_BWD_GRAD_INPUT_NCHW (grad_input written
+ * (N, C, H, W)); the workspace size depends on them.
  * grad_input need not be zeroed by the caller.
  */
 
@@ -259,7 +270,8 @@ MSDA_API int msda_grid_sample_forward(const void* input, const void* grid, void*
 MSDA_API size_t msda_grid_sample_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C,
                                                          int64_t out_h, int64_t out_w, int32_t dtype,
                                                          uint32_t flags);
-/* grad_input (N, H, W, C) and grad_grid (N, out_h, out_w, 2). */
+/* grad_input (N, H, W, C), or (N, C, H, W) with MSDA_BWD_GRAD_INPUT_NCHW,
+ * and grad_grid (N, out_h, out_w, 2). */
 MSDA_API int msda_grid_sample_backward(const void* input, const void* grid, const void* grad_output,
                                        void* grad_input, void* grad_grid, void* workspace,
                                        size_t workspace_bytes, int64_t N, int64_t H, int64_t W,
@@ -277,7 +289,8 @@ MSDA_API int msda_roi_align_forward(const void* input, const float* rois, void* 
                                     void* stream);
 MSDA_API size_t msda_roi_align_backward_workspace_size(int64_t N, int64_t H, int64_t W, int64_t C,
                                                        int32_t dtype, uint32_t flags);
-/* grad_input (N, H, W, C); the boxes get no gradient (as in torchvision). */
+/* grad_input (N, H, W, C), or (N, C, H, W) with MSDA_BWD_GRAD_INPUT_NCHW;
+ * the boxes get no gradient (as in torchvision). */
 MSDA_API int msda_roi_align_backward(const float* rois, const void* grad_output, void* grad_input,
                                      void* workspace, size_t workspace_bytes, int64_t N, int64_t H,
                                      int64_t W, int64_t C, int64_t num_rois, int32_t pooled_height,

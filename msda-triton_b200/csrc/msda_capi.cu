@@ -269,6 +269,8 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
     return fail(MSDA_ERR_UNSUPPORTED, "%s: the owner algorithm does not take the fused prologue", fn);
   if ((flags & MSDA_BWD_DETERMINISTIC) && (flags & MSDA_BWD_FORCE_OWNER))
     return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_DETERMINISTIC and MSDA_BWD_FORCE_OWNER are exclusive", fn);
+  if (flags & MSDA_BWD_GRAD_INPUT_NCHW)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_GRAD_INPUT_NCHW is a flag of the sibling gathers", fn);
   if (s.B == 0) return succeed();
   const int es = elem_size(dtype);
   const size_t gv_bytes = (size_t)s.B * s.S * s.M * s.D * es;

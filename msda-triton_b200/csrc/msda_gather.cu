@@ -119,12 +119,58 @@ int check_dims(const char* fn, const Dims& d, int32_t dtype) {
   return MSDA_OK;
 }
 
+// Grid of the tiled transposes for (N, R, C) -> (N, C, R): (column tiles,
+// row tiles, N), with the row tiles on gridDim.x (`r_in_x`) when they exceed
+// gridDim.y's 65535. False when the sizes do not fit one grid.
+bool transpose_grid(int64_t N, int64_t R, int64_t C, dim3* grid, int* r_in_x) {
+  constexpr int TL = msda::kTransposeTile;
+  const int64_t tc = (C + TL - 1) / TL, tr = (R + TL - 1) / TL;
+  *r_in_x = tr > 65535 ? 1 : 0;
+  const int64_t gx = *r_in_x ? tr : tc, gy = *r_in_x ? tc : tr;
+  if (gx > 0x7fffffff || gy > 65535 || N > 65535) return false;
+  *grid = dim3((unsigned)gx, (unsigned)gy, (unsigned)N);
+  return true;
+}
+
+// The 4-element-vector kernels apply: R and C multiples of 4, a batch slice
+// below 2^31 elements, both buffers aligned to 4 elements of their type.
+bool transpose_vec4(int64_t R, int64_t C, const void* src, int src_es, const void* dst, int dst_es) {
+  return R % 4 == 0 && C % 4 == 0 && R * C < (int64_t(1) << 31) && aligned(src, 4 * src_es) &&
+         aligned(dst, 4 * dst_es);
+}
+
+// Accumulator (NHWC, type S) -> grad_input (NCHW, data type D).
+template <typename S, typename D>
+cudaError_t launch_convert_transpose(const S* src, D* dst, int64_t N, int64_t R, int64_t C, const unsigned* hdr,
+                                     int clog2n, cudaStream_t st) {
+  dim3 grid;
+  int r_in_x;
+  transpose_grid(N, R, C, &grid, &r_in_x);  // checked before the first launch of the call
+  if (transpose_vec4(R, C, src, sizeof(S), dst, sizeof(D)))
+    return msda::launch_ex(msda::convert_transpose_kernel<S, D, true>, grid, dim3(256), 0, st, true, src, dst, R, C,
+                           r_in_x, hdr, clog2n);
+  return msda::launch_ex(msda::convert_transpose_kernel<S, D, false>, grid, dim3(256), 0, st, true, src, dst, R, C,
+                         r_in_x, hdr, clog2n);
+}
+
+template <typename D>
+cudaError_t launch_grad_nchw(int acc_kind, const void* ws, void* grad_input, int64_t N, int64_t R, int64_t C,
+                             const unsigned* hdr, int clog2n, cudaStream_t st) {
+  D* dst = static_cast<D*>(grad_input);
+  switch (acc_kind) {
+    case 2: return launch_convert_transpose(static_cast<const long long*>(ws), dst, N, R, C, hdr, clog2n, st);
+    case 1: return launch_convert_transpose(static_cast<const float*>(ws), dst, N, R, C, hdr, clog2n, st);
+    default: return launch_convert_transpose(static_cast<const D*>(ws), dst, N, R, C, hdr, clog2n, st);
+  }
+}
+
 enum class Op { kGridSample, kRoiAlign };
 
 size_t workspace_bytes_for(const Dims& d, int32_t dtype, uint32_t flags) {
   const size_t elems = (size_t)d.N * d.H * d.W * d.C;
   if (flags & MSDA_BWD_DETERMINISTIC) return 256 + elems * sizeof(long long);
   if ((flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32) return elems * sizeof(float);
+  if (flags & MSDA_BWD_GRAD_INPUT_NCHW) return elems * elem_size(dtype);
   return 0;
 }
 
@@ -134,6 +180,7 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
              size_t ws_bytes, int32_t dtype, uint32_t flags, cudaStream_t st) {
   const bool fixed = (flags & MSDA_BWD_DETERMINISTIC) != 0;
   const bool f32_ws = !fixed && (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
+  const bool nchw = (flags & MSDA_BWD_GRAD_INPUT_NCHW) != 0;  // workspace + converting transpose
   const int es = elem_size(dtype);
   const size_t need = workspace_bytes_for(d, dtype, flags);
   const size_t gi_bytes = (size_t)d.N * d.H * d.W * d.C * es;
@@ -142,11 +189,20 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
       return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: needs a workspace of %zu bytes (got %zu)", fn, need, ws_bytes);
     if (!aligned(workspace, 16)) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
   }
-  void* target = fixed ? static_cast<void*>(static_cast<char*>(workspace) + 256) : f32_ws ? workspace : grad_input;
+  void* target = fixed ? static_cast<void*>(static_cast<char*>(workspace) + 256)
+                 : (f32_ws || nchw) ? workspace
+                                    : grad_input;
   void* zdst = fixed ? workspace : target;
   const size_t zbytes = need ? need : gi_bytes;
   msda::Cfg cfg;
-  if (d.R * d.Q > 0) {  // every check before the first launch
+  if (nchw) {  // every check before the first launch
+    dim3 g;
+    int r_in_x;
+    if (!transpose_grid(d.N, d.H * d.W, d.C, &g, &r_in_x))
+      return fail(MSDA_ERR_UNSUPPORTED, "%s: the NCHW input gradient needs N <= 65535 and C <= %d", fn,
+                  65535 * msda::kTransposeTile);
+  }
+  if (d.R * d.Q > 0) {
     const bool vec_ok = aligned(p.input ? p.input : p.grad_out, 16) && aligned(p.grad_out, 16) && aligned(target, 16);
     if (int rc = choose_cfg((int32_t)d.C, es, vec_ok, &cfg)) return rc;
     if (int rc = grid_fits(fn, d.R * d.Q, cfg)) return rc;
@@ -192,7 +248,16 @@ int backward(const char* fn, Op op, GatherParams& p, const Dims& d, void* grad_i
   }
   const int64_t n = d.N * d.H * d.W * d.C;
   const bool cast_vec = aligned(grad_input, 16) && aligned(target, 16);
-  if (fixed) {
+  if (nchw) {
+    const int kind = fixed ? 2 : f32_ws ? 1 : 0;  // accumulator: fixed point, fp32, data type
+    const int64_t hw = d.H * d.W;
+    switch (dtype) {
+      case MSDA_DTYPE_F32: e = launch_grad_nchw<float>(kind, target, grad_input, d.N, hw, d.C, p.fixed_hdr, p.fixed_log2n, st); break;
+      case MSDA_DTYPE_F16: e = launch_grad_nchw<__half>(kind, target, grad_input, d.N, hw, d.C, p.fixed_hdr, p.fixed_log2n, st); break;
+      default: e = launch_grad_nchw<__nv_bfloat16>(kind, target, grad_input, d.N, hw, d.C, p.fixed_hdr, p.fixed_log2n, st); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "NCHW input gradient launch");
+  } else if (fixed) {
     const long long* src = static_cast<const long long*>(target);
     switch (dtype) {
       case MSDA_DTYPE_F32: e = msda::launch_cast_fixed<float>(src, static_cast<float*>(grad_input), n, cast_vec, p.fixed_hdr, p.fixed_log2n, sm_count(), st); break;
@@ -240,17 +305,13 @@ int msda_transpose(const void* src, void* dst, int64_t N, int64_t R, int64_t C, 
   if (N == 0 || R == 0 || C == 0) return succeed();
   if (!src || !dst) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   if (!aligned(src, es) || !aligned(dst, es)) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer", fn);
-  constexpr int TL = msda::kTransposeTile;
-  const int64_t tc = (C + TL - 1) / TL, tr = (R + TL - 1) / TL;  // column / row tiles
-  // The larger tile count goes on gridDim.x (2^31 - 1); the other must fit
-  // gridDim.y (65535).
-  const int r_in_x = tr > 65535 ? 1 : 0;
-  const int64_t gx = r_in_x ? tr : tc, gy = r_in_x ? tc : tr;
-  if (gx > 0x7fffffff || gy > 65535 || N > 65535)
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: sizes too large (N <= 65535, min(R, C) <= %d)", fn, 65535 * TL);
-  const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)N);
+  dim3 grid;
+  int r_in_x;
+  if (!transpose_grid(N, R, C, &grid, &r_in_x))
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: sizes too large (N <= 65535, min(R, C) <= %d)", fn,
+                65535 * msda::kTransposeTile);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (R % 4 == 0 && C % 4 == 0 && R * C < (int64_t(1) << 31) && aligned(src, 4 * es) && aligned(dst, 4 * es)) {
+  if (transpose_vec4(R, C, src, es, dst, es)) {
     if (es == 4)
       msda::transpose4_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst),
                                                           (int)R, (int)C, r_in_x);

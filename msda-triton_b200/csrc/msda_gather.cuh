@@ -600,4 +600,82 @@ __global__ void __launch_bounds__(256) transpose4_kernel(const T* __restrict__ s
   }
 }
 
+// Converting transpose, the last pass of a gather backward that writes an
+// NCHW input gradient: the NHWC accumulator (S = fp32, 64-bit fixed point
+// scaled by the header, or the data type) of shape (N, R = H*W, C) becomes
+// dst (N, C, R) in the data type D, each element rounded once. The tiling
+// of transpose4_kernel (V4: 4-element accesses, R and C multiples of 4,
+// a batch slice below 2^31 elements) or transpose_kernel (any size), with
+// the conversion to fp32 on the way into shared memory.
+template <typename S, typename D, bool V4>
+__global__ void __launch_bounds__(256) convert_transpose_kernel(const S* __restrict__ src, D* __restrict__ dst,
+                                                                int64_t R, int64_t C, int r_in_x,
+                                                                const unsigned* hdr, int clog2n) {
+  constexpr int TL = kTransposeTile;
+  __shared__ float tile[TL][TL + 1];
+  pdl_wait();  // the accumulator rows (and the fixed-point header) come from the backward
+  FixedScale fx{};
+  if constexpr (IsFixed<S>::value) fx = fixed_scale(hdr, clog2n);
+  const int64_t n = blockIdx.z;
+  const int64_t r0 = (int64_t)(r_in_x ? blockIdx.x : blockIdx.y) * TL;
+  const int64_t c0 = (int64_t)(r_in_x ? blockIdx.y : blockIdx.x) * TL;
+  const S* s = src + n * R * C;
+  D* d = dst + n * R * C;
+  auto cvt = [&](S v) -> float {
+    if constexpr (IsFixed<S>::value) return fixed_to_f32(v, fx);
+    else return to_f32(v);
+  };
+  if constexpr (V4) {
+    const int lo = threadIdx.x & 15, hi = threadIdx.x >> 4;  // 16 x 16 threads
+    const int Ri = (int)R, Ci = (int)C;
+#pragma unroll
+    for (int k = 0; k < TL; k += 16) {
+      const int r = (int)r0 + hi + k, c = (int)c0 + 4 * lo;
+      if (r < Ri && c < Ci) {
+        const S* p = s + r * Ci + c;
+        float v[4];
+        if constexpr (sizeof(S) == 8) {
+          const longlong2 a = __ldcs(reinterpret_cast<const longlong2*>(p));
+          const longlong2 b = __ldcs(reinterpret_cast<const longlong2*>(p) + 1);
+          v[0] = cvt(a.x); v[1] = cvt(a.y); v[2] = cvt(b.x); v[3] = cvt(b.y);
+        } else if constexpr (sizeof(S) == 4) {
+          const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        } else {
+          union { uint2 u; S e[4]; } a;
+          a.u = __ldcs(reinterpret_cast<const uint2*>(p));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = cvt(a.e[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tile[hi + k][4 * lo + e] = v[e];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < TL; k += 16) {
+      const int c = (int)c0 + hi + k, r = (int)r0 + 4 * lo;
+      if (c < Ci && r < Ri) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = tile[4 * lo + e][hi + k];
+        store_vec<D, 4>(d + c * Ri + r, v);
+      }
+    }
+  } else {
+    const int tx = threadIdx.x & (TL - 1), ty = threadIdx.x / TL;  // 64 x 4 threads
+#pragma unroll
+    for (int k = 0; k < TL; k += 4) {
+      const int64_t r = r0 + ty + k, c = c0 + tx;
+      if (r < R && c < C) tile[ty + k][tx] = cvt(__ldcs(s + r * C + c));
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < TL; k += 4) {
+      const int64_t c = c0 + ty + k, r = r0 + tx;
+      if (c < C && r < R) d[c * R + r] = from_f32<D>(tile[tx][ty + k]);
+    }
+  }
+}
+
 }  // namespace msda

@@ -27,6 +27,7 @@ MSDA_BWD_FORCE_SCATTER = 2
 MSDA_BWD_FORCE_OWNER = 4
 MSDA_BWD_FORCE_COUNTED = 8
 MSDA_BWD_DETERMINISTIC = 16
+MSDA_BWD_GRAD_INPUT_NCHW = 32
 
 # Every symbol include/msda_b200.h declares, with (restype, argtypes).
 _VP = ctypes.c_void_p

@@ -13,11 +13,13 @@ drop-ins for the public operators they replace:
 * :func:`roi_align` for ``torchvision.ops.roi_align``.
 
 The kernels read and write NHWC. An input already in ``torch.channels_last``
-memory format is used as is; an NCHW-contiguous input (and an NCHW output
-gradient) is converted by the library's tiled transpose kernel
-(``msda_transpose``), and the input gradient is returned in the input's
-layout. The outputs are channels-last NCHW tensors (same shape and values as
-the replaced operators, a different memory format). There is no CPU path.
+memory format is used as is; an NCHW input (and an NCHW output gradient) is
+converted by the library's tiled transpose kernel (``msda_transpose``), and
+the input gradient is returned in the input's layout: for an NCHW input the
+backward writes it NCHW directly (``MSDA_BWD_GRAD_INPUT_NCHW``: the
+accumulator is rounded and transposed in one pass, no separate transpose).
+The outputs are channels-last NCHW tensors (same shape and values as the
+replaced operators, a different memory format). There is no CPU path.
 """
 
 from __future__ import annotations
@@ -43,8 +45,10 @@ def _transpose(src: torch.Tensor, N: int, R: int, C: int) -> torch.Tensor:
 
 
 class _ToNHWC(torch.autograd.Function):
-    """NCHW -> contiguous NHWC with the transpose kernel; the gradient goes
-    back to contiguous NCHW the same way."""
+    """NCHW -> contiguous NHWC with the transpose kernel. The gathers'
+    backward writes the input gradient NCHW (MSDA_BWD_GRAD_INPUT_NCHW) and
+    hands it back as an (N, H, W, C)-shaped view, which passes through here
+    as is; any other gradient goes back to NCHW with the transpose kernel."""
 
     @staticmethod
     def forward(ctx, x):
@@ -54,17 +58,36 @@ class _ToNHWC(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, g):
+        nchw = g.permute(0, 3, 1, 2)
+        if nchw.is_contiguous():
+            return nchw
         N, H, W, C = g.shape
         return _transpose(_nhwc_contiguous(g), N, H * W, C).view(N, C, H, W)
 
 
-def _nhwc(x: torch.Tensor) -> torch.Tensor:
-    """(N, C, H, W) -> contiguous (N, H, W, C): a view of a channels_last
-    tensor, else one transpose kernel."""
+def _nhwc(x: torch.Tensor, flags: int) -> tuple[torch.Tensor, bool]:
+    """(N, C, H, W) -> (contiguous (N, H, W, C), whether the backward writes
+    the input gradient NCHW): a view of a channels_last tensor, else one
+    transpose kernel. The NCHW gradient is asked for where the backward has
+    a rounding pass anyway (fixed point, or fp32 accumulation of 16-bit
+    data), which then transposes for free; elsewhere it would only move the
+    transpose into the library."""
     v = x.permute(0, 2, 3, 1)
     if v.is_contiguous():
-        return v
-    return _ToNHWC.apply(x)
+        return v, False
+    rounds = bool(flags & _lib.MSDA_BWD_DETERMINISTIC) or (
+        bool(flags & _lib.MSDA_BWD_FP32_ACCUM) and x.dtype != torch.float32)
+    return _ToNHWC.apply(x), rounds
+
+
+def _grad_input(like: torch.Tensor, nhwc_shape, nchw: bool) -> torch.Tensor:
+    """The input gradient's buffer (dtype and device of `like`) as an
+    (N, H, W, C)-shaped tensor: NHWC memory, or NCHW memory seen through a
+    permute (the layout MSDA_BWD_GRAD_INPUT_NCHW writes)."""
+    N, H, W, C = nhwc_shape
+    if nchw:
+        return like.new_empty(N, C, H, W).permute(0, 2, 3, 1)
+    return like.new_empty(N, H, W, C)
 
 
 def _nhwc_contiguous(t: torch.Tensor) -> torch.Tensor:
@@ -96,7 +119,7 @@ def _workspace(nbytes, device):
 # ---------------------------------------------------------------------------
 class _GridSampleFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, grid, mode, padding, align, flags):
+    def forward(ctx, x, grid, mode, padding, align, flags, nchw):
         N, H, W, C = x.shape
         _, Ho, Wo, _ = grid.shape
         out = x.new_empty(N, Ho, Wo, C)
@@ -107,18 +130,18 @@ class _GridSampleFunction(torch.autograd.Function):
                                               _stream(x.device))
         _lib.check("msda_grid_sample_forward", rc)
         ctx.save_for_backward(x, grid)
-        ctx.cfg = (mode, padding, align, flags)
+        ctx.cfg = (mode, padding, align, flags | (_lib.MSDA_BWD_GRAD_INPUT_NCHW if nchw else 0), nchw)
         return out
 
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_out):
         x, grid = ctx.saved_tensors
-        mode, padding, align, flags = ctx.cfg
+        mode, padding, align, flags, nchw = ctx.cfg
         N, H, W, C = x.shape
         _, Ho, Wo, _ = grid.shape
         grad_out = _nhwc_contiguous(grad_out.to(x.dtype))
-        grad_in = torch.empty_like(x)
+        grad_in = _grad_input(x, x.shape, nchw)
         grad_grid = torch.empty_like(grid)
         lib = _lib.load()
         code = _DTYPE_CODE[x.dtype]
@@ -129,7 +152,7 @@ class _GridSampleFunction(torch.autograd.Function):
                 _ptr(x), _ptr(grid), _ptr(grad_out), _ptr(grad_in), _ptr(grad_grid), _ptr(ws), nbytes,
                 N, H, W, C, Ho, Wo, mode, padding, int(align), code, flags, _stream(x.device))
         _lib.check("msda_grid_sample_backward", rc)
-        return grad_in, grad_grid, None, None, None, None
+        return grad_in, grad_grid, None, None, None, None, None
 
 
 def grid_sample(
@@ -181,8 +204,9 @@ def grid_sample(
         raise ValueError(f"grid_sample: empty input {tuple(input.shape)}")
     _lib.load()
     flags = _bwd_flags(input.dtype, fp32_grad_accum, _use_deterministic(deterministic))
-    out = _GridSampleFunction.apply(_nhwc(input), grid.contiguous(), _MODE[mode], _PADDING[padding_mode],
-                                    bool(align_corners), flags)
+    x, nchw = _nhwc(input, flags)
+    out = _GridSampleFunction.apply(x, grid.contiguous(), _MODE[mode], _PADDING[padding_mode],
+                                    bool(align_corners), flags, nchw)
     return out.permute(0, 3, 1, 2)
 
 
@@ -212,7 +236,7 @@ def _rois(boxes, device) -> torch.Tensor:
 
 class _RoiAlignFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, rois, out_hw, spatial_scale, sampling_ratio, aligned, flags):
+    def forward(ctx, x, rois, out_hw, spatial_scale, sampling_ratio, aligned, flags, nchw):
         N, H, W, C = x.shape
         K = rois.shape[0]
         PH, PW = out_hw
@@ -224,17 +248,18 @@ class _RoiAlignFunction(torch.autograd.Function):
                                             _DTYPE_CODE[x.dtype], _stream(x.device))
         _lib.check("msda_roi_align_forward", rc)
         ctx.save_for_backward(rois)
-        ctx.cfg = (tuple(x.shape), x.dtype, out_hw, spatial_scale, sampling_ratio, aligned, flags)
+        ctx.cfg = (tuple(x.shape), x.dtype, out_hw, spatial_scale, sampling_ratio, aligned,
+                   flags | (_lib.MSDA_BWD_GRAD_INPUT_NCHW if nchw else 0), nchw)
         return out
 
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_out):
         (rois,) = ctx.saved_tensors
-        shape, dtype, (PH, PW), spatial_scale, sampling_ratio, aligned, flags = ctx.cfg
+        shape, dtype, (PH, PW), spatial_scale, sampling_ratio, aligned, flags, nchw = ctx.cfg
         N, H, W, C = shape
         grad_out = _nhwc_contiguous(grad_out.to(dtype))
-        grad_in = grad_out.new_empty(shape)
+        grad_in = _grad_input(grad_out, shape, nchw)
         lib = _lib.load()
         code = _DTYPE_CODE[dtype]
         nbytes = lib.msda_roi_align_backward_workspace_size(N, H, W, C, code, flags)
@@ -245,7 +270,7 @@ class _RoiAlignFunction(torch.autograd.Function):
                 PH, PW, float(spatial_scale), int(sampling_ratio), int(aligned), code, flags,
                 _stream(grad_out.device))
         _lib.check("msda_roi_align_backward", rc)
-        return grad_in, None, None, None, None, None, None
+        return grad_in, None, None, None, None, None, None, None
 
 
 def roi_align(
@@ -291,6 +316,7 @@ def roi_align(
     _lib.load()
     rois = _rois(boxes, input.device)
     flags = _bwd_flags(input.dtype, fp32_grad_accum, _use_deterministic(deterministic))
-    out = _RoiAlignFunction.apply(_nhwc(input), rois, out_hw, float(spatial_scale), int(sampling_ratio),
-                                  bool(aligned), flags)
+    x, nchw = _nhwc(input, flags)
+    out = _RoiAlignFunction.apply(x, rois, out_hw, float(spatial_scale), int(sampling_ratio),
+                                  bool(aligned), flags, nchw)
     return out.permute(0, 3, 1, 2)

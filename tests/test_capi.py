@@ -191,6 +191,38 @@ def test_gather_abi_checks_before_any_device_work():
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
 
 
+def test_gather_nchw_gradient_flag():
+    """MSDA_BWD_GRAD_INPUT_NCHW: the header value, the workspace it adds
+    (the accumulator in the data type when no other flag asks for one), its
+    refusal by the MSDA backward, and its size checks before any launch."""
+    text = HEADER.read_text()
+    assert re.search(r"#define MSDA_BWD_GRAD_INPUT_NCHW (\d+)u", text).group(1) == str(_lib.MSDA_BWD_GRAD_INPUT_NCHW)
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    NCHW = _lib.MSDA_BWD_GRAD_INPUT_NCHW
+    ws = lib.msda_grid_sample_backward_workspace_size
+    rws = lib.msda_roi_align_backward_workspace_size
+    n = 2 * 5 * 6 * 8
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_F32, NCHW) == n * 4
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_BF16, NCHW) == n * 2
+    assert ws(2, 5, 6, 8, 3, 3, _lib.MSDA_DTYPE_BF16, NCHW | _lib.MSDA_BWD_FP32_ACCUM) == n * 4
+    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F16, NCHW | _lib.MSDA_BWD_DETERMINISTIC) == 256 + n * 8
+    assert rws(2, 5, 6, 8, _lib.MSDA_DTYPE_F32, NCHW) == n * 4
+    # The flag belongs to the gathers: the MSDA backward refuses it.
+    rc = lib.msda_backward(vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16),
+                           vp(16), 1 << 20, 1, 4, 1, 1, 8, 1, 1, _lib.MSDA_DTYPE_BF16, NCHW, vp(0))
+    assert rc == _lib.MSDA_ERR_UNSUPPORTED and b"GRAD_INPUT_NCHW" in lib.msda_last_error()
+    # Without its workspace the call fails on the host.
+    rc = lib.msda_roi_align_backward(vp(16), vp(16), vp(16), vp(0), 0, 1, 4, 4, 8, 3, 2, 2, 1.0, -1, 0,
+                                     _lib.MSDA_DTYPE_F32, NCHW, vp(0))
+    assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
+    # N beyond the transpose grid's z limit is refused before any launch.
+    big = 70000
+    rc = lib.msda_roi_align_backward(vp(16), vp(16), vp(16), vp(256), 1 << 40, big, 1, 1, 4, 0, 2, 2, 1.0,
+                                     -1, 0, _lib.MSDA_DTYPE_F32, NCHW, vp(0))
+    assert rc == _lib.MSDA_ERR_UNSUPPORTED and b"NCHW" in lib.msda_last_error()
+
+
 def test_gather_op_validation():
     from msda_triton_b200 import grid_sample, roi_align
     x = torch.zeros(1, 4, 5, 5)

@@ -338,6 +338,51 @@ def test_transpose_is_exact(N, R, C, dtype):
     assert torch.equal(_transpose(y, N, C, R), x)
 
 
+@pytest.mark.parametrize("kind", ["f32", "bf16_native", "bf16_fp32", "f16_fixed", "f32_fixed"])
+@pytest.mark.parametrize("name,kw", GS_CASES[:2], ids=[c[0] for c in GS_CASES[:2]])
+def test_nchw_gradient_flag_through_the_abi(name, kw, kind):
+    """MSDA_BWD_GRAD_INPUT_NCHW for every accumulator (data type, fp32,
+    fixed point): the NCHW input gradient equals the NHWC one transposed --
+    bitwise where the accumulation is order-independent (fixed point),
+    within the bar of its accumulation otherwise -- and grad_grid is
+    unchanged."""
+    import ctypes
+
+    from msda_triton_b200 import _lib
+    from msda_triton_b200.ops import _DTYPE_CODE
+    dtype = {"f32": torch.float32, "f32_fixed": torch.float32, "f16_fixed": torch.float16}.get(kind, torch.bfloat16)
+    flags = {"bf16_fp32": _lib.MSDA_BWD_FP32_ACCUM, "f16_fixed": _lib.MSDA_BWD_DETERMINISTIC,
+             "f32_fixed": _lib.MSDA_BWD_DETERMINISTIC}.get(kind, 0)
+    x, grid, gout = _gs_inputs(kw, dtype, seed=13)
+    N, C, H, W = x.shape
+    Ho, Wo = grid.shape[1:3]
+    xn = x.permute(0, 2, 3, 1).contiguous()
+    gn = gout.permute(0, 2, 3, 1).contiguous()
+    lib = _lib.load()
+    code = _DTYPE_CODE[dtype]
+    p = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
+
+    def run(f, gi_shape):
+        nbytes = lib.msda_grid_sample_backward_workspace_size(N, H, W, C, Ho, Wo, code, f)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV) if nbytes else None
+        gi = torch.full(gi_shape, float("nan"), dtype=dtype, device=DEV)
+        gg = torch.empty_like(grid)
+        rc = lib.msda_grid_sample_backward(p(xn), p(grid), p(gn), p(gi), p(gg), p(ws), nbytes, N, H, W, C, Ho, Wo,
+                                           0, 0, 0, code, f, ctypes.c_void_p(0))
+        assert rc == _lib.MSDA_OK, lib.msda_last_error()
+        return gi, gg
+
+    gi_hwc, gg_a = run(flags, (N, H, W, C))
+    gi_chw, gg_b = run(flags | _lib.MSDA_BWD_GRAD_INPUT_NCHW, (N, C, H, W))
+    torch.cuda.synchronize()
+    if "fixed" in kind:
+        assert _bitwise_equal(gi_chw, gi_hwc.permute(0, 3, 1, 2))
+    else:
+        tol = REF_BWD_TOL[dtype] if kind == "bf16_native" else STRICT_TOL[dtype]  # native: rounded per add
+        close(gi_chw, gi_hwc.permute(0, 3, 1, 2), tol, "grad_input (NCHW)")
+    assert torch.equal(gg_a, gg_b)
+
+
 @pytest.mark.parametrize("channels_last", [False, True], ids=["nchw", "channels_last"])
 def test_gather_ops_keep_the_input_layout(channels_last):
     """An NCHW input gets an NCHW-contiguous gradient (and a channels_last one
