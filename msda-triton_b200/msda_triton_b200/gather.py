@@ -65,19 +65,23 @@ class _ToNHWC(torch.autograd.Function):
         return _transpose(_nhwc_contiguous(g), N, H * W, C).view(N, C, H, W)
 
 
+def _backward_rounds(dtype: torch.dtype, flags: int) -> bool:
+    """Whether the gather backward ends with a rounding pass over its
+    accumulator (fixed point, or fp32 accumulation of 16-bit data)."""
+    return bool(flags & _lib.MSDA_BWD_DETERMINISTIC) or (
+        bool(flags & _lib.MSDA_BWD_FP32_ACCUM) and dtype != torch.float32)
+
+
 def _nhwc(x: torch.Tensor, flags: int) -> tuple[torch.Tensor, bool]:
     """(N, C, H, W) -> (contiguous (N, H, W, C), whether the backward writes
     the input gradient NCHW): a view of a channels_last tensor, else one
     transpose kernel. The NCHW gradient is asked for where the backward has
-    a rounding pass anyway (fixed point, or fp32 accumulation of 16-bit
-    data), which then transposes for free; elsewhere it would only move the
-    transpose into the library."""
+    a rounding pass anyway, which then transposes for free; elsewhere it
+    would only move the transpose into the library."""
     v = x.permute(0, 2, 3, 1)
     if v.is_contiguous():
         return v, False
-    rounds = bool(flags & _lib.MSDA_BWD_DETERMINISTIC) or (
-        bool(flags & _lib.MSDA_BWD_FP32_ACCUM) and x.dtype != torch.float32)
-    return _ToNHWC.apply(x), rounds
+    return _ToNHWC.apply(x), _backward_rounds(x.dtype, flags)
 
 
 def _grad_input(like: torch.Tensor, nhwc_shape, nchw: bool) -> torch.Tensor:

@@ -191,6 +191,19 @@ def test_gather_abi_checks_before_any_device_work():
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
 
 
+def test_gather_nchw_gradient_is_asked_for_where_the_backward_rounds():
+    """The host asks for MSDA_BWD_GRAD_INPUT_NCHW only where the backward
+    has a rounding pass to fold the transpose into."""
+    from msda_triton_b200.gather import _backward_rounds, _bwd_flags
+    for dtype in (torch.float16, torch.bfloat16):
+        assert _backward_rounds(dtype, _bwd_flags(dtype, None, False))       # fp32 accumulation by default
+        assert not _backward_rounds(dtype, _bwd_flags(dtype, False, False))  # native atomics: no pass
+        assert _backward_rounds(dtype, _bwd_flags(dtype, False, True))
+    assert not _backward_rounds(torch.float32, _bwd_flags(torch.float32, None, False))
+    assert not _backward_rounds(torch.float32, _bwd_flags(torch.float32, True, False))
+    assert _backward_rounds(torch.float32, _bwd_flags(torch.float32, None, True))
+
+
 def test_gather_nchw_gradient_flag():
     """MSDA_BWD_GRAD_INPUT_NCHW: the header value, the workspace it adds
     (the accumulator in the data type when no other flag asks for one), its
