@@ -191,6 +191,25 @@ def test_gather_abi_checks_before_any_device_work():
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
 
 
+def test_transpose_abi_checks_before_any_device_work():
+    """msda_transpose: dtype, sizes, pointers and alignment are checked on
+    the host, empty work is a no-op, and sizes no grid can cover are refused
+    (N past gridDim.z; both tile counts past gridDim.y) -- all without a
+    device (the pointers below are never dereferenced)."""
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    t = lambda N=1, R=64, C=64, dtype=0, src=256, dst=512: lib.msda_transpose(  # noqa: E731
+        vp(src), vp(dst), N, R, C, dtype, vp(0))
+    assert t(dtype=7) == _lib.MSDA_ERR_UNSUPPORTED
+    assert t(R=-1) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert t(N=0, src=0, dst=0) == _lib.MSDA_OK and t(C=0) == _lib.MSDA_OK
+    assert t(src=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert t(dst=514) == _lib.MSDA_ERR_INVALID_ARGUMENT  # fp32 needs 4-byte alignment
+    assert t(N=70000) == _lib.MSDA_ERR_UNSUPPORTED
+    assert t(R=64 * 65536, C=64 * 65536) == _lib.MSDA_ERR_UNSUPPORTED
+    assert b"too large" in lib.msda_last_error()
+
+
 def test_gather_nchw_gradient_is_asked_for_where_the_backward_rounds():
     """The host asks for MSDA_BWD_GRAD_INPUT_NCHW only where the backward
     has a rounding pass to fold the transpose into."""
