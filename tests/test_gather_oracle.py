@@ -68,3 +68,30 @@ def test_roi_align_restatement_matches_torchvision(sampling_ratio, aligned):
     # fp32 box arithmetic (the kernels') moves sample positions by ~1e-6 px.
     out32 = go.roi_align(x, boxes, (5, 4), 0.5, sampling_ratio, aligned)
     torch.testing.assert_close(out32, ref.detach(), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("sampling_ratio", [2, 5])
+def test_roi_align_restatement_on_reversed_and_tiny_boxes(sampling_ratio):
+    """Boxes with x2 < x1 and/or y2 < y1 (aligned=True keeps the negative bin
+    size), boxes under one pixel, and a box mostly outside the image: the
+    restatement agrees with torchvision in float64, forward and backward.
+    (torchvision's CPU kernel rejects an adaptive sampling grid on a reversed
+    box, so the ratio is fixed here.)"""
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(2, 3, 14, 17, generator=g, dtype=torch.float64)
+    boxes = torch.tensor([
+        [0, 20.0, 4.0, 6.0, 22.0],    # x reversed
+        [1, 3.0, 25.0, 30.0, 5.0],    # y reversed
+        [0, 28.0, 24.0, 2.0, 1.0],    # both reversed
+        [1, 9.3, 7.1, 9.9, 7.6],      # under one pixel
+        [0, -12.0, -8.0, 2.0, 3.2],   # mostly outside
+    ], dtype=torch.float64)
+    a = x.clone().requires_grad_(True)
+    b = x.clone().requires_grad_(True)
+    out = go.roi_align(a, boxes, (4, 3), 0.5, sampling_ratio, True, box_dtype=torch.float64)
+    ref = torchvision.ops.roi_align(b, boxes, (4, 3), 0.5, sampling_ratio, True)
+    torch.testing.assert_close(out, ref, rtol=1e-12, atol=1e-12)
+    gout = torch.randn(ref.shape, generator=g, dtype=torch.float64)
+    out.backward(gout)
+    ref.backward(gout)
+    torch.testing.assert_close(a.grad, b.grad, rtol=1e-12, atol=1e-12)
