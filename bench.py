@@ -219,12 +219,18 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
         # One graph per step (forward then backward), as a training step
         # captured whole would run; an event recorded inside the graph
         # (external: a real event-record node) splits forward from backward.
+        # Event nodes at the graph's first and last node also give the
+        # step's device time without the graph launch latency (in_graph).
         mid = torch.cuda.Event(enable_timing=True, external=True)
+        first = torch.cuda.Event(enable_timing=True, external=True)
+        last = torch.cuda.Event(enable_timing=True, external=True)
         gs = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gs):
+            first.record()
             msda_ops._forward(*args)
             mid.record()
             msda_ops._backward(*args, g, fp32_acc, algo_flags)
+            last.record()
 
         def one(e):
             # Flush: write 512 MiB (evicts everything of ours from L2), then
@@ -238,7 +244,7 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
             # The in-graph event is overwritten by the next replay: read the
             # split now (outside the timed region of the next step).
             e[2].synchronize()
-            e[1] = (e[0].elapsed_time(mid), mid.elapsed_time(e[2]))
+            e[1] = (e[0].elapsed_time(mid), mid.elapsed_time(e[2]), first.elapsed_time(last))
     else:
         gs = None
 
@@ -260,8 +266,42 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
 def split_ms(e):
     """(forward ms, backward ms) of one timed step."""
     if isinstance(e[1], tuple):
-        return e[1]
+        return e[1][:2]
     return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+
+
+def in_graph_ms(e):
+    """Device time from the step graph's first node to its last (None
+    without graphs)."""
+    return e[1][2] if isinstance(e[1], tuple) else None
+
+
+def workload_leg(name, dtype, steps, warmup):
+    """Forward + backward of another operating point on this GPU (default
+    accumulator policy), timed like the headline device leg: mean forward /
+    backward / step times and the step's algorithmic-byte roofline."""
+    preset = presets.get(name)
+    x = presets.make_inputs(preset, dtype=dtype, device="cuda")
+    fp32_acc = msda_ops._use_fp32_grad_accum(x["value"])
+    gs, one, evs = device_leg(x, steps, warmup, fp32_acc)
+    for e in evs:
+        one(e)
+    f = statistics.fmean(split_ms(e)[0] for e in evs)
+    b = statistics.fmean(split_ms(e)[1] for e in evs)
+    inner = statistics.fmean(in_graph_ms(e) for e in evs)
+    B, S, M, D = x["value"].shape
+    Q = x["sampling_locations"].shape[1]
+    fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, preset.L, preset.K, x["value"].element_size())
+    peak, _ = load_peaks()
+    del gs, x
+    return {"dtype": str(dtype).replace("torch.", ""), "B": B, "Q": Q, "S": S,
+            "fwd_us": f * 1e3, "bwd_us": b * 1e3, "fwd_bwd_us": (f + b) * 1e3,
+            "in_graph_us": inner * 1e3, "queries_per_s": B * Q / ((f + b) / 1e3),
+            "roofline": {"bound": "hbm", "unit": "GB/s", "peak": peak,
+                         "fwd_frac": fwd_b / (f / 1e3) / 1e9 / peak,
+                         "bwd_frac": bwd_b / (b / 1e3) / 1e9 / peak,
+                         "step_frac": (fwd_b + bwd_b) / ((f + b) / 1e3) / 1e9 / peak,
+                         "algorithmic_bytes": fwd_b + bwd_b}}
 
 
 def kernel_breakdown(one, steps=5):
@@ -289,8 +329,6 @@ def backward_algorithm(kernels):
         return f"deterministic {kind} (64-bit fixed-point rows)"
     if "msda_count_kernel" in kernels:
         return "counted (fp32 rows for multi-hit pixels)"
-    if "msda_bwd_value_owner_kernel" in kernels:
-        return "owner"
     if "msda_cast_kernel" in kernels:
         return "scatter into fp32 workspace + cast"
     return "scatter (native packed reductions)"
@@ -354,6 +392,112 @@ def e2e_leg(x, steps, warmup, fp32_acc, deterministic=False):
     run(warmup)
     torch.cuda.synchronize()
     return run, h2d, d2h
+
+
+# ---------------------------------------------------------------------------
+# GPU bar: the reference's own Triton kernels on the same GPU
+# ---------------------------------------------------------------------------
+REF_INSTALL = REPO / "baseline" / "_ref"
+
+
+def reference_package():
+    """The reference package (src/msda_triton) installed unmodified into
+    baseline/_ref by baseline/install_reference.sh: (module, None), or
+    (None, why it is unavailable)."""
+    if not (REF_INSTALL / "msda_triton" / "kernels.py").is_file():
+        return None, "baseline/_ref/msda_triton not installed (baseline/install_reference.sh)"
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    try:
+        import msda_triton  # noqa: PLC0415
+    except Exception as exc:  # noqa: BLE001
+        return None, f"import msda_triton failed: {exc}"
+    if getattr(msda_triton.ops, "triton", None) is None:
+        return None, "the reference's Triton path is unavailable (triton did not import)"
+    return msda_triton, None
+
+
+def public_op_leg(op, x, steps, warmup, **kwargs):
+    """Forward + autograd backward through a public operator
+    ``op(value, spatial_shapes, level_start_index, sampling_locations,
+    attention_weights, **kwargs)``, captured as one CUDA graph per step and
+    timed like the device leg (L2 flushed before every step, CUDA events).
+    Besides the events around the replay, event nodes inside the graph mark
+    its first and last node, so the step's device time is also reported
+    without the graph's launch latency. Returns mean (fwd ms, bwd ms,
+    in-graph fwd+bwd ms)."""
+    shapes, starts = x["spatial_shapes"], x["level_start_index"]
+    v = x["value"].detach().clone().requires_grad_(True)
+    l = x["sampling_locations"].detach().clone().requires_grad_(True)
+    a = x["attention_weights"].detach().clone().requires_grad_(True)
+    g = x["grad_output"]
+
+    def body():
+        out = op(v, shapes, starts, l, a, **kwargs)
+        return out, torch.autograd.grad(out, (v, l, a), g)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # autotune, JIT and allocator warm-up outside capture
+        for _ in range(3):
+            body()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    ev = {k: torch.cuda.Event(enable_timing=True, external=True) for k in ("first", "mid", "last")}
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ev["first"].record()
+        out = op(v, shapes, starts, l, a, **kwargs)
+        ev["mid"].record()
+        grads = torch.autograd.grad(out, (v, l, a), g)
+        ev["last"].record()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    drain = torch.ones(L2_DRAIN_BYTES // 4, dtype=torch.float32, device="cuda")
+    fwd, bwd, inner = [], [], []
+    for i in range(warmup + steps):
+        flush.fill_(1)
+        drain.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        if i >= warmup:
+            fwd.append(e0.elapsed_time(ev["mid"]))
+            bwd.append(ev["mid"].elapsed_time(e1))
+            inner.append(ev["first"].elapsed_time(ev["last"]))
+    del graph, out, grads
+    return statistics.fmean(fwd), statistics.fmean(bwd), statistics.fmean(inner)
+
+
+def gpu_bar(presets_dtypes, steps, warmup):
+    """The reference's Triton kernels (baseline/_ref, through its public
+    multi_scale_deformable_attention) and this build's public operator, timed
+    the same way on the same GPU, at both accumulator settings: the
+    reference's B200 default (native bf16 atomics, ops.py:21-33) and
+    fp32_grad_accum=True (fp32 scratch + downcast). Keyed by workload."""
+    ref, why = reference_package()
+    if ref is None:
+        return {"unavailable": why}
+    from msda_triton_b200 import multi_scale_deformable_attention as ours  # noqa: PLC0415
+
+    res = {"reference": "msda_triton (baseline/_ref, unmodified) Triton kernels, triton "
+                        + __import__("triton").__version__,
+           "method": "public op forward + torch.autograd.grad, one CUDA graph per step, L2 flushed, "
+                     "CUDA events; in_graph_us excludes the graph launch latency"}
+    for preset, dtype in presets_dtypes:
+        x = presets.make_inputs(preset, dtype=dtype, device="cuda")
+        row = {}
+        for acc_name, acc in (("native", False), ("fp32", True)):
+            for impl, op in (("triton", ref.multi_scale_deformable_attention), ("b200", ours)):
+                f, b, inner = public_op_leg(op, x, steps, warmup, fp32_grad_accum=acc)
+                row[f"{impl}_{acc_name}"] = {"fwd_us": f * 1e3, "bwd_us": b * 1e3,
+                                             "fwd_bwd_us": (f + b) * 1e3, "in_graph_us": inner * 1e3}
+            row[f"speedup_{acc_name}"] = (row[f"triton_{acc_name}"]["fwd_bwd_us"]
+                                          / row[f"b200_{acc_name}"]["fwd_bwd_us"])
+        res[preset.name] = row
+        del x
+    return res
 
 
 CPU_SAMPLE_MAX_BATCH = 4  # the CPU legs time at most 4 batch items per step
@@ -534,14 +678,6 @@ def run_gather_bench(args):
     return 0
 
 
-def load_traffic(config_name):
-    p = REPO / "profiles" / "traffic.json"
-    if not p.exists():
-        return None
-    d = json.loads(p.read_text())
-    return d.get(config_name)
-
-
 def run_reference_arm(args, preset, dtype):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -593,7 +729,7 @@ def main(argv=None) -> int:
                     help="msda (default): the headline benchmark; grid_sample / roi_align: the "
                          "sibling gathers on their own workloads, next to torch / torchvision (1 GPU)")
     ap.add_argument("--fp32-grad-accum", default="auto", choices=["auto", "on", "off"])
-    ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "owner", "counted"],
+    ap.add_argument("--bwd-algo", default="auto", choices=["auto", "scatter", "counted"],
                     help="force the grad_value algorithm of the device leg (default: automatic)")
     ap.add_argument("--deterministic", action="store_true",
                     help="bitwise-reproducible grad_value (64-bit fixed-point accumulation)")
@@ -603,6 +739,10 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-breakdown", action="store_true",
                     help="skip the CUPTI per-kernel pass (use under ncu)")
+    ap.add_argument("--no-gpu-bar", action="store_true",
+                    help="skip timing the reference's Triton kernels (baseline/_ref) on this GPU")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the encoder / m2f device legs of the default line")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -627,7 +767,6 @@ def main(argv=None) -> int:
 
     lib = msda_ops._lib
     algo_flags = {"auto": 0, "scatter": lib.MSDA_BWD_FORCE_SCATTER,
-                  "owner": lib.MSDA_BWD_FORCE_OWNER,
                   "counted": lib.MSDA_BWD_FORCE_COUNTED}[args.bwd_algo]
     if args.deterministic:
         algo_flags |= lib.MSDA_BWD_DETERMINISTIC
@@ -643,6 +782,9 @@ def main(argv=None) -> int:
     fwd_ms = [split_ms(e)[0] for e in evs]
     bwd_ms = [split_ms(e)[1] for e in evs]
     dev_total_ms = max_over_ranks(sum(f + b for f, b in zip(fwd_ms, bwd_ms)), world)
+    inner = [in_graph_ms(e) for e in evs]
+    in_graph_us = (max_over_ranks(statistics.fmean(inner), world) * 1e3
+                   if None not in inner else None)
     fwd_mean = max_over_ranks(statistics.fmean(fwd_ms), world)
     bwd_mean = max_over_ranks(statistics.fmean(bwd_ms), world)
 
@@ -682,14 +824,13 @@ def main(argv=None) -> int:
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (bwd_mean / 1e3) / 1e9
     step_achieved = (fwd_b + bwd_b) / ((fwd_mean + bwd_mean) / 1e3) / 1e9
-    traffic = load_traffic(f"{preset.name}-{str(dtype).replace('torch.', '')}")
     algo = backward_algorithm(kernels) if kernels else "automatic (not inspected)"
     roofline = {"kernel": "msda_backward call (" + " + ".join(
                     k for k in kernels if k != "msda_fwd_kernel") + "), CUDA-event time",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                 "frac_of_nominal_8TBs": achieved / NOMINAL_HBM_GBS,
-                "traffic": traffic, "algorithmic_bytes": bwd_b,
+                "traffic": None, "algorithmic_bytes": bwd_b,
                 "fwd": {"achieved": fwd_b / (fwd_mean / 1e3) / 1e9, "algorithmic_bytes": fwd_b,
                         "us": fwd_mean * 1e3, "frac": fwd_b / (fwd_mean / 1e3) / 1e9 / peak},
                 "step": {"achieved": step_achieved, "algorithmic_bytes": fwd_b + bwd_b,
@@ -706,6 +847,18 @@ def main(argv=None) -> int:
                                          f"{preset.name} workload, grid_sample oracle in "
                                          f"{str(dtype).replace('torch.', '')}"}
 
+    # ---- other operating points and the reference's Triton kernels (N=1) ----
+    workloads = None
+    bar = None
+    if world == 1 and not args.no_workloads and args.config == "decoder":
+        workloads = {"encoder": workload_leg("encoder", torch.bfloat16, min(args.steps, 20), 3),
+                     "m2f": workload_leg("m2f", torch.float16, min(args.steps, 20), 3)}
+    if world == 1 and not args.no_gpu_bar:
+        pd = [(preset, dtype)]
+        if args.config == "decoder" and dtype == torch.bfloat16:
+            pd.append((presets.get("encoder"), torch.bfloat16))
+        bar = gpu_bar(pd, min(args.steps, 20), 3)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
@@ -716,8 +869,13 @@ def main(argv=None) -> int:
             "fwd_us": fwd_mean * 1e3, "bwd_us": bwd_mean * 1e3,
             "fwd_bwd_us": (fwd_mean + bwd_mean) * 1e3,
             "fp32_grad_accum": fp32_acc, "deterministic": args.deterministic, "bwd_algo": algo,
+            "in_graph_us": in_graph_us,
             "kernels_us": {k: round(t, 2) for k, (t, _) in kernels.items()},
+            "kernels_us_note": "CUPTI spans; a kernel launched with programmatic dependent launch "
+                               "starts before its predecessor ends, so its span includes that wait "
+                               "and the spans can sum to more than the step",
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "workloads": workloads, "gpu_bar": bar,
             "gpu_launches": (None if launches_per_step is None
                              else int(round(launches_per_step * args.steps))),
             "clocks": clk.summary(),

@@ -75,13 +75,9 @@ typedef enum msda_status {
  *   writes zeros / rounds the fp32 rows. Same result as fp32 accumulation,
  *   with fp32 traffic only where rows are hit more than once (the automatic
  *   choice for fp32 accumulation when sampling is sparse, Q*L*K <= 2*S).
- * OWNER: pixel-chunk ownership -- each CTA accumulates chunks of grad_value
- *   rows in fp32 shared memory and writes each once; no workspace, no
- *   zero-fill, no global atomics. Falls back to SCATTER when a head slice has
- *   more sampling points (L*Q*K) than its shared-memory point list holds
- *   (65535) or its shared-memory plan does not fit. */
+ * Flag bit 4u is unused; msda_backward rejects flag bits it does not know
+ * with MSDA_ERR_INVALID_ARGUMENT. */
 #define MSDA_BWD_FORCE_SCATTER 2u
-#define MSDA_BWD_FORCE_OWNER 4u
 #define MSDA_BWD_FORCE_COUNTED 8u
 /* Deterministic grad_value (no counterpart in the reference, which documents
  * its backward as nondeterministic, README.md:179 and ops.py:135-138):
@@ -99,7 +95,7 @@ typedef enum msda_status {
  * atomics (Inf / NaN propagate as in fp32 accumulation; no determinism
  * claim then). Takes the hit-counted algorithm for sparse sampling
  * (Q*L*K <= 2*S), else the scatter; MSDA_BWD_FORCE_SCATTER / _COUNTED pick
- * one. MSDA_BWD_FP32_ACCUM is implied; MSDA_BWD_FORCE_OWNER is rejected.
+ * one. MSDA_BWD_FP32_ACCUM is implied.
  * Needs a workspace (msda_backward_workspace_size with this flag). */
 #define MSDA_BWD_DETERMINISTIC 16u
 /* Sibling gathers only (msda_grid_sample_backward, msda_roi_align_backward;
@@ -157,8 +153,7 @@ MSDA_API int msda_forward_fused(const void* value, const int64_t* spatial_shapes
  * sampling offsets (B,Q,M,L,K,2) and of the attention logits (B,Q,M,L,K)
  * (through the softmax), in `dtype`. The reference points' gradient is the
  * offsets' gradient times (W_l, H_l), summed over (m, l, k); the caller forms
- * it. Workspace and flags as msda_backward (same workspace size);
- * MSDA_BWD_FORCE_OWNER is not supported here.
+ * it. Workspace and flags as msda_backward (same workspace size).
  */
 MSDA_API int msda_backward_fused(const void* value, const int64_t* spatial_shapes,
                                  const int64_t* level_start_index, const void* reference_points,

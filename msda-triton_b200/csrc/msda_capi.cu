@@ -47,13 +47,6 @@ int kshift_of(int32_t K) {
   return s;
 }
 
-// Sampling points per value row (per head) below which the automatic choice
-// takes the pixel-chunk owner kernel. Disabled (0): on B200 the owner kernel's
-// shared-memory accumulation is slower than the scatter's L2 reductions at
-// every measured operating point; it stays available through
-// MSDA_BWD_FORCE_OWNER (deterministic grad_value).
-constexpr double kOwnerMaxPointsPerRow = 0.0;
-
 // Sampling points per value row (per head) up to which fp32 accumulation
 // uses the hit-counted scatter; denser sampling hits almost every row more
 // than once, and the plain fp32 scatter is cheaper.
@@ -63,9 +56,13 @@ constexpr double kCountedMaxPointsPerRow = 2.0;
 // warp's same-row contributions before reducing them.
 constexpr double kMergeMinPointsPerRow = 2.0;
 
-enum class Algo { kScatterNative, kScatterF32, kCounted, kOwner, kScatterFixed, kCountedFixed };
+// Every flag bit msda_backward / msda_backward_fused understand.
+constexpr uint32_t kKnownBwdFlags = MSDA_BWD_FP32_ACCUM | MSDA_BWD_FORCE_SCATTER | MSDA_BWD_FORCE_COUNTED |
+                                    MSDA_BWD_DETERMINISTIC;
 
-Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
+enum class Algo { kScatterNative, kScatterF32, kCounted, kScatterFixed, kCountedFixed };
+
+Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags) {
   const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
   const bool fp32_semantics = (flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32;
   const double density = (double)s.Q * s.L * s.K / (double)s.S;
@@ -76,11 +73,9 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags, bool owner_ok) {
   }
   const Algo scatter = fp32_ws ? Algo::kScatterF32 : Algo::kScatterNative;
   if (flags & MSDA_BWD_FORCE_SCATTER) return scatter;
-  if ((flags & MSDA_BWD_FORCE_OWNER) && owner_ok) return Algo::kOwner;
   if (flags & MSDA_BWD_FORCE_COUNTED) return Algo::kCounted;
   if (!fp32_semantics) return scatter;
   if (density <= kCountedMaxPointsPerRow) return Algo::kCounted;
-  if (owner_ok && density < kOwnerMaxPointsPerRow) return Algo::kOwner;
   return scatter;
 }
 
@@ -112,41 +107,6 @@ namespace msda {
 // Lets other translation units of the library (msda_noalloc.cu) report a
 // failure through msda_last_error(). Not exported.
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
-
-static size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
-
-bool plan_owner(int64_t B, int64_t S, int64_t Q, int M, int D, int L, int K, int es,
-                int num_sms, OwnerPlan* plan) {
-  // Point indices are 16-bit.
-  const int64_t max_points = (int64_t)L * Q * K;
-  if (max_points > 65535) return false;
-  OwnerArgs& a = plan->args;
-  // fp32 tile of ~32 KB per chunk; P a multiple of 4 keeps it float4-aligned.
-  int P = (8192 / D) & ~3;
-  if (P < 16) P = 16;
-  a.P = P;
-  const int64_t nchunks = (S + P - 1) / P;
-  if (nchunks > (1 << 30)) return false;
-  a.nchunks = (int)nchunks;
-  // One wave at two CTAs per SM; each CTA bins at most `seg` chunks at a time.
-  const int64_t slices = B * M;
-  int64_t per_slice = (2 * (int64_t)num_sms + slices - 1) / slices;
-  if (per_slice < 1) per_slice = 1;
-  if (per_slice > nchunks) per_slice = nchunks;
-  plan->ctas_per_slice = (int)per_slice;
-  a.seg = (int)((nchunks + per_slice - 1) / per_slice);
-  a.max_points = (int)max_points;
-  a.max_bins = a.seg * P + 2 * L + 1;
-  const size_t tile = (size_t)P * D * sizeof(float);
-  a.off_g = align16(tile);
-  a.off_pts = align16(a.off_g + (size_t)Q * D * es);
-  a.off_sorted = align16(a.off_pts + (size_t)3 * max_points * es);
-  a.off_bins = align16(a.off_sorted + (size_t)2 * max_points);
-  plan->smem = a.off_bins + (size_t)(a.max_bins + 1) * sizeof(unsigned);
-  plan->ovec = 1;
-  a.stage_vec = 0;
-  return plan->smem <= 220 * 1024;
-}
 
 }  // namespace msda
 
@@ -230,12 +190,6 @@ int msda_forward_fused(const void* value, const int64_t* spatial_shapes,
                       stream);
 }
 
-static bool owner_possible(const Shape& s, int es, msda::OwnerPlan* plan) {
-  // The owner grid is (CTAs per head slice, B*M); gridDim.y is limited to 65535.
-  if (s.B * s.M > 65535) return false;
-  return msda::plan_owner(s.B, s.S, s.Q, s.M, s.D, s.L, s.K, es, sm_count(), plan);
-}
-
 size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t num_queries,
                                     int32_t num_heads, int32_t head_dim, int32_t num_levels,
                                     int32_t num_points, int32_t dtype, uint32_t flags) {
@@ -244,8 +198,8 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
   if (es == 0 || batch <= 0 || num_queries <= 0 || num_values <= 0 || num_heads <= 0 ||
       head_dim <= 0 || num_levels <= 0 || num_points <= 0)
     return 0;
-  msda::OwnerPlan plan;
-  const Algo a = choose_algo(s, dtype, flags, owner_possible(s, es, &plan));
+  if (flags & ~kKnownBwdFlags) return 0;
+  const Algo a = choose_algo(s, dtype, flags);
   if (a == Algo::kCounted || a == Algo::kCountedFixed) {
     size_t coff, aoff;
     return counted_ws_bytes(s, dtype, a == Algo::kCountedFixed, &coff, &aoff);
@@ -257,7 +211,7 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
 }
 
 // The backward behind msda_backward and msda_backward_fused (fused: offsets
-// and logits in, their gradients out; the owner algorithm is not offered).
+// and logits in, their gradients out).
 static int backward_impl(const char* fn, const void* value, const int64_t* spatial_shapes,
                          const int64_t* level_start_index, const void* ref,
                          const void* sampling_locations, const void* attention_weights,
@@ -265,12 +219,10 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
                          void* grad_attention_weights, void* workspace, size_t workspace_bytes,
                          bool fused, const Shape& s, int32_t dtype, uint32_t flags, void* stream) {
   if (int rc = check_shape(s, dtype)) return rc;
-  if (fused && (flags & MSDA_BWD_FORCE_OWNER))
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: the owner algorithm does not take the fused prologue", fn);
-  if ((flags & MSDA_BWD_DETERMINISTIC) && (flags & MSDA_BWD_FORCE_OWNER))
-    return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_DETERMINISTIC and MSDA_BWD_FORCE_OWNER are exclusive", fn);
   if (flags & MSDA_BWD_GRAD_INPUT_NCHW)
     return fail(MSDA_ERR_UNSUPPORTED, "%s: MSDA_BWD_GRAD_INPUT_NCHW is a flag of the sibling gathers", fn);
+  if (flags & ~kKnownBwdFlags)
+    return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: unknown flag bits 0x%x", fn, (unsigned)(flags & ~kKnownBwdFlags));
   if (s.B == 0) return succeed();
   const int es = elem_size(dtype);
   const size_t gv_bytes = (size_t)s.B * s.S * s.M * s.D * es;
@@ -290,9 +242,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
       !aligned(spatial_shapes, 8) || !aligned(level_start_index, 8) || (fused && !aligned(ref, 2 * es)))
     return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: misaligned buffer (locations / offsets and reference points need %d-byte alignment)", fn, 2 * es);
 
-  msda::OwnerPlan plan;
-  const bool owner_ok = !fused && owner_possible(s, es, &plan);
-  const Algo algo = choose_algo(s, dtype, flags, owner_ok);
+  const Algo algo = choose_algo(s, dtype, flags);
   const bool fixed = algo == Algo::kScatterFixed || algo == Algo::kCountedFixed;
   const bool fp32_ws = algo == Algo::kScatterF32;
   const bool counted = algo == Algo::kCounted || algo == Algo::kCountedFixed;
@@ -310,7 +260,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
                                            : grad_value;
   msda::Cfg cfg;
   const bool vec_ok = aligned(value, 16) && aligned(grad_output, 16) &&
-                      (algo == Algo::kOwner || aligned(target, 16)) &&
+                      aligned(target, 16) &&
                       (!counted || aligned(grad_value, 16));
   if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
   if (fused && cfg.vec != 16 / es)
@@ -329,7 +279,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   // not a memset).
   bool bwd_pdl = counted;
   bool zero_kernel = false;
-  if (!counted && algo != Algo::kOwner) {
+  if (!counted) {
     // The deterministic scatter zeroes the header with the accumulator.
     void* zdst = algo == Algo::kScatterFixed ? workspace : target;
     const size_t zbytes = ws_target ? ws_need : gv_bytes;
@@ -364,7 +314,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.ref = ref;
   p.fused = fused ? 1 : 0;
   p.grad_out = grad_output;
-  p.grad_value = (algo == Algo::kOwner || counted) ? grad_value : target;
+  p.grad_value = counted ? grad_value : target;
   p.acc_words = fixed ? 2 : 1;
   p.fixed_hdr = fixed_hdr;
   p.fixed_log2n = ceil_log2(s.Q * s.K);
@@ -391,10 +341,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   // queries at every pixel) makes the points of one query share rows: merge
   // them before the reductions. Sparse sampling rarely does.
   const bool merge = (double)s.Q * s.L * s.K > kMergeMinPointsPerRow * (double)s.S;
-  const int mode = algo == Algo::kOwner ? msda::kNoScatter
-                   : counted            ? msda::kCounted
-                   : merge              ? msda::kScatterMerge
-                                        : msda::kScatter;
+  const int mode = counted ? msda::kCounted : merge ? msda::kScatterMerge : msda::kScatter;
   const int acc = fixed ? msda::kAccFixed : (fp32_ws || dtype == MSDA_DTYPE_F32) ? msda::kAccF32 : msda::kAccNative;
   switch (dtype) {
     case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, acc, bwd_pdl, st); break;
@@ -410,16 +357,6 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
       default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, fixed, sm_count(), st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward finalize launch");
-  }
-  if (algo == Algo::kOwner) {
-    plan.ovec = (aligned(grad_value, 16) && s.D % (16 / es) == 0) ? 16 / es : 1;
-    plan.args.stage_vec = (aligned(grad_output, 16) && (s.D * es) % 16 == 0) ? 1 : 0;
-    switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_owner<float>(p, plan, st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_owner<__half>(p, plan, st); break;
-      default: e = msda::launch_owner<__nv_bfloat16>(p, plan, st); break;
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "msda_backward grad_value launch");
   }
   if (algo == Algo::kScatterFixed) {
     const int64_t n = s.B * s.S * s.M * s.D;

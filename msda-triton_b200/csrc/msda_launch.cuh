@@ -80,19 +80,6 @@ template <typename T>
 cudaError_t launch_cast_fixed(const long long* src, T* dst, int64_t n, bool vec_ok,
                               const unsigned* hdr, int clog2n, int num_sms, cudaStream_t st);
 
-// grad_value by pixel-chunk ownership (see msda_bwd_value_owner_kernel).
-struct OwnerPlan {
-  OwnerArgs args;
-  int ctas_per_slice;  // grid.x
-  int ovec;            // output vector width (elements)
-  size_t smem;         // dynamic shared memory bytes
-};
-// Returns false when the owner kernel cannot take these sizes (its per-CTA
-// shared-memory arrays must hold all L*Q*K points of a head slice).
-bool plan_owner(int64_t B, int64_t S, int64_t Q, int M, int D, int L, int K, int es,
-                int num_sms, OwnerPlan* plan);
-template <typename T>
-cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st);
 template <typename T>
 cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st);
 // Zero `bytes` (a multiple of 16, 16-byte aligned) with L2 evict_last stores.
@@ -192,10 +179,8 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
     return mode == kScatterMerge ? bwd_by_shape<T, T, V16, kScatterMerge, true>(p, c, pdl, st)
                                  : bwd_by_shape<T, T, V16, kScatter, true>(p, c, pdl, st);
   }
-  if (mode == kNoScatter) {
-    if (c.vec == V16) return bwd_by_shape<T, T, V16, kNoScatter>(p, c, false, st);
-    if (c.vec == 1) return bwd_by_shape<T, T, 1, kNoScatter>(p, c, false, st);
-  } else if (mode == kCounted) {
+  if (mode == kNoScatter) return cudaErrorNotSupported;
+  if (mode == kCounted) {
     if (c.vec == V16) return bwd_by_shape<T, T, V16, kCounted>(p, c, pdl, st);
     if (c.vec == 1) return bwd_by_shape<T, T, 1, kCounted>(p, c, pdl, st);
   } else if (fp32_scatter || sizeof(T) == 4) {
@@ -276,29 +261,6 @@ cudaError_t launch_cast_fixed(const long long* src, T* dst, int64_t n, bool vec_
                    0, st, true, src, dst, n, hdr, clog2n);
 }
 
-template <typename T, int OVEC, int DT>
-static cudaError_t owner_launch(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
-  auto kern = msda_bwd_value_owner_kernel<T, OVEC, DT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)plan.smem);
-  if (e != cudaSuccess) return e;
-  const dim3 grid((unsigned)plan.ctas_per_slice, (unsigned)(p.B * p.M));
-  kern<<<grid, kOwnerThreads, plan.smem, st>>>(p, plan.args);
-  return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t launch_owner(const OpParams& p, const OwnerPlan& plan, cudaStream_t st) {
-  constexpr int V16 = 16 / (int)sizeof(T);
-  if (plan.ovec == V16) {
-    if (p.D == 32) return owner_launch<T, V16, 32>(p, plan, st);
-    if (p.D == 64) return owner_launch<T, V16, 64>(p, plan, st);
-    return owner_launch<T, V16, 0>(p, plan, st);
-  }
-  if (plan.ovec == 1) return owner_launch<T, 1, 0>(p, plan, st);
-  return cudaErrorInvalidConfiguration;
-}
-
 template <typename T>
 cudaError_t launch_cast(const float* src, T* dst, int64_t n, bool vec_ok, int num_sms, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
@@ -335,7 +297,6 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
   template cudaError_t launch_finalize<T>(const OpParams&, bool, bool, int, cudaStream_t);        \
   template cudaError_t launch_absmax<T>(const void*, int64_t, bool, const void*, int64_t, unsigned*, int, bool, cudaStream_t); \
   template cudaError_t launch_cast_fixed<T>(const long long*, T*, int64_t, bool, const unsigned*, int, int, cudaStream_t); \
-  template cudaError_t launch_owner<T>(const OpParams&, const OwnerPlan&, cudaStream_t);          \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);
 
 #endif  // MSDA_LAUNCH_IMPL

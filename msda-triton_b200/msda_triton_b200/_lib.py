@@ -24,7 +24,6 @@ MSDA_DTYPE_BF16 = 2
 
 MSDA_BWD_FP32_ACCUM = 1
 MSDA_BWD_FORCE_SCATTER = 2
-MSDA_BWD_FORCE_OWNER = 4
 MSDA_BWD_FORCE_COUNTED = 8
 MSDA_BWD_DETERMINISTIC = 16
 MSDA_BWD_GRAD_INPUT_NCHW = 32

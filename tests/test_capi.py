@@ -97,12 +97,10 @@ def test_abi_workspace_size():
     assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f) == counted
     assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_F32, 0) == 256
     assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_COUNTED) == counted
-    # Forcing the plain scatter keeps the full fp32 workspace; the owner path has none.
+    # Forcing the plain scatter keeps the full fp32 workspace.
     assert ws(2, 10, 2, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_SCATTER) == full
-    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 0
-    # More than 65535 sampling points per head slice (L*Q*K) exceed the owner
-    # kernel's shared-memory point list: it always scatters then.
-    assert ws(1, 10, 20000, 1, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | _lib.MSDA_BWD_FORCE_OWNER) == 10 * 8 * 4
+    # Unknown flag bits (4 was the removed owner algorithm's) size nothing.
+    assert ws(2, 10, 50, 3, 8, 1, 4, _lib.MSDA_DTYPE_BF16, f | 4) == 0
 
 
 def test_abi_workspace_size_deterministic():
@@ -132,9 +130,9 @@ def test_abi_deterministic_flag_checks():
     call = lambda flags, ws=0: lib.msda_backward(  # noqa: E731
         vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16), vp(16),
         vp(ws), 0, 1, 4, 1, 1, 8, 1, 1, _lib.MSDA_DTYPE_BF16, flags, vp(0))
-    # The owner algorithm is not a deterministic one: the combination is refused.
-    assert call(_lib.MSDA_BWD_DETERMINISTIC | _lib.MSDA_BWD_FORCE_OWNER) == _lib.MSDA_ERR_UNSUPPORTED
-    assert b"exclusive" in lib.msda_last_error()
+    # Flag bits the library does not know are refused.
+    assert call(_lib.MSDA_BWD_DETERMINISTIC | 4) == _lib.MSDA_ERR_INVALID_ARGUMENT
+    assert b"unknown flag" in lib.msda_last_error()
     # The fixed-point accumulator lives in the workspace.
     assert call(_lib.MSDA_BWD_DETERMINISTIC) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert b"deterministic" in lib.msda_last_error()

@@ -413,7 +413,6 @@ from msda_triton_b200 import _lib as _clib  # noqa: E402
 from msda_triton_b200 import ops as _ops  # noqa: E402
 
 ALGOS = {
-    "owner": (_clib.MSDA_BWD_FORCE_OWNER, True),
     "scatter_fp32": (_clib.MSDA_BWD_FORCE_SCATTER, True),
     "scatter_native": (_clib.MSDA_BWD_FORCE_SCATTER, False),
     "counted": (_clib.MSDA_BWD_FORCE_COUNTED, True),
@@ -447,7 +446,7 @@ def test_backward_algorithms(name, kw, lo, hi, dtype, algo):
     cases.assert_grads_close(got, ref, loc, shapes, STRICT_TOL[dtype], gv_tol=gv_tol, what=algo)
 
 
-@pytest.mark.parametrize("algo", ["owner", "scatter_fp32", "counted"])
+@pytest.mark.parametrize("algo", ["scatter_fp32", "counted"])
 @pytest.mark.parametrize("name", ["decoder", "small"])
 def test_backward_algorithms_at_baseline_points(name, algo):
     flags, fp32 = ALGOS[algo]
@@ -458,25 +457,6 @@ def test_backward_algorithms_at_baseline_points(name, algo):
     got = _ops._backward(v, s, st, l, a, g, fp32, flags)
     _, ref = oracle64(v, s, st, l, a, g)
     cases.assert_grads_close(got, ref, l, s, STRICT_TOL[v.dtype], what=f"{name}/{algo}")
-
-
-def test_owner_writes_every_grad_value_element():
-    """The owner path writes grad_value without a zero-fill: rows no sampling
-    point touches (padding rows past the last level included) must come back
-    as exact zeros even when the output buffer starts as garbage."""
-    value, shapes, starts, loc, attn = cases.make_inputs(
-        B=2, Q=3, M=2, D=32, shapes=[(9, 11), (4, 5)], K=2, dtype=torch.bfloat16, device=DEV)
-    pad = torch.randn(2, 17, 2, 32, device=DEV, dtype=torch.bfloat16)
-    value = torch.cat([value, pad], 1)  # S = 119 + 17 rows, the last 17 unused
-    g = cases.grad_output_like(torch.empty(2, 3, 2, 32, device=DEV, dtype=torch.bfloat16))
-    torch.cuda.empty_cache()
-    junk = torch.full((value.numel() * 4,), float("nan"), device=DEV)
-    del junk  # leave NaN garbage in the caching allocator's blocks
-    gv, _, _ = _ops._backward(value, shapes, starts, loc, attn, g, True, _clib.MSDA_BWD_FORCE_OWNER)
-    assert torch.isfinite(gv).all()
-    assert (gv[:, 119:] == 0).all()
-    _, ref = oracle64(value, shapes, starts, loc, attn, g)
-    close(gv, ref[0], STRICT_TOL[torch.bfloat16], "grad_value")
 
 
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
@@ -597,11 +577,6 @@ def test_fused_public_op_gradients_including_reference_points(dtype):
         assert (got_r - gr_r[q_keep]).abs().max() <= 2e-2 * gr_r.abs().max()
 
 
-def test_fused_rejects_the_owner_algorithm():
-    value, shapes, starts, ref, off, logits = _fused_inputs(FUSED_CASES[0][1], torch.bfloat16)
-    g = torch.zeros(2, 40, 4, 32, device=DEV, dtype=torch.bfloat16)
-    with pytest.raises(_clib.MSDALibraryError, match="owner"):
-        _ops._backward_fused(value, shapes, starts, ref, off, logits, g, True, _clib.MSDA_BWD_FORCE_OWNER)
 
 
 def test_fused_op_falls_back_off_the_vector_path():
