@@ -213,9 +213,13 @@ MSDA_API int msda_backward(const void* value, const int64_t* spatial_shapes, con
  *   fp16/bf16; larger sizes fail with MSDA_ERR_INVALID_ARGUMENT. fp32 inputs
  *   accumulate directly in grad_value and use no scratch.
  * - Every GPU that loads the library holds the 16 MiB array until exit.
- * - The first call on a device looks up the array's device address
- *   (cudaGetSymbolAddress, with that device current); make that first call
- *   before any stream capture. The stream must belong to the current device.
+ * - The array's device address belongs to a CUDA context: the first call in
+ *   each context (the device's primary context, or one the caller created
+ *   and made current) looks it up (cudaGetSymbolAddress, with that context
+ *   current) and keeps it per context handle; make that first call before
+ *   any stream capture, and again after cudaDeviceReset. The stream must
+ *   belong to the current device. Sizes are checked as msda_backward checks
+ *   them before the scratch limit is.
  * - All calls on a device share the one array (each call zeroes what it
  *   uses): calls that overlap on the GPU -- on different streams, or from
  *   different threads -- race and corrupt each other's gradients. Serialise
@@ -276,7 +280,11 @@ MSDA_API int msda_grid_sample_backward(const void* input, const void* grid, cons
 
 /* torchvision.ops.roi_align(input, rois, (pooled_height, pooled_width),
  * spatial_scale, sampling_ratio, aligned) on NHWC data. An ROI whose batch
- * index is outside [0, N) yields zeros. */
+ * index is outside [0, N) yields zeros. sampling_ratio > 1024 fails with
+ * MSDA_ERR_UNSUPPORTED; with sampling_ratio <= 0 (adaptive: ceil(bin size)
+ * samples per side, as torchvision) a bin walks at most 1024 samples per
+ * side, so boxes whose bins span more than 1024 pixels (or non-finite boxes)
+ * are sampled more coarsely than torchvision would. */
 MSDA_API int msda_roi_align_forward(const void* input, const float* rois, void* output, int64_t N,
                                     int64_t H, int64_t W, int64_t C, int64_t num_rois,
                                     int32_t pooled_height, int32_t pooled_width, float spatial_scale,

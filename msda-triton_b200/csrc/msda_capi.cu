@@ -40,6 +40,14 @@ int check_shape(const Shape& s, int32_t dtype) {
   return MSDA_OK;
 }
 
+// Whether the one-query-per-warp grid (ceil(Q / 8), M, B) is at most
+// kShortGridWaves waves of 4 CTAs per SM (a decoder's few hundred queries);
+// longer grids take the multi-query launch shapes.
+bool short_grid(const Shape& s) {
+  const int64_t ctas = (s.Q + msda::kWarpsPerCta - 1) / msda::kWarpsPerCta * s.M * s.B;
+  return ctas <= (int64_t)msda::kShortGridWaves * 4 * sm_count();
+}
+
 int kshift_of(int32_t K) {
   if ((K & (K - 1)) != 0) return -1;
   int s = 0;
@@ -108,6 +116,13 @@ namespace msda {
 // failure through msda_last_error(). Not exported.
 void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
+// The size checks of msda_backward, for entry points that size their own
+// buffers before calling it (msda_noalloc.cu). Not exported.
+int check_backward_shape(int64_t B, int64_t S, int64_t Q, int32_t M, int32_t D, int32_t L, int32_t K,
+                         int32_t dtype) {
+  return check_shape(Shape{B, S, Q, M, D, L, K}, dtype);
+}
+
 }  // namespace msda
 
 extern "C" {
@@ -139,10 +154,7 @@ static int forward_impl(const char* fn, const void* value, const int64_t* spatia
   if (int rc = choose_cfg(s.D, es, aligned(value, 16) && aligned(output, 16), &cfg)) return rc;
   if (fused && cfg.vec != 16 / es)
     return fail(MSDA_ERR_UNSUPPORTED, "%s: the fused prologue needs 16-byte aligned buffers and head_dim a multiple of %d", fn, 16 / es);
-  {
-    const int64_t ctas = (s.Q + msda::kWarpsPerCta - 1) / msda::kWarpsPerCta * s.M * s.B;
-    cfg.short_grid = ctas <= (int64_t)msda::kShortGridWaves * 4 * sm_count();
-  }
+  cfg.short_grid = short_grid(s);
 
   msda::OpParams p{};
   p.value = value;
@@ -265,6 +277,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   if (int rc = choose_cfg(s.D, es, vec_ok, &cfg)) return rc;
   if (fused && cfg.vec != 16 / es)
     return fail(MSDA_ERR_UNSUPPORTED, "%s: the fused prologue needs 16-byte aligned buffers and head_dim a multiple of %d", fn, 16 / es);
+  cfg.short_grid = short_grid(s);
 
   cudaError_t e;
   size_t counts_off = 0, acc_off = 0;

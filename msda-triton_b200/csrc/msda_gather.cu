@@ -398,8 +398,14 @@ int msda_grid_sample_backward(const void* input, const void* grid, const void* g
                   reinterpret_cast<cudaStream_t>(stream));
 }
 
-static int roi_checks(const char* fn, const Dims& d, int32_t ph, int32_t pw, int32_t dtype) {
+static int roi_checks(const char* fn, const Dims& d, int32_t ph, int32_t pw, int32_t sampling_ratio,
+                      int32_t dtype) {
   if (ph < 1 || pw < 1) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: output size must be >= 1", fn);
+  // The kernels walk at most kRoiMaxGrid samples per bin side; a larger
+  // explicit ratio would be clamped and differ from torchvision.
+  if (sampling_ratio > msda::kRoiMaxGrid)
+    return fail(MSDA_ERR_UNSUPPORTED, "%s: sampling_ratio=%d exceeds %d", fn, sampling_ratio,
+                msda::kRoiMaxGrid);
   return check_dims(fn, d, dtype);
 }
 
@@ -409,7 +415,7 @@ int msda_roi_align_forward(const void* input, const float* rois, void* output, i
                            int32_t aligned_, int32_t dtype, void* stream) {
   const char* fn = "msda_roi_align_forward";
   const Dims d{N, H, W, C, num_rois, (int64_t)pooled_height * pooled_width};
-  if (int rc = roi_checks(fn, d, pooled_height, pooled_width, dtype)) return rc;
+  if (int rc = roi_checks(fn, d, pooled_height, pooled_width, sampling_ratio, dtype)) return rc;
   if (num_rois == 0) return succeed();
   const int es = elem_size(dtype);
   if (!input || !rois || !output) return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
@@ -441,7 +447,7 @@ int msda_roi_align_backward(const float* rois, const void* grad_output, void* gr
                             uint32_t flags, void* stream) {
   const char* fn = "msda_roi_align_backward";
   const Dims d{N, H, W, C, num_rois, (int64_t)pooled_height * pooled_width};
-  if (int rc = roi_checks(fn, d, pooled_height, pooled_width, dtype)) return rc;
+  if (int rc = roi_checks(fn, d, pooled_height, pooled_width, sampling_ratio, dtype)) return rc;
   if (N == 0) return succeed();
   const int es = elem_size(dtype);
   if (!grad_input || (num_rois > 0 && (!rois || !grad_output)))

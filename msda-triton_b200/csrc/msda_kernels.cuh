@@ -71,18 +71,18 @@ __device__ __forceinline__ bool query_block_of(const OpParams& p, int warps, int
   return q < p.Q;
 }
 
-// Sums the G lane groups' partial rows of a warp and stores the output row
-// (shared by the forward kernels).
-template <typename T, int VEC, int LPR, int CPL>
-__device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&acc)[CPL][VEC]) {
-  constexpr int G = 32 / LPR;
-  const int grp = lane / LPR, sub = lane % LPR;
-  if constexpr (CPL == 1 && G > 1 && VEC >= 2) {
-    // Reduce-scatter across the G groups: each xor stage halves the values a
+// Sums the partial rows of the GQ lane groups that share a query (GQ = 32 /
+// LPR when the warp serves one query) and stores the output row when `live`.
+template <typename T, int VEC, int LPR, int CPL, int GQ = 32 / LPR>
+__device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&acc)[CPL][VEC],
+                                              bool live = true) {
+  const int gq = (lane / LPR) % GQ, sub = lane % LPR;
+  if constexpr (CPL == 1 && GQ > 1 && VEC >= 2) {
+    // Reduce-scatter across the GQ groups: each xor stage halves the values a
     // lane keeps (it keeps the half its partner sends it the other of), so
-    // log2(VEC) stages cost VEC-1 shuffles instead of VEC*log2(G); once a lane
-    // holds one value the remaining stages are plain xor-sums.
-    constexpr int STAGES = __builtin_ctz(G);
+    // log2(VEC) stages cost VEC-1 shuffles instead of VEC*log2(GQ); once a
+    // lane holds one value the remaining stages are plain xor-sums.
+    constexpr int STAGES = __builtin_ctz(GQ);
     int base = 0;
 #pragma unroll
     for (int st = 0; st < STAGES; ++st) {
@@ -105,9 +105,9 @@ __device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&ac
     constexpr int NF = (VEC >> STAGES) > 0 ? (VEC >> STAGES) : 1;  // values left per lane
     constexpr int HALVINGS = __builtin_ctz(VEC) < STAGES ? __builtin_ctz(VEC) : STAGES;
     // Lanes that only replicated a value in the plain xor stages skip the store.
-    const int rep_mask = ((G - 1) << __builtin_ctz(LPR)) & ~(((1 << HALVINGS) - 1) << __builtin_ctz(LPR));
+    const int rep_mask = ((GQ - 1) << __builtin_ctz(LPR)) & ~(((1 << HALVINGS) - 1) << __builtin_ctz(LPR));
     const int ch = sub * VEC + base;
-    if ((lane & rep_mask) == 0 && sub * VEC < D) {
+    if (live && (lane & rep_mask) == 0 && sub * VEC < D) {
       float outv[NF];
 #pragma unroll
       for (int i = 0; i < NF; ++i) outv[i] = acc[0][i];
@@ -115,12 +115,12 @@ __device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&ac
     }
   } else {
 #pragma unroll
-    for (int off = LPR; off < 32; off <<= 1)
+    for (int off = LPR; off < LPR * GQ; off <<= 1)
 #pragma unroll
       for (int j = 0; j < CPL; ++j)
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], off);
-    if (grp == 0) {
+    if (live && gq == 0) {
 #pragma unroll
       for (int j = 0; j < CPL; ++j) {
         const int ch = (j * LPR + sub) * VEC;
@@ -138,140 +138,143 @@ __device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&ac
 // the register budget to the compiler). A grid of a few waves runs faster
 // with fewer, register-richer warps per SM (MINB = 3); a long grid needs the
 // occupancy of the compiler's default.
-// FUSED: the layer's prologue runs here (OpParams::ref / fused).
-// HOIST: the first points' (x, y, a) are loaded before the level-table
-// sync and every step loads the next step's while its gathers are in flight
-// (one dependent load less per warp; pays for grids of a few waves).
+// QW: queries a warp serves at once -- its G = 32 / LPR lane groups split
+// into QW sets of GQ = G / QW groups, each set walking one query's L*K
+// points GQ*NB at a time (QW = 2 packs the 12 points of a 3-level, 4-point
+// head into 4 groups x 3 steps with no idle slot, where one query per warp
+// leaves 4 of 16 slots empty).
+// QPW: rounds per warp; a CTA covers WARPS*QW*QPW consecutive queries of one
+// (batch, head) slice, so neighbouring queries' shared corner rows are
+// re-read from L1 and the level table is loaded once per CTA.
+// FUSED: the layer's prologue runs here (OpParams::ref / fused; QW = 1).
 template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB, int MINB, bool FUSED = false,
-          bool HOIST = false>
+          int QW = 1, int QPW = 1>
 __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpParams p) {
-  __shared__ LevelInfo lv[kMaxLevels];
+  static_assert(!FUSED || QW == 1, "the fused prologue's softmax spans the warp");
   constexpr int G = 32 / LPR;
-  using Raw = typename Pack<T, VEC>::Raw;
-  const int lane = threadIdx.x & 31;
-  int64_t b, q;
-  int m;
-  const bool live = query_block_of(p, WARPS, b, m, q);
-  const int64_t qm = (b * p.Q + q) * p.M + m;
-  const int grp = lane / LPR, sub = lane % LPR;
-  const int LK = p.L * p.K;
-  const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
-  const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
-  float2 pxy[NB];
-  float pat[NB];
-#pragma unroll
-  for (int n = 0; n < NB; ++n) {
-    const int s = n * G + grp;
-    pxy[n] = make_float2(0.f, 0.f);
-    pat[n] = 0.f;
-    if (HOIST && live && s < LK) {
-      pxy[n] = load_pair(lp + 2 * s);
-      pat[n] = to_f32(ap[s]);
-    }
-  }
+  static_assert(QW >= 1 && G % QW == 0, "QW must divide the lane groups");
+  constexpr int GQ = G / QW;
+  __shared__ LevelInfo lv[kMaxLevels];
   load_levels(p.shapes, p.starts, p.L, p.S, lv);
-  if (!live) return;
+
+  using Raw = typename Pack<T, VEC>::Raw;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane / LPR, sub = lane % LPR;
+  const int qsub = grp / GQ, gq = grp % GQ;
+  const int m = (int)blockIdx.y;
+  const int64_t b = (int64_t)blockIdx.z;
   const int D = p.D;
   const int rs = p.M * D;  // row stride; pix * rs < S*M*D < 2^31 (checked on the host)
   const T* vb = reinterpret_cast<const T*>(p.value) + (b * p.S * p.M + m) * D;
-  // Fused prologue: this query's reference point and its head's softmax.
-  float2 refp = make_float2(0.f, 0.f);
-  float smx = 0.f, sinv = 1.f;
-  if constexpr (FUSED) {
-    refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
-    warp_softmax_stats(ap, LK, lane, smx, sinv);
+  const int LK = p.L * p.K;
+  // With several rounds and one step covering a query's points, a lane's NB
+  // point slots sit on the same levels for every query: keep those levels in
+  // registers (a single round reads them from shared memory, off the
+  // dependent chain of its first loads).
+  const bool one_step = QPW > 1 && LK <= GQ * NB;
+  LevelInfo lvn[QPW > 1 ? NB : 1];
+  if constexpr (QPW > 1) {
+#pragma unroll
+    for (int n = 0; n < NB; ++n) {
+      const int s = n * GQ + gq;
+      lvn[n] = lv[s < LK ? level_of(s, p.K, p.kshift) : 0];
+    }
   }
 
   // Packed-pair accumulators (f32x2 FMA) on the vector path, scalars otherwise.
   constexpr bool kPairs = VEC >= 2 && VEC % 2 == 0;
   constexpr int NP = kPairs ? VEC / 2 : 1;
-  uint64_t acc2[CPL][NP];
-  float acc[CPL][VEC];
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-#pragma unroll
-    for (int v = 0; v < NP; ++v) acc2[j][v] = 0ull;
-#pragma unroll
-    for (int v = 0; v < VEC; ++v) acc[j][v] = 0.f;
-  }
-
-  for (int s0 = 0; s0 < LK; s0 += G * NB) {
-    Bilinear bl[NB];
-    float at[NB];
-#pragma unroll
-    for (int n = 0; n < NB; ++n) {
-      const int s = s0 + n * G + grp;
-      if (s < LK) {
-        const float2 xy = HOIST ? pxy[n] : load_pair(lp + 2 * s);
-        const float a = HOIST ? pat[n] : to_f32(ap[s]);
-        const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
-        if constexpr (FUSED) {
-          at[n] = expf(a - smx) * sinv;
-          bl[n] = resolve_fused(refp, xy, L);
-        } else {
-          at[n] = a;
-          bl[n] = resolve(xy.x, xy.y, L);
-        }
-      } else {
-        at[n] = 0.f;
-        bl[n] = empty_slot();
-      }
+  for (int round = 0; round < QPW; ++round) {
+    const int64_t q = (((int64_t)blockIdx.x * QPW + round) * WARPS + warp) * QW + qsub;
+    const bool live = q < p.Q;
+    if (!__any_sync(kFullMask, live)) break;  // warp-uniform: past the last query
+    const int64_t qm = (b * p.Q + (live ? q : 0)) * p.M + m;
+    const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
+    const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
+    // Fused prologue: this query's reference point and its head's softmax.
+    float2 refp = make_float2(0.f, 0.f);
+    float smx = 0.f, sinv = 1.f;
+    if constexpr (FUSED) {
+      refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
+      warp_softmax_stats(ap, LK, lane, smx, sinv);
     }
-    Raw raw[NB][4][CPL];
+    uint64_t acc2[CPL][NP];
+    float acc[CPL][VEC];
 #pragma unroll
-    for (int n = 0; n < NB; ++n)
+    for (int j = 0; j < CPL; ++j) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int v = 0; v < NP; ++v) acc2[j][v] = 0ull;
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-          const int ch = (j * LPR + sub) * VEC;
-          Raw r{};
-          if (((bl[n].valid >> c) & 1u) && ch < D) r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
-          raw[n][c][j] = r;
-        }
-    if constexpr (HOIST) {  // the next step's (x, y, a), in flight with these gathers
+      for (int v = 0; v < VEC; ++v) acc[j][v] = 0.f;
+    }
+
+    for (int s0 = 0; s0 < LK; s0 += GQ * NB) {
+      Bilinear bl[NB];
+      float at[NB];
 #pragma unroll
       for (int n = 0; n < NB; ++n) {
-        const int sn = s0 + G * NB + n * G + grp;
-        if (sn < LK) {
-          pxy[n] = load_pair(lp + 2 * sn);
-          pat[n] = to_f32(ap[sn]);
-        }
-      }
-    }
-#pragma unroll
-    for (int n = 0; n < NB; ++n)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float wc = at[n] * bl[n].w[c];
-        if constexpr (kPairs) {
-          const uint64_t w2 = f2_pack(wc, wc);
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            uint64_t v2[NP];
-            raw_to_f2<T, VEC>(raw[n][c][j], v2);
-#pragma unroll
-            for (int e = 0; e < NP; ++e) acc2[j][e] = f2_fma(w2, v2[e], acc2[j][e]);
+        const int s = s0 + n * GQ + gq;
+        if (live && s < LK) {
+          const float2 xy = load_pair(lp + 2 * s);
+          const float a = to_f32(ap[s]);
+          const LevelInfo& L = one_step ? lvn[QPW > 1 ? n : 0] : lv[level_of(s, p.K, p.kshift)];
+          if constexpr (FUSED) {
+            at[n] = expf(a - smx) * sinv;
+            bl[n] = resolve_fused(refp, xy, L);
+          } else {
+            at[n] = a;
+            bl[n] = resolve(xy.x, xy.y, L);
           }
         } else {
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            float v[VEC];
-            unpack_raw<T, VEC>(raw[n][c][j], v);
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[j][e] = fmaf(wc, v[e], acc[j][e]);
-          }
+          at[n] = 0.f;
+          bl[n] = empty_slot();
         }
       }
-  }
-  if constexpr (kPairs) {
+      Raw raw[NB][4][CPL];
 #pragma unroll
-    for (int j = 0; j < CPL; ++j)
+      for (int n = 0; n < NB; ++n)
 #pragma unroll
-      for (int e = 0; e < NP; ++e) f2_unpack(acc2[j][e], acc[j][2 * e], acc[j][2 * e + 1]);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) {
+            const int ch = (j * LPR + sub) * VEC;
+            Raw r{};
+            if (((bl[n].valid >> c) & 1u) && ch < D) r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
+            raw[n][c][j] = r;
+          }
+#pragma unroll
+      for (int n = 0; n < NB; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float wc = at[n] * bl[n].w[c];
+          if constexpr (kPairs) {
+            const uint64_t w2 = f2_pack(wc, wc);
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+              uint64_t v2[NP];
+              raw_to_f2<T, VEC>(raw[n][c][j], v2);
+#pragma unroll
+              for (int e = 0; e < NP; ++e) acc2[j][e] = f2_fma(w2, v2[e], acc2[j][e]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+              float v[VEC];
+              unpack_raw<T, VEC>(raw[n][c][j], v);
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) acc[j][e] = fmaf(wc, v[e], acc[j][e]);
+            }
+          }
+        }
+    }
+    if constexpr (kPairs) {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j)
+#pragma unroll
+        for (int e = 0; e < NP; ++e) f2_unpack(acc2[j][e], acc[j][2 * e], acc[j][2 * e + 1]);
+    }
+    fwd_store_row<T, VEC, LPR, CPL, GQ>(reinterpret_cast<T*>(p.out) + qm * D, D, lane, acc, live);
   }
-
-  fwd_store_row<T, VEC, LPR, CPL>(reinterpret_cast<T*>(p.out) + qm * D, D, lane, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -307,9 +310,18 @@ constexpr int kFusedMaxLK = 128;
 #ifndef MSDA_BWD_COUNTED_MIN_BLOCKS
 #define MSDA_BWD_COUNTED_MIN_BLOCKS 3
 #endif
+// The caps above count CTAs of kBwdCapWarps warps; smaller CTAs scale the
+// count so the per-thread register budget stays the same.
+constexpr int kBwdCapWarps = 8;
 
-template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE, bool FUSED = false>
-__global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS)
+// QW / QPW as in the forward: a warp serves QW queries at once (GQ = G / QW
+// lane groups each) over QPW rounds of consecutive queries; the same-row
+// merge then matches (row, query) keys, since only one query's corners share
+// a grad_out vector. FUSED and the hit-counted mode take QW = QPW = 1.
+template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE, bool FUSED = false,
+          int QW = 1, int QPW = 1>
+__global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS) *
+                                                  kBwdCapWarps / WARPS)
     msda_bwd_kernel(const OpParams p) {
   constexpr bool SCATTER = MODE != kNoScatter;
   // A = long long: deterministic grad_value in 64-bit fixed point (see
@@ -321,13 +333,15 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   __shared__ float fused_ga[FUSED ? WARPS : 1][FUSED ? kFusedMaxLK : 1];  // fused: dL/da per point
 
   constexpr int G = 32 / LPR;
+  static_assert((QW == 1 || QW == 2) && G % QW == 0, "QW: 1 or 2 queries per warp");
+  static_assert(QW == 1 || (!FUSED && MODE != kCounted), "one query per warp for FUSED / kCounted");
+  constexpr int GQ = G / QW;
   using Raw = typename Pack<T, VEC>::Raw;
-  const int lane = threadIdx.x & 31;
-  int64_t b, q;
-  int m;
-  const bool live = query_block_of(p, WARPS, b, m, q);
-  const int64_t qm = (b * p.Q + q) * p.M + m;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = (int)blockIdx.y;
+  const int64_t b = (int64_t)blockIdx.z;
   const int grp = lane / LPR, sub = lane % LPR;
+  const int qsub = grp / GQ, gq_ = grp % GQ;
   const int D = p.D;
   const int rs = p.M * D;  // row stride; pix * rs < S*M*D < 2^31 (checked on the host)
   const int64_t head_base = (b * p.S * p.M + m) * D;
@@ -338,414 +352,422 @@ __global__ void __launch_bounds__(WARPS * 32, MODE == kCounted ? MSDA_BWD_COUNTE
   long long* faccb = reinterpret_cast<long long*>(p.acc) + head_base;  // kCounted, fixed point
   const unsigned* cnb = p.counts + (b * p.S * p.M + m);  // kCounted: row pix at cnb[pix * M]
   const int LK = p.L * p.K;
-  const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
-  const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
-  T* glp = reinterpret_cast<T*>(p.grad_loc) + qm * (2 * LK);
-  T* gap = reinterpret_cast<T*>(p.grad_attn) + qm * LK;
   // Scatter: keep the reduction target in L2, let the gathered value rows go first.
   uint64_t pol_keep = 0, pol_stream = 0;
   if constexpr (SCATTER) {
     pol_keep = policy_evict_last();
     pol_stream = policy_evict_first();
   }
-
-  // Dot products of 16-bit data by mixed-precision FMA on the raw words
-  // (fewer instructions; measured faster where the backward is throughput
-  // bound, slower in the latency-bound hit-counted mode, which keeps the
-  // packed f32x2 FMAs).
-  constexpr bool MIXED = sizeof(T) == 2 && VEC == 8 && MODE != kCounted;
-  float g[CPL][VEC];
-  Raw graw[MIXED ? CPL : 1];
-  {
-    const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const int ch = (j * LPR + sub) * VEC;
-      Raw r{};
-      if (live && ch < D) r = load_raw<T, VEC>(gp + ch);
-      unpack_raw<T, VEC>(r, g[j]);
-      if constexpr (MIXED) graw[j] = r;
-    }
-  }
-  // grad_out as packed fp32 pairs (VEC even).
-  uint64_t g2[CPL][VEC / 2 > 0 ? VEC / 2 : 1];
-#pragma unroll
-  for (int j = 0; j < CPL; ++j)
-#pragma unroll
-    for (int e = 0; e < VEC / 2; ++e) g2[j][e] = f2_pack(g[j][2 * e], g[j][2 * e + 1]);
-  // fp32 reductions of 16-bit data: a lane's 8 channels are 32 bytes of
-  // fp32, and two `red.v4` per lane would put the lanes of one instruction
-  // in different 32-byte sectors. Reduce channel quads interleaved instead:
-  // in reduction k (0, 1) lane `sub` adds channels (k*LPR + sub)*4 .. +3, so
-  // neighbouring lanes fill one sector per instruction. gq holds grad_out in
-  // that order.
-  constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 && !FIXED &&
-                         (MODE == kCounted || (MODE != kNoScatter && sizeof(A) == 4));
-  // Same-row merging (see the scatter below): one corner item per lane needs
-  // the 4 corners of a group to fit in its LPR lanes, one point per group.
-  // It pays where a query's points share rows (dense, local sampling such as
-  // an encoder's) and costs where they do not, so the host selects it.
-  constexpr bool COMBINE = MODE == kScatterMerge && LPR >= 4 && NB == 1;
-  // Fixed-point reductions are scalar 8-byte `red`s; in reduction k lane
-  // `sub` adds channel j*LPR*VEC + k*LPR + sub, so the LPR lanes of a group
-  // fill consecutive 8-byte words. gi holds grad_out in that order.
-  float gi[FIXED ? CPL : 1][FIXED ? VEC : 1];
-  if constexpr (FIXED) {
-    const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j)
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) {
-        const int ch = j * LPR * VEC + k * LPR + sub;
-        gi[j][k] = (live && ch < D) ? to_f32(gp[ch]) : 0.f;
-      }
-  }
-  float gq[QUADS ? CPL : 1][2][4];
-  if constexpr (QUADS) {
-    const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j)
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int ch = j * LPR * VEC + (k * LPR + sub) * 4;
-        if (live && ch < D) {
-          load_vec<T, 4>(gp + ch, gq[j][k]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) gq[j][k][e] = 0.f;
-        }
-      }
-  }
-
-  // The first NB points' (x, y, a) are in flight while the level table loads;
-  // every iteration then loads the next one's while its gathers are in flight.
-  float2 pxy[NB];
-  float pat[NB];
-#pragma unroll
-  for (int n = 0; n < NB; ++n) {
-    const int s = n * G + grp;
-    pxy[n] = make_float2(0.f, 0.f);
-    pat[n] = 0.f;
-    if (live && s < LK) {
-      pxy[n] = load_pair(lp + 2 * s);
-      pat[n] = to_f32(ap[s]);
-    }
-  }
-  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
-  if (!live) return;
-  // Fused prologue: this query's reference point and its head's softmax;
-  // sdot accumulates sum_s a_s * dL/da_s for the softmax backward.
-  float2 refp = make_float2(0.f, 0.f);
-  float smx = 0.f, sinv = 1.f, sdot = 0.f;
-  if constexpr (FUSED) {
-    refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
-    warp_softmax_stats(ap, LK, lane, smx, sinv);
-  }
   FixedScale fx{1.0, 1.f, 1.f, true};
 
-  for (int s0 = 0; s0 < LK; s0 += G * NB) {
-    Bilinear bl[NB];
-    float at[NB];
-    float fw[NB], fh[NB];
-    bool dense[NB];
-#pragma unroll
-    for (int n = 0; n < NB; ++n) {
-      const int s = s0 + n * G + grp;
-      if (s < LK) {
-        const float2 xy = pxy[n];  // loaded one iteration ahead
-        const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
-        if constexpr (FUSED) {
-          at[n] = expf(pat[n] - smx) * sinv;
-          bl[n] = resolve_fused(refp, xy, L);
-        } else {
-          at[n] = pat[n];
-          bl[n] = resolve(xy.x, xy.y, L);
-        }
-        fw[n] = L.fW;
-        fh[n] = L.fH;
-        dense[n] = L.dense;
-      } else {
-        at[n] = 0.f;
-        fw[n] = fh[n] = 0.f;
-        bl[n] = empty_slot();
-        dense[n] = false;
-      }
-    }
-    Raw raw[NB][4][CPL];
-    unsigned hits[NB][4];
-#pragma unroll
-    for (int n = 0; n < NB; ++n)
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-          const int ch = (j * LPR + sub) * VEC;
-          Raw r{};
-          if (((bl[n].valid >> c) & 1u) && ch < D) {
-            if constexpr (SCATTER && VEC * sizeof(T) == 16) {
-              const uint4 u = ldg16_hint(vb + bl[n].pix[c] * rs + ch, pol_stream);
-              r = *reinterpret_cast<const Raw*>(&u);
-            } else {
-              r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
-            }
-          }
-          raw[n][c][j] = r;
-        }
+  for (int round = 0; round < QPW; ++round) {
+    const int64_t q = (((int64_t)blockIdx.x * QPW + round) * WARPS + warp) * QW + qsub;
+    const bool live = q < p.Q;
+    const int64_t qm = (b * p.Q + (live ? q : 0)) * p.M + m;
+    const T* lp = reinterpret_cast<const T*>(p.loc) + qm * (2 * LK);
+    const T* ap = reinterpret_cast<const T*>(p.attn) + qm * LK;
+    T* glp = reinterpret_cast<T*>(p.grad_loc) + qm * (2 * LK);
+    T* gap = reinterpret_cast<T*>(p.grad_attn) + qm * LK;
 
-    // The next iteration's (x, y, a), in flight with this iteration's gathers.
+    // Dot products of 16-bit data by mixed-precision FMA on the raw words
+    // (fewer instructions; measured faster where the backward is throughput
+    // bound, slower in the latency-bound hit-counted mode, which keeps the
+    // packed f32x2 FMAs).
+    constexpr bool MIXED = sizeof(T) == 2 && VEC == 8 && MODE != kCounted;
+    float g[CPL][VEC];
+    Raw graw[MIXED ? CPL : 1];
+    {
+      const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
 #pragma unroll
-    for (int n = 0; n < NB; ++n) {
-      const int sn = s0 + G * NB + n * G + grp;
-      if (sn < LK) {
-        pxy[n] = load_pair(lp + 2 * sn);
-        pat[n] = to_f32(ap[sn]);
+      for (int j = 0; j < CPL; ++j) {
+        const int ch = (j * LPR + sub) * VEC;
+        Raw r{};
+        if (live && ch < D) r = load_raw<T, VEC>(gp + ch);
+        unpack_raw<T, VEC>(r, g[j]);
+        if constexpr (MIXED) graw[j] = r;
       }
     }
-    // The value gathers above need nothing from the kernel before this one
-    // (the zero-fill or the hit count); the counts and the reduction target do.
-    if constexpr (SCATTER) pdl_wait();
+    // grad_out as packed fp32 pairs (VEC even).
+    uint64_t g2[CPL][VEC / 2 > 0 ? VEC / 2 : 1];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j)
+#pragma unroll
+      for (int e = 0; e < VEC / 2; ++e) g2[j][e] = f2_pack(g[j][2 * e], g[j][2 * e + 1]);
+    // fp32 reductions of 16-bit data: a lane's 8 channels are 32 bytes of
+    // fp32, and two `red.v4` per lane would put the lanes of one instruction
+    // in different 32-byte sectors. Reduce channel quads interleaved instead:
+    // in reduction k (0, 1) lane `sub` adds channels (k*LPR + sub)*4 .. +3, so
+    // neighbouring lanes fill one sector per instruction. gq holds grad_out in
+    // that order.
+    constexpr bool QUADS = sizeof(T) == 2 && VEC == 8 && !FIXED &&
+                           (MODE == kCounted || (MODE != kNoScatter && sizeof(A) == 4));
+    // Same-row merging (see the scatter below): one corner item per lane needs
+    // the 4 corners of a group to fit in its LPR lanes, one point per group.
+    // It pays where a query's points share rows (dense, local sampling such as
+    // an encoder's) and costs where they do not, so the host selects it.
+    constexpr bool COMBINE = MODE == kScatterMerge && LPR >= 4 && NB == 1;
+    // Fixed-point reductions are scalar 8-byte `red`s; in reduction k lane
+    // `sub` adds channel j*LPR*VEC + k*LPR + sub, so the LPR lanes of a group
+    // fill consecutive 8-byte words. gi holds grad_out in that order.
+    float gi[FIXED ? CPL : 1][FIXED ? VEC : 1];
     if constexpr (FIXED) {
-      if (s0 == 0) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);  // written by the absmax pass
+      const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          const int ch = j * LPR * VEC + k * LPR + sub;
+          gi[j][k] = (live && ch < D) ? to_f32(gp[ch]) : 0.f;
+        }
     }
+    float gq[QUADS ? CPL : 1][2][4];
+    if constexpr (QUADS) {
+      const T* gp = reinterpret_cast<const T*>(p.grad_out) + qm * D;
 #pragma unroll
-    for (int n = 0; n < NB; ++n)
+      for (int j = 0; j < CPL; ++j)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        hits[n][c] = 0u;
-        // Dense-level rows are always reduced in fp32: no count to read.
-        if constexpr (MODE == kCounted && !COMBINE)
-          if ((bl[n].valid >> c) & 1u)
-            hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
-      }
+        for (int k = 0; k < 2; ++k) {
+          const int ch = j * LPR * VEC + (k * LPR + sub) * 4;
+          if (live && ch < D) {
+            load_vec<T, 4>(gp + ch, gq[j][k]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) gq[j][k][e] = 0.f;
+          }
+        }
+    }
+
+    // The first NB points' (x, y, a) are in flight while the level table loads;
+    // every iteration then loads the next one's while its gathers are in flight.
+    float2 pxy[NB];
+    float pat[NB];
 #pragma unroll
     for (int n = 0; n < NB; ++n) {
-      // Per-corner dot products over this lane's channels,
-      // P_c = sum_d g_d * v_c,d; the three gradients are linear in them:
-      //   ga = sum_c w_c P_c
-      //   gx = (1 - ly)(P01 - P00) + ly (P11 - P10)
-      //   gy = (1 - lx)(P10 - P00) + lx (P11 - P01)
-      float P[4];
-      if constexpr (MIXED) {
-        // Two fp32 accumulators per corner (low / high halves of each word).
-        float pl[4] = {0.f, 0.f, 0.f, 0.f}, ph[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-          const unsigned* gw = reinterpret_cast<const unsigned*>(&graw[j]);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const unsigned* vw = reinterpret_cast<const unsigned*>(&raw[n][c][j]);
-#pragma unroll
-            for (int e = 0; e < VEC / 2; ++e) {
-              pl[c] = fma_lo16(gw[e], vw[e], pl[c], (const T*)nullptr);
-              ph[c] = fma_hi16(gw[e], vw[e], ph[c], (const T*)nullptr);
-            }
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) P[c] = pl[c] + ph[c];
-      } else if constexpr (VEC % 2 == 0) {
-        uint64_t acc2[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
-#pragma unroll
-        for (int j = 0; j < CPL; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint64_t v2[VEC / 2];
-            raw_to_f2<T, VEC>(raw[n][c][j], v2);
-#pragma unroll
-            for (int e = 0; e < VEC / 2; ++e) acc2[c] = f2_fma(g2[j][e], v2[e], acc2[c]);
-          }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float lo, hi;
-          f2_unpack(acc2[c], lo, hi);
-          P[c] = lo + hi;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) P[c] = 0.f;
-#pragma unroll
-        for (int j = 0; j < CPL; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float v[VEC];
-            unpack_raw<T, VEC>(raw[n][c][j], v);
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) P[c] = fmaf(g[j][e], v[e], P[c]);
-          }
+      const int s = n * GQ + gq_;
+      pxy[n] = make_float2(0.f, 0.f);
+      pat[n] = 0.f;
+      if (live && s < LK) {
+        pxy[n] = load_pair(lp + 2 * s);
+        pat[n] = to_f32(ap[s]);
       }
-      const float lx = bl[n].lx, ly = bl[n].ly;
-      float ga = bl[n].w[0] * P[0];
-      ga = fmaf(bl[n].w[1], P[1], ga);
-      ga = fmaf(bl[n].w[2], P[2], ga);
-      ga = fmaf(bl[n].w[3], P[3], ga);
-      float gx = (1.f - ly) * (P[1] - P[0]);
-      gx = fmaf(ly, P[3] - P[2], gx);
-      float gy = (1.f - lx) * (P[2] - P[0]);
-      gy = fmaf(lx, P[3] - P[1], gy);
+    }
+    if (round == 0) load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);  // syncs the block
+    if (!__any_sync(kFullMask, live)) break;  // warp-uniform: past the last query
+    // Fused prologue: this query's reference point and its head's softmax;
+    // sdot accumulates sum_s a_s * dL/da_s for the softmax backward.
+    float2 refp = make_float2(0.f, 0.f);
+    float smx = 0.f, sinv = 1.f, sdot = 0.f;
+    if constexpr (FUSED) {
+      refp = load_pair(reinterpret_cast<const T*>(p.ref) + 2 * (b * p.Q + q));
+      warp_softmax_stats(ap, LK, lane, smx, sinv);
+    }
+
+    for (int s0 = 0; s0 < LK; s0 += GQ * NB) {
+      Bilinear bl[NB];
+      float at[NB];
+      float fw[NB], fh[NB];
+      bool dense[NB];
 #pragma unroll
-      for (int off = 1; off < LPR; off <<= 1) {
-        ga += __shfl_xor_sync(kFullMask, ga, off);
-        gx += __shfl_xor_sync(kFullMask, gx, off);
-        gy += __shfl_xor_sync(kFullMask, gy, off);
-      }
-      const int s = s0 + n * G + grp;
-      if (s < LK && sub == 0) {
-        if constexpr (FUSED) {
-          // d/d offset = d/d pixel coordinate; dL/da kept (fp32 in shared
-          // memory when it fits) for the softmax pass.
-          store_pair(glp + 2 * s, at[n] * gx, at[n] * gy);
-          sdot = fmaf(at[n], ga, sdot);
-          if (LK <= kFusedMaxLK)
-            fused_ga[threadIdx.x >> 5][s] = ga;
-          else
-            gap[s] = from_f32<T>(ga);
+      for (int n = 0; n < NB; ++n) {
+        const int s = s0 + n * GQ + gq_;
+        if (live && s < LK) {
+          const float2 xy = pxy[n];  // loaded one iteration ahead
+          const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
+          if constexpr (FUSED) {
+            at[n] = expf(pat[n] - smx) * sinv;
+            bl[n] = resolve_fused(refp, xy, L);
+          } else {
+            at[n] = pat[n];
+            bl[n] = resolve(xy.x, xy.y, L);
+          }
+          fw[n] = L.fW;
+          fh[n] = L.fH;
+          dense[n] = L.dense;
         } else {
-          store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
-          gap[s] = from_f32<T>(ga);
+          at[n] = 0.f;
+          fw[n] = fh[n] = 0.f;
+          bl[n] = empty_slot();
+          dense[n] = false;
         }
       }
-      if constexpr (SCATTER) {
-        // Writes this lane's channels of a * w * grad_out into row `pix`
-        // (weight wc; `hits` is the row's count in the counted mode).
-        auto scatter_row = [&](int pix, float wc, unsigned hits) {
+      Raw raw[NB][4][CPL];
+      unsigned hits[NB][4];
+#pragma unroll
+      for (int n = 0; n < NB; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int j = 0; j < CPL; ++j) {
             const int ch = (j * LPR + sub) * VEC;
-            if constexpr (FIXED) {
-              // Fixed-point reduction in interleaved channels (see gi). In
-              // the counted mode a one-hit row is stored and a two-hit row
-              // reduced in fp32 (below): fp32 addition is commutative, so
-              // 0 + a + b == 0 + b + a bitwise and two terms need no fixed
-              // point; three or more (and dense-level rows) do.
-              if (MODE != kCounted || hits > 2u) {
-                long long* row = (MODE == kCounted ? faccb : reinterpret_cast<long long*>(gvb)) + pix * rs;
-                if (fx.ok) {
-                  const double wd = (double)wc * fx.scale;  // exact
-#pragma unroll
-                  for (int k = 0; k < VEC; ++k) {
-                    const int ci = j * LPR * VEC + k * LPR + sub;
-                    if (ci < D) red_fixed(row + ci, wd, (double)gi[j][k], pol_keep);
-                  }
-                } else {  // fp32 fallback into the low words
-#pragma unroll
-                  for (int k = 0; k < VEC; ++k) {
-                    const int ci = j * LPR * VEC + k * LPR + sub;
-                    if (ci < D) atomicAdd(reinterpret_cast<float*>(row + ci), wc * gi[j][k]);
-                  }
-                }
-                continue;
-              }
-            }
-            if constexpr (QUADS) {
-              // fp32 reduction in interleaved quads (see gq); a counted
-              // one-hit row is stored in the natural layout.
-              if (MODE != kCounted || hits != 1u) {
-                float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + pix * rs;
-#pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                  const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
-                  if (cq < D)
-                    red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
-                                       wc * gq[j][k][3], pol_keep);
-                }
-                continue;
-              }
-            }
-            if (ch < D) {
-              float contrib[VEC];
-              if constexpr (VEC % 2 == 0) {
-                const uint64_t wc2 = f2_pack(wc, wc);
-#pragma unroll
-                for (int e = 0; e < VEC / 2; ++e)
-                  f2_unpack(f2_mul(wc2, g2[j][e]), contrib[2 * e], contrib[2 * e + 1]);
+            Raw r{};
+            if (((bl[n].valid >> c) & 1u) && ch < D) {
+              if constexpr (SCATTER && VEC * sizeof(T) == 16) {
+                const uint4 u = ldg16_hint(vb + bl[n].pix[c] * rs + ch, pol_stream);
+                r = *reinterpret_cast<const Raw*>(&u);
               } else {
+                r = load_raw<T, VEC>(vb + bl[n].pix[c] * rs + ch);
+              }
+            }
+            raw[n][c][j] = r;
+          }
+
+      // The next iteration's (x, y, a), in flight with this iteration's gathers.
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
-              }
-              if constexpr (MODE == kCounted) {
-                // A row with one hit gets its only contribution stored
-                // (rounded once, as fp32 accumulation would); rows with
-                // more hits accumulate in fp32.
-                if (hits == 1u)
-                  store_vec<T, VEC>(gvt + pix * rs + ch, contrib);
-                else if constexpr (!FIXED)
-                  red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
-                else  // two hits: fp32 in the first half of the 64-bit row
-                  red_add_vec_hint<float, VEC>(reinterpret_cast<float*>(faccb + pix * rs) + ch, contrib,
-                                               pol_keep);
-              } else if constexpr (!FIXED) {
-                red_add_vec_hint<A, VEC>(gvb + pix * rs + ch, contrib, pol_keep);
-              }
-            }
-          }
-        };
-        if constexpr (COMBINE) {
-          // Same-row merging. Every contribution of this query is a multiple
-          // of the same grad_out vector, so corners of the warp's points that
-          // land on one row need one write of (sum of their weights) *
-          // grad_out. Lane `sub` < 4 of a group holds corner `sub` of the
-          // group's point as an item (row, weight); lanes with equal rows
-          // find each other with a match, the lowest one leads and owns the
-          // summed weight (added in lane order: deterministic).
-          const int cs = sub & 3;
-          const unsigned vbit = (bl[n].valid >> cs) & 1u;
-          const bool have = s < LK && sub < 4 && vbit != 0u;
-          const int pix_s = cs == 0 ? bl[n].pix[0] : cs == 1 ? bl[n].pix[1] : cs == 2 ? bl[n].pix[2] : bl[n].pix[3];
-          const float w_s = cs == 0 ? bl[n].w[0] : cs == 1 ? bl[n].w[1] : cs == 2 ? bl[n].w[2] : bl[n].w[3];
-          const int key = have ? pix_s : -1 - lane;  // rows are >= 0; empty items never match
-          const float wt = have ? at[n] * w_s : 0.f;
-          const unsigned same = __match_any_sync(kFullMask, key);
-          float wsum = wt;
-          if (__any_sync(kFullMask, __popc(same) > 1)) {
-            wsum = 0.f;
-            unsigned rest = same;
-            const int rounds = __reduce_max_sync(kFullMask, (unsigned)__popc(same));
-            for (int r = 0; r < rounds; ++r) {
-              const int src = rest ? __ffs(rest) - 1 : lane;
-              const float v = __shfl_sync(kFullMask, wt, src);
-              if (rest) {
-                wsum += v;
-                rest &= rest - 1;
+      for (int n = 0; n < NB; ++n) {
+        const int sn = s0 + GQ * NB + n * GQ + gq_;
+        if (live && sn < LK) {
+          pxy[n] = load_pair(lp + 2 * sn);
+          pat[n] = to_f32(ap[sn]);
+        }
+      }
+      // The value gathers above need nothing from the kernel before this one
+      // (the zero-fill or the hit count); the counts and the reduction target do.
+      if constexpr (SCATTER) pdl_wait();
+      if constexpr (FIXED) {
+        if (round == 0 && s0 == 0) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);  // written by the absmax pass
+      }
+#pragma unroll
+      for (int n = 0; n < NB; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          hits[n][c] = 0u;
+          // Dense-level rows are always reduced in fp32: no count to read.
+          if constexpr (MODE == kCounted && !COMBINE)
+            if ((bl[n].valid >> c) & 1u)
+              hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
+        }
+#pragma unroll
+      for (int n = 0; n < NB; ++n) {
+        // Per-corner dot products over this lane's channels,
+        // P_c = sum_d g_d * v_c,d; the three gradients are linear in them:
+        //   ga = sum_c w_c P_c
+        //   gx = (1 - ly)(P01 - P00) + ly (P11 - P10)
+        //   gy = (1 - lx)(P10 - P00) + lx (P11 - P01)
+        float P[4];
+        if constexpr (MIXED) {
+          // Two fp32 accumulators per corner (low / high halves of each word).
+          float pl[4] = {0.f, 0.f, 0.f, 0.f}, ph[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < CPL; ++j) {
+            const unsigned* gw = reinterpret_cast<const unsigned*>(&graw[j]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const unsigned* vw = reinterpret_cast<const unsigned*>(&raw[n][c][j]);
+#pragma unroll
+              for (int e = 0; e < VEC / 2; ++e) {
+                pl[c] = fma_lo16(gw[e], vw[e], pl[c], (const T*)nullptr);
+                ph[c] = fma_hi16(gw[e], vw[e], ph[c], (const T*)nullptr);
               }
             }
           }
-          const int lead = have && __ffs(same) - 1 == lane;
-          unsigned hits_me = 0u;
-          if constexpr (MODE == kCounted)
-            if (lead) hits_me = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)key * p.M);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) P[c] = pl[c] + ph[c];
+        } else if constexpr (VEC % 2 == 0) {
+          uint64_t acc2[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
+#pragma unroll
+          for (int j = 0; j < CPL; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint64_t v2[VEC / 2];
+              raw_to_f2<T, VEC>(raw[n][c][j], v2);
+#pragma unroll
+              for (int e = 0; e < VEC / 2; ++e) acc2[c] = f2_fma(g2[j][e], v2[e], acc2[c]);
+            }
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const int src = grp * LPR + c;
-            const int lead_c = __shfl_sync(kFullMask, lead, src);
-            const int pix_c = __shfl_sync(kFullMask, key, src);
-            const float w_c = __shfl_sync(kFullMask, wsum, src);
-            unsigned hits_c = 0u;
-            if constexpr (MODE == kCounted) hits_c = __shfl_sync(kFullMask, hits_me, src);
-            if (lead_c) scatter_row(pix_c, w_c, hits_c);
+            float lo, hi;
+            f2_unpack(acc2[c], lo, hi);
+            P[c] = lo + hi;
           }
-        } else if (s < LK) {
+        } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            if ((bl[n].valid >> c) & 1u) scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c]);
+          for (int c = 0; c < 4; ++c) P[c] = 0.f;
+#pragma unroll
+          for (int j = 0; j < CPL; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float v[VEC];
+              unpack_raw<T, VEC>(raw[n][c][j], v);
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) P[c] = fmaf(g[j][e], v[e], P[c]);
+            }
+        }
+        const float lx = bl[n].lx, ly = bl[n].ly;
+        float ga = bl[n].w[0] * P[0];
+        ga = fmaf(bl[n].w[1], P[1], ga);
+        ga = fmaf(bl[n].w[2], P[2], ga);
+        ga = fmaf(bl[n].w[3], P[3], ga);
+        float gx = (1.f - ly) * (P[1] - P[0]);
+        gx = fmaf(ly, P[3] - P[2], gx);
+        float gy = (1.f - lx) * (P[2] - P[0]);
+        gy = fmaf(lx, P[3] - P[1], gy);
+#pragma unroll
+        for (int off = 1; off < LPR; off <<= 1) {
+          ga += __shfl_xor_sync(kFullMask, ga, off);
+          gx += __shfl_xor_sync(kFullMask, gx, off);
+          gy += __shfl_xor_sync(kFullMask, gy, off);
+        }
+        const int s = s0 + n * GQ + gq_;
+        if (live && s < LK && sub == 0) {
+          if constexpr (FUSED) {
+            // d/d offset = d/d pixel coordinate; dL/da kept (fp32 in shared
+            // memory when it fits) for the softmax pass.
+            store_pair(glp + 2 * s, at[n] * gx, at[n] * gy);
+            sdot = fmaf(at[n], ga, sdot);
+            if (LK <= kFusedMaxLK)
+              fused_ga[threadIdx.x >> 5][s] = ga;
+            else
+              gap[s] = from_f32<T>(ga);
+          } else {
+            store_pair(glp + 2 * s, at[n] * fw[n] * gx, at[n] * fh[n] * gy);
+            gap[s] = from_f32<T>(ga);
+          }
+        }
+        if constexpr (SCATTER) {
+          // Writes this lane's channels of a * w * grad_out into row `pix`
+          // (weight wc; `hits` is the row's count in the counted mode).
+          auto scatter_row = [&](int pix, float wc, unsigned hits) {
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+              const int ch = (j * LPR + sub) * VEC;
+              if constexpr (FIXED) {
+                // Fixed-point reduction in interleaved channels (see gi). In
+                // the counted mode a one-hit row is stored and a two-hit row
+                // reduced in fp32 (below): fp32 addition is commutative, so
+                // 0 + a + b == 0 + b + a bitwise and two terms need no fixed
+                // point; three or more (and dense-level rows) do.
+                if (MODE != kCounted || hits > 2u) {
+                  long long* row = (MODE == kCounted ? faccb : reinterpret_cast<long long*>(gvb)) + pix * rs;
+                  if (fx.ok) {
+                    const double wd = (double)wc * fx.scale;  // exact
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                      const int ci = j * LPR * VEC + k * LPR + sub;
+                      if (ci < D) red_fixed(row + ci, wd, (double)gi[j][k], pol_keep);
+                    }
+                  } else {  // fp32 fallback into the low words
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) {
+                      const int ci = j * LPR * VEC + k * LPR + sub;
+                      if (ci < D) atomicAdd(reinterpret_cast<float*>(row + ci), wc * gi[j][k]);
+                    }
+                  }
+                  continue;
+                }
+              }
+              if constexpr (QUADS) {
+                // fp32 reduction in interleaved quads (see gq); a counted
+                // one-hit row is stored in the natural layout.
+                if (MODE != kCounted || hits != 1u) {
+                  float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + pix * rs;
+#pragma unroll
+                  for (int k = 0; k < 2; ++k) {
+                    const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
+                    if (cq < D)
+                      red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
+                                         wc * gq[j][k][3], pol_keep);
+                  }
+                  continue;
+                }
+              }
+              if (ch < D) {
+                float contrib[VEC];
+                if constexpr (VEC % 2 == 0) {
+                  const uint64_t wc2 = f2_pack(wc, wc);
+#pragma unroll
+                  for (int e = 0; e < VEC / 2; ++e)
+                    f2_unpack(f2_mul(wc2, g2[j][e]), contrib[2 * e], contrib[2 * e + 1]);
+                } else {
+#pragma unroll
+                  for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
+                }
+                if constexpr (MODE == kCounted) {
+                  // A row with one hit gets its only contribution stored
+                  // (rounded once, as fp32 accumulation would); rows with
+                  // more hits accumulate in fp32.
+                  if (hits == 1u)
+                    store_vec<T, VEC>(gvt + pix * rs + ch, contrib);
+                  else if constexpr (!FIXED)
+                    red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
+                  else  // two hits: fp32 in the first half of the 64-bit row
+                    red_add_vec_hint<float, VEC>(reinterpret_cast<float*>(faccb + pix * rs) + ch, contrib,
+                                                 pol_keep);
+                } else if constexpr (!FIXED) {
+                  red_add_vec_hint<A, VEC>(gvb + pix * rs + ch, contrib, pol_keep);
+                }
+              }
+            }
+          };
+          if constexpr (COMBINE) {
+            // Same-row merging. Every contribution of this query is a multiple
+            // of the same grad_out vector, so corners of the warp's points that
+            // land on one row need one write of (sum of their weights) *
+            // grad_out. Lane `sub` < 4 of a group holds corner `sub` of the
+            // group's point as an item (row, weight); lanes with equal rows
+            // find each other with a match, the lowest one leads and owns the
+            // summed weight (added in lane order: deterministic).
+            const int cs = sub & 3;
+            const unsigned vbit = (bl[n].valid >> cs) & 1u;
+            const bool have = live && s < LK && sub < 4 && vbit != 0u;
+            const int pix_s = cs == 0 ? bl[n].pix[0] : cs == 1 ? bl[n].pix[1] : cs == 2 ? bl[n].pix[2] : bl[n].pix[3];
+            const float w_s = cs == 0 ? bl[n].w[0] : cs == 1 ? bl[n].w[1] : cs == 2 ? bl[n].w[2] : bl[n].w[3];
+            // rows are >= 0 (pix * QW + query stays below 2^31: S <= 2^30, QW <= 2);
+            // empty items never match
+            const int key = have ? pix_s * QW + qsub : -1 - lane;
+            const float wt = have ? at[n] * w_s : 0.f;
+            const unsigned same = __match_any_sync(kFullMask, key);
+            float wsum = wt;
+            if (__any_sync(kFullMask, __popc(same) > 1)) {
+              wsum = 0.f;
+              unsigned rest = same;
+              const int rounds = __reduce_max_sync(kFullMask, (unsigned)__popc(same));
+              for (int r = 0; r < rounds; ++r) {
+                const int src = rest ? __ffs(rest) - 1 : lane;
+                const float v = __shfl_sync(kFullMask, wt, src);
+                if (rest) {
+                  wsum += v;
+                  rest &= rest - 1;
+                }
+              }
+            }
+            const int lead = have && __ffs(same) - 1 == lane;
+            unsigned hits_me = 0u;
+            if constexpr (MODE == kCounted)
+              if (lead) hits_me = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)(key / QW) * p.M);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int src = grp * LPR + c;
+              const int lead_c = __shfl_sync(kFullMask, lead, src);
+              const int pix_c = __shfl_sync(kFullMask, key, src);
+              const float w_c = __shfl_sync(kFullMask, wsum, src);
+              unsigned hits_c = 0u;
+              if constexpr (MODE == kCounted) hits_c = __shfl_sync(kFullMask, hits_me, src);
+              if (lead_c) scatter_row(pix_c / QW, w_c, hits_c);
+            }
+          } else if (live && s < LK) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              if ((bl[n].valid >> c) & 1u) scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c]);
+          }
         }
       }
     }
-  }
-  if constexpr (FUSED) {
-    // Softmax backward over the query-head's L*K points:
-    //   dL/dlogit_s = a_s * (dL/da_s - sum_t a_t * dL/da_t),
-    // dL/da_s as written above by this warp's lanes.
+    if constexpr (FUSED) {
+      // Softmax backward over the query-head's L*K points:
+      //   dL/dlogit_s = a_s * (dL/da_s - sum_t a_t * dL/da_t),
+      // dL/da_s as written above by this warp's lanes.
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(kFullMask, sdot, off);
-    __syncwarp();
-    for (int s = lane; s < LK; s += 32) {
-      const float a = expf(to_f32(ap[s]) - smx) * sinv;
-      const float ga = LK <= kFusedMaxLK ? fused_ga[threadIdx.x >> 5][s] : to_f32(gap[s]);
-      gap[s] = from_f32<T>(a * (ga - sdot));
+      for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(kFullMask, sdot, off);
+      __syncwarp();
+      for (int s = lane; s < LK; s += 32) {
+        const float a = expf(to_f32(ap[s]) - smx) * sinv;
+        const float ga = LK <= kFusedMaxLK ? fused_ga[threadIdx.x >> 5][s] : to_f32(gap[s]);
+        gap[s] = from_f32<T>(a * (ga - sdot));
+      }
     }
-  }
+  }  // rounds
 }
 
 // ---------------------------------------------------------------------------

@@ -105,33 +105,71 @@ inline dim3 query_block_grid(const OpParams& p) {
   return dim3((unsigned)((p.Q + kWarpsPerCta - 1) / kWarpsPerCta), (unsigned)p.M, (unsigned)p.B);
 }
 
+// Forward launch shapes. Grids of at most kShortGridWaves waves (a decoder's
+// few hundred queries per head) keep one query per warp in 8-warp CTAs with
+// the register-rich budget (3 CTAs / SM) and NB points per group in flight.
+// Longer grids (an encoder's query at every pixel) take 4-warp CTAs whose
+// warps serve 2 queries at once over kLongRounds rounds of consecutive
+// queries, one point per lane group per step (measured on B200: encoder
+// forward 405 -> 332 us, Mask2Former 201 -> 139 us; the decoder is fastest
+// with the short shape).
+constexpr int kLongWarps = 4;
+constexpr int kLongRounds = 4;
+
+template <typename T, int VEC, int LPR, int CPL, int NB, bool FUSED>
+static cudaError_t fwd_launch(const OpParams& p, bool short_grid, cudaStream_t st) {
+  const dim3 grid_short = query_block_grid(p);
+  if (short_grid) {
+    if constexpr (VEC > 1)
+      msda_fwd_kernel<T, VEC, LPR, CPL, kWarpsPerCta, NB, 3, FUSED><<<grid_short, kWarpsPerCta * 32, 0, st>>>(p);
+    else
+      msda_fwd_kernel<T, VEC, LPR, CPL, kWarpsPerCta, NB, 0, FUSED><<<grid_short, kWarpsPerCta * 32, 0, st>>>(p);
+    return cudaGetLastError();
+  }
+  constexpr int QW = (FUSED || LPR == 32) ? 1 : 2;
+  constexpr int NBL = FUSED ? NB : 1;
+  constexpr int per_cta = kLongWarps * QW * kLongRounds;
+  const dim3 grid((unsigned)((p.Q + per_cta - 1) / per_cta), (unsigned)p.M, (unsigned)p.B);
+  msda_fwd_kernel<T, VEC, LPR, CPL, kLongWarps, NBL, 0, FUSED, QW, kLongRounds><<<grid, kLongWarps * 32, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, int VEC, bool FUSED = false>
 static cudaError_t fwd_by_shape(const OpParams& p, const Cfg& c, cudaStream_t st) {
-  const dim3 block(kWarpsPerCta * 32);
-  const dim3 grid = query_block_grid(p);
-#define MSDA_FWD_CASE(LPR_, CPL_, NB_)                                                          \
-  if (c.lpr == LPR_ && c.cpl == CPL_) {                                                         \
-    if (VEC > 1 && c.short_grid)                                                                \
-      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 3, FUSED><<<grid, block, 0, st>>>(p); \
-    else                                                                                        \
-      msda_fwd_kernel<T, VEC, LPR_, CPL_, kWarpsPerCta, NB_, 0, FUSED><<<grid, block, 0, st>>>(p); \
-    return cudaGetLastError();                                                                  \
-  }
+#define MSDA_FWD_CASE(LPR_, CPL_, NB_) \
+  if (c.lpr == LPR_ && c.cpl == CPL_) return fwd_launch<T, VEC, LPR_, CPL_, NB_, FUSED>(p, c.short_grid, st);
   MSDA_FOR_EACH_SHAPE(MSDA_FWD_CASE)
 #undef MSDA_FWD_CASE
   return cudaErrorInvalidConfiguration;
 }
 
+// Backward launch shapes. The hit-counted mode (sparse sampling), the fused
+// prologue and short grids keep one query per warp in 8-warp CTAs. Long
+// grids of the scatter modes on the 16-byte vector path take the forward's
+// long shape -- 4-warp CTAs, 2 queries per warp, kLongRounds rounds of
+// consecutive queries (measured on B200: encoder fp32-accumulation backward
+// 1005 -> 853 us, Mask2Former 465 -> 333 us).
+template <typename T, typename A, int VEC, int LPR, int CPL, int MODE, bool FUSED>
+static cudaError_t bwd_launch(const OpParams& p, bool short_grid, bool pdl, cudaStream_t st) {
+  constexpr bool kLongOk = !FUSED && MODE != kCounted && VEC * sizeof(T) == 16 && LPR <= 16;
+  if constexpr (kLongOk) {
+    if (!short_grid) {
+      constexpr int per_cta = kLongWarps * 2 * kLongRounds;
+      const dim3 grid((unsigned)((p.Q + per_cta - 1) / per_cta), (unsigned)p.M, (unsigned)p.B);
+      return launch_ex(msda_bwd_kernel<T, A, VEC, LPR, CPL, kLongWarps, 1, MODE, false, 2, kLongRounds>, grid,
+                       dim3(kLongWarps * 32), 0, st, pdl, p);
+    }
+  }
+  // One point per group in flight (NB = 1): the backward's per-point state
+  // (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
+  return launch_ex(msda_bwd_kernel<T, A, VEC, LPR, CPL, kWarpsPerCta, 1, MODE, FUSED>, query_block_grid(p),
+                   dim3(kWarpsPerCta * 32), 0, st, pdl, p);
+}
+
 template <typename T, typename A, int VEC, int MODE, bool FUSED = false>
 static cudaError_t bwd_by_shape(const OpParams& p, const Cfg& c, bool pdl, cudaStream_t st) {
-  const dim3 block(kWarpsPerCta * 32);
-  const dim3 grid = query_block_grid(p);
-// The backward keeps one point per group in flight (NB = 1): its per-point
-// state (gradients, weights, scatter operands) makes NB = 2 cost occupancy.
-#define MSDA_BWD_CASE(LPR_, CPL_, NB_)                                                                   \
-  if (c.lpr == LPR_ && c.cpl == CPL_)                                                                    \
-    return launch_ex(msda_bwd_kernel<T, A, VEC, LPR_, CPL_, kWarpsPerCta, 1, MODE, FUSED>, grid, block, 0, \
-                     st, pdl, p);
+#define MSDA_BWD_CASE(LPR_, CPL_, NB_) \
+  if (c.lpr == LPR_ && c.cpl == CPL_) return bwd_launch<T, A, VEC, LPR_, CPL_, MODE, FUSED>(p, c.short_grid, pdl, st);
   MSDA_FOR_EACH_SHAPE(MSDA_BWD_CASE)
 #undef MSDA_BWD_CASE
   return cudaErrorInvalidConfiguration;

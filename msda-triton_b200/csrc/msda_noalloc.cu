@@ -11,8 +11,15 @@
 // The array is a file-scope `__device__` variable: every GPU that loads the
 // library holds MSDA_NOALLOC_SCRATCH_BYTES of device memory for it until the
 // process exits. In host code its name is only a host-side stand-in, never a
-// device address; the address is looked up with cudaGetSymbolAddress once per
-// device, with that device current, by the first call made on that device.
+// device address. A module variable's address belongs to one CUDA context,
+// so the address is looked up with cudaGetSymbolAddress by the first call
+// made in each context (the device's primary context, or a context the
+// caller created and made current), with that context current, and kept per
+// context handle. A context destroyed and re-created (cudaDeviceReset) may
+// come back under the same handle: call msda_backward_noalloc again only
+// after the reset has finished, before any stream capture.
+#include <cuda.h>
+
 #include <cstdio>
 #include <mutex>
 
@@ -20,15 +27,38 @@
 
 namespace msda {
 void set_last_error(const char* msg);
+int check_backward_shape(int64_t B, int64_t S, int64_t Q, int32_t M, int32_t D, int32_t L, int32_t K,
+                         int32_t dtype);
 }
 
 namespace {
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MSDA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
+// (context, scratch address) pairs: one per CUDA context the entry point ran in.
+constexpr int kMaxContexts = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_dev[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxContexts] = {};
+void* g_scratch_ptr[kMaxContexts] = {};
+int g_scratch_n = 0;
+
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+// The current context's handle, through the driver entry point the runtime
+// hands out (the library links the runtime statically and not libcuda).
+cudaError_t current_context(CUcontext* ctx) {
+  static CtxGetCurrent fn = nullptr;
+  if (fn == nullptr) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || f == nullptr) return cudaErrorSymbolNotFound;
+    fn = reinterpret_cast<CtxGetCurrent>(f);
+  }
+  *ctx = nullptr;
+  return fn(ctx) == CUDA_SUCCESS ? cudaSuccess : cudaErrorDeviceUninitialized;
+}
 
 int report(int code, const char* msg) {
   msda::set_last_error(msg);
@@ -46,6 +76,11 @@ extern "C" int msda_backward_noalloc(const void* value, const int64_t* spatial_s
                                      int32_t head_dim, int32_t num_levels, int32_t num_points,
                                      int32_t dtype, void* stream) {
   const uint32_t flags = MSDA_BWD_FP32_ACCUM | MSDA_BWD_FORCE_SCATTER;
+  // msda_backward's own size checks first, so unsupported sizes fail as
+  // they would there instead of as a scratch overflow.
+  if (int rc = msda::check_backward_shape(batch, num_values, num_queries, num_heads, head_dim, num_levels,
+                                          num_points, dtype))
+    return rc;
   const size_t need = msda_backward_workspace_size(batch, num_values, num_queries, num_heads,
                                                    head_dim, num_levels, num_points, dtype, flags);
   char msg[256];
@@ -72,15 +107,26 @@ extern "C" int msda_backward_noalloc(const void* value, const int64_t* spatial_s
         return report(MSDA_ERR_INVALID_ARGUMENT, msg);
       }
     }
-    if (e == cudaSuccess && (dev < 0 || dev >= kMaxDevices)) e = cudaErrorInvalidDevice;
+    CUcontext ctx = nullptr;
+    if (e == cudaSuccess) e = current_context(&ctx);
     if (e == cudaSuccess) {
       std::lock_guard<std::mutex> lock(g_scratch_mu);
-      if (g_scratch_dev[dev] == nullptr) {
+      for (int i = 0; i < g_scratch_n && ctx != nullptr && scratch == nullptr; ++i)
+        if (g_scratch_ctx[i] == ctx) scratch = g_scratch_ptr[i];
+      if (scratch == nullptr) {
+        // First call in this context (with none current yet, the lookup
+        // binds the device's primary context, whose handle is read after it).
         void* ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e == cudaSuccess) g_scratch_dev[dev] = ptr;
+        if (e == cudaSuccess && ctx == nullptr) e = current_context(&ctx);
+        if (e == cudaSuccess) {
+          scratch = ptr;
+          if (ctx != nullptr && g_scratch_n < kMaxContexts) {
+            g_scratch_ctx[g_scratch_n] = ctx;
+            g_scratch_ptr[g_scratch_n++] = ptr;
+          }
+        }
       }
-      scratch = g_scratch_dev[dev];
     }
     if (e != cudaSuccess) {
       snprintf(msg, sizeof(msg), "msda_backward_noalloc: static scratch unavailable: %s (%s)",

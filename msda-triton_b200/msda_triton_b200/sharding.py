@@ -8,7 +8,8 @@ This module holds the host-side pieces of that path:
 * ``rank_batch``: the slice of the global batch a rank owns. Presets with
   ``scaling == "weak"`` give every rank ``preset.B`` items of its own (the
   global batch grows with the world); ``"strong"`` presets split
-  ``preset.B`` evenly (global B = 64 over 1..8 GPUs).
+  ``preset.B`` evenly (the scaling sweep: global B = 64 at encoder shapes over
+  1..8 GPUs).
 * ``init_ranks``: process-group setup from the torchrun environment.
 * ``max_over_ranks`` / ``barrier``: the only collectives, used for timing.
 

@@ -113,20 +113,22 @@ def msda_backward_analytic(value, spatial_shapes, level_start_index, sampling_lo
     arithmetic does (src/msda_triton/kernels.py:112-113, one fused
     multiply-add), and keeps everything after that in the working dtype.
     Returns (grad_value (B,S,M,D), grad_loc (B,Q,M,L,K,2), grad_attn
-    (B,Q,M,L,K))."""
+    (B,Q,M,L,K)) on the device of ``value`` (a test may run this checker on
+    the GPU in float64 when the CPU would take minutes)."""
     B, S, M, D = value.shape
     _, Q, _, L, K, _ = sampling_locations.shape
     dt = value.dtype
+    dev = value.device
     flat = value.reshape(-1)
-    loc = sampling_locations.to(dt)
-    att = attention_weights.to(dt)
-    g = grad_out.reshape(B, Q, M, D).to(dt)
-    grad_value = torch.zeros(B * S * M * D, dtype=dt)
-    grad_loc = torch.zeros(B, Q, M, L, K, 2, dtype=dt)
-    grad_attn = torch.zeros(B, Q, M, L, K, dtype=dt)
-    bi = torch.arange(B).view(B, 1, 1)
-    mi = torch.arange(M).view(1, 1, M)
-    di = torch.arange(D)
+    loc = sampling_locations.to(device=dev, dtype=dt)
+    att = attention_weights.to(device=dev, dtype=dt)
+    g = grad_out.reshape(B, Q, M, D).to(device=dev, dtype=dt)
+    grad_value = torch.zeros(B * S * M * D, dtype=dt, device=dev)
+    grad_loc = torch.zeros(B, Q, M, L, K, 2, dtype=dt, device=dev)
+    grad_attn = torch.zeros(B, Q, M, L, K, dtype=dt, device=dev)
+    bi = torch.arange(B, device=dev).view(B, 1, 1)
+    mi = torch.arange(M, device=dev).view(1, 1, M)
+    di = torch.arange(D, device=dev)
     for lvl in range(L):
         h = int(spatial_shapes[lvl, 0])
         w = int(spatial_shapes[lvl, 1])

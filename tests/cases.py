@@ -143,7 +143,24 @@ def kink_mask(loc: torch.Tensor, shapes: torch.Tensor, eps: float = 1e-3) -> tor
     return ((px - px.round()).abs() < eps).any(-1)
 
 
-def assert_grads_close(got, ref, loc, shapes, tol, gl_tol=None, gv_tol=None, what=""):
+def assert_native_grad_value_close(gv, ref, what=""):
+    """grad_value accumulated with native fp16/bf16 reductions. Each hit
+    rounds the running sum to 16 bits, in the order the atomics land, so an
+    element whose contributions cancel can sit far from the exact sum relative
+    to itself (the reason fp32 accumulation is the default). Held normwise
+    instead: ||gv - ref|| <= 3e-2 ||ref|| (bf16 measured 1.7e-2 at the
+    encoder point and up to 2.6e-2 on clustered sampling), and every element
+    within 8e-2 of max|ref| (the reference suite's bf16 tolerance, relative
+    to the tensor's scale)."""
+    d = (gv.double().cpu() - ref.double().cpu())
+    scale = ref.double().abs().max().item()
+    norm_err = d.norm().item() / max(ref.double().norm().item(), 1e-30)
+    assert norm_err <= 3e-2, f"{what} grad_value (native): normwise error {norm_err:.3g} > 3e-2"
+    worst = d.abs().max().item()
+    assert worst <= 8e-2 * scale, f"{what} grad_value (native): max error {worst:.3g} > 8e-2 * {scale:.3g}"
+
+
+def assert_grads_close(got, ref, loc, shapes, tol, gl_tol=None, gv_tol=None, what="", native_gv=False):
     """Compare (grad_value, grad_loc, grad_attn): grad_loc in pixel units. For
     fp32 locations, kink points are excluded from the grad_loc comparison (at
     most 1% of points may be); fp16/bf16 locations make x = loc*W - 0.5 exact
@@ -151,8 +168,11 @@ def assert_grads_close(got, ref, loc, shapes, tol, gl_tol=None, gv_tol=None, wha
     gv, gl, ga = got
     gv_r, gl_r, ga_r = ref
     kw = lambda t: dict(rtol=t["rtol"], atol=t["atol"])  # noqa: E731
-    torch.testing.assert_close(gv.double().cpu(), gv_r.double().cpu(), **kw(gv_tol or tol),
-                               msg=lambda m: f"{what} grad_value: {m}")
+    if native_gv:
+        assert_native_grad_value_close(gv, gv_r, what)
+    else:
+        torch.testing.assert_close(gv.double().cpu(), gv_r.double().cpu(), **kw(gv_tol or tol),
+                                   msg=lambda m: f"{what} grad_value: {m}")
     torch.testing.assert_close(ga.double().cpu(), ga_r.double().cpu(), **kw(tol),
                                msg=lambda m: f"{what} grad_attn: {m}")
     K = loc.shape[-2]

@@ -1,8 +1,8 @@
 """Generate the golden vectors under tests/golden/ from the REFERENCE's own code.
 
-Runs only where the reference checkout is present (its path in
-MSDA_REFERENCE; the default is the read-only checkout the committed vectors
-were made from). It imports, by file path:
+Runs only where the reference checkout is present; its path must be given
+in MSDA_REFERENCE (``MSDA_REFERENCE=<checkout> python tests/golden/make_golden.py``).
+It imports, by file path:
 
 * tests/reference_impls.py -- ``msda_reference`` (grid_sample) and
   ``msda_naive`` (loops), the reference's CPU implementations;
@@ -13,7 +13,7 @@ were made from). It imports, by file path:
 
 Inputs come from the reference suite's own generator
 (tests/test_msda.py:65-77, imported from the reference) and, for the
-BASELINE ``small`` operating point, from ``msda_triton_b200.presets``. Each
+``small`` operating point (B=1 Q=100 M=8 D=32 L=4 K=4, fp32), from ``msda_triton_b200.presets``. Each
 case is written as ``<case>.npz``: input sha256 digests (the tests regenerate
 the inputs and check the digests), the reference outputs, and the Triton
 interpreter outputs. Tensors above 65536 elements are stored as 8192 seeded
@@ -39,7 +39,9 @@ import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("MSDA_REFERENCE", "/root/reference"))
+if not os.environ.get("MSDA_REFERENCE"):
+    raise SystemExit("set MSDA_REFERENCE to the roulbac/msda-triton checkout the vectors are made from")
+REF = Path(os.environ["MSDA_REFERENCE"])
 FULL_LIMIT = 65536
 N_SAMPLES = 8192
 
@@ -196,7 +198,7 @@ def main() -> int:
                    dict(value=value, loc=loc, attn=attn, grad_out=g),
                    dict(out=out, grad_value=gv, grad_loc=gl, grad_attn=ga))
 
-    # 4. the BASELINE small operating point (fp32), inputs from msda_triton_b200.presets.
+    # 4. the ``small`` operating point (fp32), inputs from msda_triton_b200.presets.
     p = presets.get("small")
     x = presets.make_inputs(p, seed=0)
     value, shapes, starts = x["value"], x["spatial_shapes"], x["level_start_index"]

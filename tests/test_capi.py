@@ -13,6 +13,7 @@ import pytest
 import torch
 
 import cases
+from hostonly import host_only
 from msda_triton_b200 import MultiScaleDeformableAttnFunction, _lib, multi_scale_deformable_attention
 from msda_triton_b200.ops import _use_fp32_grad_accum
 
@@ -55,6 +56,7 @@ def _fwd(lib, **over):
                             args["dtype"], vp(0))
 
 
+@host_only
 def test_abi_rejects_bad_arguments_before_any_device_work():
     lib = _lib.load()
     assert _fwd(lib, dtype=7) == _lib.MSDA_ERR_UNSUPPORTED
@@ -122,6 +124,7 @@ def test_abi_workspace_size_deterministic():
             assert ws(50, dt, d | f | _lib.MSDA_BWD_FORCE_COUNTED) == counted
 
 
+@host_only
 def test_abi_deterministic_flag_checks():
     text = HEADER.read_text()
     assert re.search(r"#define MSDA_BWD_DETERMINISTIC (\d+)u", text).group(1) == str(_lib.MSDA_BWD_DETERMINISTIC)
@@ -151,6 +154,7 @@ def test_deterministic_option_follows_torch_flag():
         torch.use_deterministic_algorithms(before)
 
 
+@host_only
 def test_gather_abi_checks_before_any_device_work():
     """grid_sample / roi_align entry points: argument checks on the host,
     workspace sizes, and empty work as a no-op (no device touched)."""
@@ -183,12 +187,17 @@ def test_gather_abi_checks_before_any_device_work():
         vp(16), vp(16), vp(16), 1, 4, 4, 8, o.get("K", 3), o.get("ph", 2), 2, 1.0, -1, 0, 0, vp(0))
     assert ra(ph=0) == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert ra(K=0) == _lib.MSDA_OK
+    # An explicit sampling ratio beyond the kernels' 1024 samples per bin side
+    # would be clamped (torchvision honours it): refused instead.
+    rc = lib.msda_roi_align_forward(vp(16), vp(16), vp(16), 1, 4, 4, 8, 3, 2, 2, 1.0, 1025, 0, 0, vp(0))
+    assert rc == _lib.MSDA_ERR_UNSUPPORTED and b"sampling_ratio" in lib.msda_last_error()
     # The deterministic backward needs its fixed-point workspace.
     rc = lib.msda_roi_align_backward(vp(16), vp(16), vp(16), vp(0), 0, 1, 4, 4, 8, 3, 2, 2, 1.0, -1, 0,
                                      0, _lib.MSDA_BWD_DETERMINISTIC, vp(0))
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"workspace" in lib.msda_last_error()
 
 
+@host_only
 def test_transpose_abi_checks_before_any_device_work():
     """msda_transpose: dtype, sizes, pointers and alignment are checked on
     the host, empty work is a no-op, and sizes no grid can cover are refused
@@ -221,6 +230,7 @@ def test_gather_nchw_gradient_is_asked_for_where_the_backward_rounds():
     assert _backward_rounds(torch.float32, _bwd_flags(torch.float32, None, True))
 
 
+@host_only
 def test_gather_nchw_gradient_flag():
     """MSDA_BWD_GRAD_INPUT_NCHW: the header value, the workspace it adds
     (the accumulator in the data type when no other flag asks for one), its
@@ -273,6 +283,7 @@ def test_gather_op_validation():
         roi_align(x, torch.zeros(3, 5), 2)
 
 
+@host_only
 def test_abi_backward_needs_workspace_for_fp32_accumulation():
     lib = _lib.load()
     vp = ctypes.c_void_p

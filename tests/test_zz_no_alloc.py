@@ -98,9 +98,47 @@ def test_no_alloc_backward_rejects_sizes_beyond_the_static_scratch():
     B, S, Q, M, D, L, K = 2, 8193, 10, 8, 32, 1, 4
     need = lib.msda_backward_workspace_size(B, S, Q, M, D, L, K, _lib.MSDA_DTYPE_BF16, FLAGS)
     assert need > _lib.MSDA_NOALLOC_SCRATCH_BYTES
+    # Null buffers: the scratch limit is checked first; were that check ever
+    # to move behind the launch, msda_backward would still refuse the nulls
+    # on the host (and the message would not name the static scratch).
     vp = ctypes.c_void_p
-    rc = lib.msda_backward_noalloc(vp(256), vp(256), vp(256), vp(256), vp(256), vp(256), vp(256),
-                                   vp(256), vp(256), B, S, Q, M, D, L, K, _lib.MSDA_DTYPE_BF16,
+    rc = lib.msda_backward_noalloc(vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0),
+                                   B, S, Q, M, D, L, K, _lib.MSDA_DTYPE_BF16,
                                    vp(torch.cuda.current_stream().cuda_stream))
     assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT
     assert b"static scratch" in lib.msda_last_error()
+    # Sizes msda_backward does not support fail as they fail there, before
+    # the scratch limit is considered.
+    rc = lib.msda_backward_noalloc(vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0), vp(0),
+                                   1, 1 << 28, 1, 8, 1, 1, 1, _lib.MSDA_DTYPE_BF16,
+                                   vp(torch.cuda.current_stream().cuda_stream))
+    assert rc == _lib.MSDA_ERR_UNSUPPORTED and b"2^31" in lib.msda_last_error()
+
+
+def test_no_alloc_backward_on_a_side_stream():
+    """On a non-default stream of the current device: the same gradients as
+    msda_backward, twice in a row."""
+    lib = _lib.load()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for seed in (2, 3):
+            args = _inputs(torch.bfloat16, seed)
+            want = _regular(lib, *args)
+            outs = tuple(torch.full_like(t, float("nan")) for t in want)
+            got = _no_alloc(lib, *args, outs)
+            side.synchronize()
+            for a, b in zip(got, want):
+                torch.testing.assert_close(a.float(), b.float(), **TOL[torch.bfloat16])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_no_alloc_backward_refuses_a_stream_of_another_device():
+    lib = _lib.load()
+    args = _inputs(torch.bfloat16, 4)
+    outs = tuple(torch.empty_like(t) for t in (args[0], args[3], args[4]))
+    other = torch.cuda.Stream(device=1)
+    B, S, Q, M, D, L, K = _dims(args[0], args[3])
+    rc = lib.msda_backward_noalloc(*(_p(t) for t in args), *(_p(t) for t in outs), B, S, Q, M, D, L, K,
+                                   CODE[torch.bfloat16], ctypes.c_void_p(other.cuda_stream))
+    assert rc == _lib.MSDA_ERR_INVALID_ARGUMENT and b"belongs to device" in lib.msda_last_error()
