@@ -18,10 +18,15 @@ Reported (one JSON line on rank 0):
              in HBM; device time = CUDA-event time of one CUDA-graph replay
              per step (forward then backward launches), L2 flushed before
              every step, max over ranks.
+  in_graph_us  the step's device time between event nodes at the first and
+             last node of its CUDA graph (without the graph launch latency).
   e2e        the same metric through the public op with pinned HOST buffers:
              every step copies its inputs host->device and the output and the
              three gradients device->host inside the timed region (the next
-             step's uploads overlap this step's downloads on a copy stream).
+             step's uploads overlap this step's downloads on a copy stream);
+             `copy_only_ms_per_step` times the same copies with no operator,
+             `frac_of_copy_only` = copy-only time / e2e time. Each rank's
+             host threads (and pinned buffers) sit on its GPU's NUMA node.
   roofline   the backward call (the dominant launch sequence): algorithmic
              bytes / its CUDA-event time against the measured HBM copy
              bandwidth; `step` gives the same for forward + backward.
@@ -30,6 +35,12 @@ Reported (one JSON line on rank 0):
   cpu_baseline  the reference's CPU implementation (grid_sample forward +
              autograd backward, restated in oracle/msda_oracle.py) on the
              host cores, rank 0 at N=1.
+  workloads  (decoder line, N=1) the encoder (bf16) and Mask2Former (fp16)
+             operating points timed the same way, with their step rooflines.
+  gpu_bar    (N=1) the reference's own Triton kernels (baseline/_ref, the
+             unmodified package) and this build, both through their public op
+             and torch.autograd, one CUDA graph per step, at the reference's
+             B200 default accumulation (native) and with fp32_grad_accum.
 
 With --op grid_sample / roi_align the line covers the sibling gathers on
 their own workloads (GATHER_WORKLOADS), next to the operators they replace
@@ -189,6 +200,38 @@ def dist_setup(n_gpus: int):
     return ranks
 
 
+def bind_to_gpu_numa_node(device_index):
+    """Run this rank's host threads on the CPUs of its GPU's NUMA node (when
+    the host has more than one node), so pinned host buffers allocated
+    afterwards are local to the GPU's PCIe root. Returns {"node", "cpus"} or
+    None. Changes only this process's CPU affinity."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        bus = pynvml.nvmlDeviceGetPciInfo(h).busId
+        bus = bus.decode() if isinstance(bus, bytes) else bus
+        dom, rest = bus.lower().split(":", 1)
+        node_file = Path(f"/sys/bus/pci/devices/{int(dom, 16):04x}:{rest}/numa_node")
+        node = int(node_file.read_text())
+        nodes = [p for p in Path("/sys/devices/system/node").glob("node[0-9]*")]
+        if node < 0 or len(nodes) < 2:
+            return None
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return {"node": node, "cpus": len(cpus)}
+    except Exception:  # noqa: BLE001 - no NVML / sysfs: leave the affinity alone
+        return None
+
+
 max_over_ranks = sharding.max_over_ranks
 barrier = sharding.barrier
 
@@ -339,12 +382,14 @@ def e2e_leg(x, steps, warmup, fp32_acc, deterministic=False):
     host->device, runs forward + backward through
     multi_scale_deformable_attention, and copies the output and the three
     gradients device->host. The steps are pipelined the way a data loader
-    would run them: the inputs of step i+1 go up on a copy stream while the
-    compute stream runs step i and copies its results down (PCIe is full
-    duplex), with two device input buffers. The results are copied on the
-    compute stream itself, so no tensor outlives its stream. Returns
-    run(n) -> None, which runs n such steps, and the bytes copied per step
-    each way."""
+    would run them: the inputs of step i+1 go up on an upload stream and the
+    results of step i go down on a download stream while the compute stream
+    runs the next step (PCIe is full duplex), with two device input buffers;
+    each result tensor is recorded on the download stream, so the allocator
+    keeps it until its copy is done. Returns
+    run(n, compute=True) -> None, which runs n such steps (compute=False:
+    the same copies with no operator in between, the host link's own rate),
+    and the bytes copied per step each way."""
     keys = ("value", "sampling_locations", "attention_weights", "grad_output")
     host = {k: x[k].cpu().pin_memory() for k in keys}
     shapes, starts = x["spatial_shapes"], x["level_start_index"]
@@ -358,9 +403,13 @@ def e2e_leg(x, steps, warmup, fp32_acc, deterministic=False):
     d2h = sum(t.numel() * t.element_size() for t in (out_h, gv_h, gl_h, ga_h))
     compute = torch.cuda.current_stream()
     s_in = torch.cuda.Stream()
+    s_out = torch.cuda.Stream()
     bufs = [{k: torch.empty_like(x[k]) for k in keys} for _ in range(2)]
+    # Result-shaped device tensors for the copy-only leg.
+    idle = (torch.zeros(B, Q, M * D, dtype=x["value"].dtype, device="cuda"), torch.zeros_like(x["value"]),
+            torch.zeros_like(x["sampling_locations"]), torch.zeros_like(x["attention_weights"]))
 
-    def run(n):
+    def run(n, compute_op=True):
         up = [torch.cuda.Event() for _ in range(2)]    # inputs of a buffer are on the device
         used = [torch.cuda.Event() for _ in range(2)]  # a buffer's step has finished with it
         used[0].record(compute)
@@ -377,17 +426,25 @@ def e2e_leg(x, steps, warmup, fp32_acc, deterministic=False):
         for i in range(n):
             compute.wait_event(up[i % 2])
             b = bufs[i % 2]
-            v = b["value"].detach().requires_grad_(True)
-            l = b["sampling_locations"].detach().requires_grad_(True)
-            a = b["attention_weights"].detach().requires_grad_(True)
-            out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc,
-                                                   deterministic=deterministic)
-            out.backward(b["grad_output"])
+            if compute_op:
+                v = b["value"].detach().requires_grad_(True)
+                l = b["sampling_locations"].detach().requires_grad_(True)
+                a = b["attention_weights"].detach().requires_grad_(True)
+                out = multi_scale_deformable_attention(v, shapes, starts, l, a, fp32_grad_accum=fp32_acc,
+                                                       deterministic=deterministic)
+                out.backward(b["grad_output"])
+                results = (out.detach(), v.grad, l.grad, a.grad)
+            else:
+                results = idle
             used[i % 2].record(compute)
             if i + 1 < n:
                 upload(i + 1)  # into the other buffer, once step i-1 is done with it
-            for dst, src in zip((out_h, gv_h, gl_h, ga_h), (out.detach(), v.grad, l.grad, a.grad)):
-                dst.copy_(src, non_blocking=True)
+            s_out.wait_event(used[i % 2])
+            with torch.cuda.stream(s_out):
+                for dst, src in zip((out_h, gv_h, gl_h, ga_h), results):
+                    dst.copy_(src, non_blocking=True)
+                    src.record_stream(s_out)
+        compute.wait_stream(s_out)  # the last results are on the host when the caller's events fire
 
     run(warmup)
     torch.cuda.synchronize()
@@ -760,6 +817,7 @@ def main(argv=None) -> int:
 
     rank, world, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
+    host_numa = bind_to_gpu_numa_node(local)
     b0, nb = sharding.rank_batch(preset, world, rank)
     x = presets.make_inputs(preset, dtype=dtype, device="cuda", batch=nb, batch_offset=b0)
     fp32_acc = {"auto": msda_ops._use_fp32_grad_accum(x["value"]), "on": True,
@@ -805,9 +863,21 @@ def main(argv=None) -> int:
         t1.record()
         barrier(world)
         e2e_ms = max_over_ranks(t0.elapsed_time(t1), world)
+        # The same copies with no operator between them: the host link's rate.
+        run_e2e(args.warmup, compute_op=False)
+        barrier(world)
+        t0.record()
+        run_e2e(args.steps, compute_op=False)
+        t1.record()
+        barrier(world)
+        copy_ms = max_over_ranks(t0.elapsed_time(t1), world)
         e2e = {"value": queries_per_step * args.steps / (e2e_ms / 1e3), "unit": "queries/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": e2e_ms / args.steps}
+               "ms_per_step": e2e_ms / args.steps,
+               "copy_only_ms_per_step": copy_ms / args.steps,
+               "frac_of_copy_only": copy_ms / e2e_ms,
+               "host_link_gbs_per_rank": (h2d + d2h) / (copy_ms / args.steps / 1e3) / 1e9,
+               "host_numa": host_numa}
 
     # ---- per-kernel breakdown (CUPTI, untimed extra steps) -------------------
     if args.no_kernel_breakdown:
