@@ -243,7 +243,11 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
     """Forward and backward launches (one CUDA-graph replay per step, or
     direct launches with use_graph=False), L2 flushed before every step, each
     step bracketed by CUDA events. Returns (graph, step function, per-step
-    events)."""
+    events, in_graph) where in_graph(n) -> mean ms between the first and the
+    last node of a second graph of the same step (None without graphs),
+    measured after the timed region: event nodes cost time inside a graph,
+    so the timed graph carries only the one that splits forward from
+    backward."""
     args = (x["value"], x["spatial_shapes"], x["level_start_index"], x["sampling_locations"],
             x["attention_weights"])
     g = x["grad_output"].reshape(x["value"].shape[0], -1, x["value"].shape[2], x["value"].shape[3])
@@ -258,42 +262,57 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+
+    def flush_l2():
+        # Write 512 MiB (evicts everything of ours from L2), then read 256 MiB
+        # so the flush's own dirty lines are written back before the timed
+        # region instead of inside it.
+        flush.fill_(1)
+        drain.sum()
+
+    in_graph = None
     if use_graph:
         # One graph per step (forward then backward), as a training step
         # captured whole would run; an event recorded inside the graph
         # (external: a real event-record node) splits forward from backward.
-        # Event nodes at the graph's first and last node also give the
-        # step's device time without the graph launch latency (in_graph).
         mid = torch.cuda.Event(enable_timing=True, external=True)
-        first = torch.cuda.Event(enable_timing=True, external=True)
-        last = torch.cuda.Event(enable_timing=True, external=True)
         gs = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gs):
-            first.record()
             msda_ops._forward(*args)
             mid.record()
+            msda_ops._backward(*args, g, fp32_acc, algo_flags)
+        first = torch.cuda.Event(enable_timing=True, external=True)
+        last = torch.cuda.Event(enable_timing=True, external=True)
+        gi = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gi):
+            first.record()
+            msda_ops._forward(*args)
             msda_ops._backward(*args, g, fp32_acc, algo_flags)
             last.record()
 
         def one(e):
-            # Flush: write 512 MiB (evicts everything of ours from L2), then
-            # read 256 MiB so the flush's own dirty lines are written back
-            # before the timed region instead of inside it.
-            flush.fill_(1)
-            drain.sum()
+            flush_l2()
             e[0].record()
             gs.replay()
             e[2].record()
             # The in-graph event is overwritten by the next replay: read the
             # split now (outside the timed region of the next step).
             e[2].synchronize()
-            e[1] = (e[0].elapsed_time(mid), mid.elapsed_time(e[2]), first.elapsed_time(last))
+            e[1] = (e[0].elapsed_time(mid), mid.elapsed_time(e[2]))
+
+        def in_graph(n):
+            out = []
+            for _ in range(n):
+                flush_l2()
+                gi.replay()
+                last.synchronize()
+                out.append(first.elapsed_time(last))
+            return statistics.fmean(out)
     else:
         gs = None
 
         def one(e):
-            flush.fill_(1)
-            drain.sum()
+            flush_l2()
             e[0].record()
             msda_ops._forward(*args)
             e[1].record()
@@ -303,7 +322,7 @@ def device_leg(x, steps, warmup, fp32_acc, algo_flags=0, use_graph=True):
     tmp = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for _ in range(warmup):
         one(tmp)
-    return gs, one, evs
+    return gs, one, evs, in_graph
 
 
 def split_ms(e):
@@ -313,12 +332,6 @@ def split_ms(e):
     return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
 
 
-def in_graph_ms(e):
-    """Device time from the step graph's first node to its last (None
-    without graphs)."""
-    return e[1][2] if isinstance(e[1], tuple) else None
-
-
 def workload_leg(name, dtype, steps, warmup):
     """Forward + backward of another operating point on this GPU (default
     accumulator policy), timed like the headline device leg: mean forward /
@@ -326,12 +339,12 @@ def workload_leg(name, dtype, steps, warmup):
     preset = presets.get(name)
     x = presets.make_inputs(preset, dtype=dtype, device="cuda")
     fp32_acc = msda_ops._use_fp32_grad_accum(x["value"])
-    gs, one, evs = device_leg(x, steps, warmup, fp32_acc)
+    gs, one, evs, in_graph = device_leg(x, steps, warmup, fp32_acc)
     for e in evs:
         one(e)
     f = statistics.fmean(split_ms(e)[0] for e in evs)
     b = statistics.fmean(split_ms(e)[1] for e in evs)
-    inner = statistics.fmean(in_graph_ms(e) for e in evs)
+    inner = in_graph(steps)
     B, S, M, D = x["value"].shape
     Q = x["sampling_locations"].shape[1]
     fwd_b, bwd_b = algorithmic_bytes(B, S, Q, M, D, preset.L, preset.K, x["value"].element_size())
@@ -479,10 +492,10 @@ def public_op_leg(op, x, steps, warmup, **kwargs):
     ``op(value, spatial_shapes, level_start_index, sampling_locations,
     attention_weights, **kwargs)``, captured as one CUDA graph per step and
     timed like the device leg (L2 flushed before every step, CUDA events).
-    Besides the events around the replay, event nodes inside the graph mark
-    its first and last node, so the step's device time is also reported
-    without the graph's launch latency. Returns mean (fwd ms, bwd ms,
-    in-graph fwd+bwd ms)."""
+    A second graph of the same step with event nodes at its first and last
+    node, replayed after the timed ones, gives the step's device time without
+    the graph launch latency. Returns mean (fwd ms, bwd ms, in-graph fwd+bwd
+    ms)."""
     shapes, starts = x["spatial_shapes"], x["level_start_index"]
     v = x["value"].detach().clone().requires_grad_(True)
     l = x["sampling_locations"].detach().clone().requires_grad_(True)
@@ -501,12 +514,16 @@ def public_op_leg(op, x, steps, warmup, **kwargs):
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     ev = {k: torch.cuda.Event(enable_timing=True, external=True) for k in ("first", "mid", "last")}
-    graph = torch.cuda.CUDAGraph()
+    graph = torch.cuda.CUDAGraph()  # timed: one event node splits forward from backward
     with torch.cuda.graph(graph):
-        ev["first"].record()
         out = op(v, shapes, starts, l, a, **kwargs)
         ev["mid"].record()
         grads = torch.autograd.grad(out, (v, l, a), g)
+    inner_graph = torch.cuda.CUDAGraph()  # untimed copy with event nodes at its ends
+    with torch.cuda.graph(inner_graph):
+        ev["first"].record()
+        out2 = op(v, shapes, starts, l, a, **kwargs)
+        grads2 = torch.autograd.grad(out2, (v, l, a), g)
         ev["last"].record()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     drain = torch.ones(L2_DRAIN_BYTES // 4, dtype=torch.float32, device="cuda")
@@ -522,8 +539,13 @@ def public_op_leg(op, x, steps, warmup, **kwargs):
         if i >= warmup:
             fwd.append(e0.elapsed_time(ev["mid"]))
             bwd.append(ev["mid"].elapsed_time(e1))
-            inner.append(ev["first"].elapsed_time(ev["last"]))
-    del graph, out, grads
+    for i in range(steps):
+        flush.fill_(1)
+        drain.sum()
+        inner_graph.replay()
+        ev["last"].synchronize()
+        inner.append(ev["first"].elapsed_time(ev["last"]))
+    del graph, inner_graph, out, grads, out2, grads2
     return statistics.fmean(fwd), statistics.fmean(bwd), statistics.fmean(inner)
 
 
@@ -830,8 +852,8 @@ def main(argv=None) -> int:
         algo_flags |= lib.MSDA_BWD_DETERMINISTIC
 
     # ---- device leg -------------------------------------------------------
-    gs, one, evs = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
-                              use_graph=not args.no_graph)
+    gs, one, evs, in_graph = device_leg(x, args.steps, args.warmup, fp32_acc, algo_flags,
+                                        use_graph=not args.no_graph)
     barrier(world)
     with ClockSampler(torch.cuda.current_device()) as clk:
         for e in evs:
@@ -840,9 +862,10 @@ def main(argv=None) -> int:
     fwd_ms = [split_ms(e)[0] for e in evs]
     bwd_ms = [split_ms(e)[1] for e in evs]
     dev_total_ms = max_over_ranks(sum(f + b for f, b in zip(fwd_ms, bwd_ms)), world)
-    inner = [in_graph_ms(e) for e in evs]
-    in_graph_us = (max_over_ranks(statistics.fmean(inner), world) * 1e3
-                   if None not in inner else None)
+    # Device time of the same step between its graph's first and last node
+    # (a second graph with those two event nodes, after the timed region).
+    in_graph_us = (max_over_ranks(in_graph(min(args.steps, 50)), world) * 1e3
+                   if in_graph is not None else None)
     fwd_mean = max_over_ranks(statistics.fmean(fwd_ms), world)
     bwd_mean = max_over_ranks(statistics.fmean(bwd_ms), world)
 
