@@ -949,7 +949,7 @@ def main(argv=None) -> int:
     if world == 1 and not args.no_gpu_bar:
         pd = [(preset, dtype)]
         if args.config == "decoder" and dtype == torch.bfloat16:
-            pd.append((presets.get("encoder"), torch.bfloat16))
+            pd += [(presets.get("encoder"), torch.bfloat16), (presets.get("m2f"), torch.float16)]
         bar = gpu_bar(pd, min(args.steps, 20), 3)
 
     if rank == 0:
