@@ -147,10 +147,15 @@ __device__ __forceinline__ void fwd_store_row(T* op, int D, int lane, float (&ac
 // (batch, head) slice, so neighbouring queries' shared corner rows are
 // re-read from L1 and the level table is loaded once per CTA.
 // FUSED: the layer's prologue runs here (OpParams::ref / fused; QW = 1).
+// SHARE (needs QW * L * K <= 32, checked on the host): lane i resolves point
+// i of the warp's QW queries once per round (coalesced parameter loads), and
+// each step fetches its point's corner rows, fractions, weight and validity
+// from that lane by shuffle instead of the group's lanes each resolving it.
 template <typename T, int VEC, int LPR, int CPL, int WARPS, int NB, int MINB, bool FUSED = false,
-          int QW = 1, int QPW = 1>
+          int QW = 1, int QPW = 1, bool SHARE = false>
 __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpParams p) {
   static_assert(!FUSED || QW == 1, "the fused prologue's softmax spans the warp");
+  static_assert(!SHARE || !FUSED, "SHARE: no fused prologue");
   constexpr int G = 32 / LPR;
   static_assert(QW >= 1 && G % QW == 0, "QW must divide the lane groups");
   constexpr int GQ = G / QW;
@@ -207,27 +212,72 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) msda_fwd_kernel(const OpPara
 #pragma unroll
       for (int v = 0; v < VEC; ++v) acc[j][v] = 0.f;
     }
+    // SHARE: this lane's own point (query my_q of the warp, point my_s).
+    int sh_p00 = 0, sh_p10 = 0;
+    unsigned sh_valid = 0u;
+    float sh_lx = 0.f, sh_ly = 0.f, sh_at = 0.f;
+    if constexpr (SHARE) {
+      const int my_q = lane / LK, my_s = lane - my_q * LK;
+      const int64_t q_mine = q - qsub + my_q;  // the warp's first query + my_q
+      if (my_q < QW && q_mine < p.Q) {
+        const int64_t qm_mine = (b * p.Q + q_mine) * p.M + m;
+        const T* lpm = reinterpret_cast<const T*>(p.loc) + qm_mine * (2 * LK);
+        const float2 xy = load_pair(lpm + 2 * my_s);
+        sh_at = to_f32(reinterpret_cast<const T*>(p.attn)[qm_mine * LK + my_s]);
+        const Bilinear bm = resolve(xy.x, xy.y, lv[level_of(my_s, p.K, p.kshift)]);
+        sh_p00 = bm.pix[0];
+        sh_p10 = bm.pix[2];
+        sh_lx = bm.lx;
+        sh_ly = bm.ly;
+        sh_valid = bm.valid;
+      }
+    }
 
     for (int s0 = 0; s0 < LK; s0 += GQ * NB) {
       Bilinear bl[NB];
       float at[NB];
+      if constexpr (SHARE) {
 #pragma unroll
-      for (int n = 0; n < NB; ++n) {
-        const int s = s0 + n * GQ + gq;
-        if (live && s < LK) {
-          const float2 xy = load_pair(lp + 2 * s);
-          const float a = to_f32(ap[s]);
-          const LevelInfo& L = one_step ? lvn[QPW > 1 ? n : 0] : lv[level_of(s, p.K, p.kshift)];
-          if constexpr (FUSED) {
-            at[n] = expf(a - smx) * sinv;
-            bl[n] = resolve_fused(refp, xy, L);
+        for (int n = 0; n < NB; ++n) {
+          const int s = s0 + n * GQ + gq;
+          const int src = qsub * LK + (s < LK ? s : 0);
+          const int p00 = __shfl_sync(kFullMask, sh_p00, src), p10 = __shfl_sync(kFullMask, sh_p10, src);
+          const float lx = __shfl_sync(kFullMask, sh_lx, src), ly = __shfl_sync(kFullMask, sh_ly, src);
+          const float a = __shfl_sync(kFullMask, sh_at, src);
+          const unsigned v = __shfl_sync(kFullMask, sh_valid, src);
+          bl[n].pix[0] = p00;
+          bl[n].pix[1] = p00 + 1;
+          bl[n].pix[2] = p10;
+          bl[n].pix[3] = p10 + 1;
+          bl[n].lx = lx;
+          bl[n].ly = ly;
+          bl[n].w[0] = (1.0f - lx) * (1.0f - ly);
+          bl[n].w[1] = lx * (1.0f - ly);
+          bl[n].w[2] = (1.0f - lx) * ly;
+          bl[n].w[3] = lx * ly;
+          const bool ok = live && s < LK;
+          bl[n].valid = ok ? v : 0u;
+          at[n] = ok ? a : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < NB; ++n) {
+          const int s = s0 + n * GQ + gq;
+          if (live && s < LK) {
+            const float2 xy = load_pair(lp + 2 * s);
+            const float a = to_f32(ap[s]);
+            const LevelInfo& L = one_step ? lvn[QPW > 1 ? n : 0] : lv[level_of(s, p.K, p.kshift)];
+            if constexpr (FUSED) {
+              at[n] = expf(a - smx) * sinv;
+              bl[n] = resolve_fused(refp, xy, L);
+            } else {
+              at[n] = a;
+              bl[n] = resolve(xy.x, xy.y, L);
+            }
           } else {
-            at[n] = a;
-            bl[n] = resolve(xy.x, xy.y, L);
+            at[n] = 0.f;
+            bl[n] = empty_slot();
           }
-        } else {
-          at[n] = 0.f;
-          bl[n] = empty_slot();
         }
       }
       Raw raw[NB][4][CPL];
@@ -318,8 +368,10 @@ constexpr int kBwdCapWarps = 8;
 // lane groups each) over QPW rounds of consecutive queries; the same-row
 // merge then matches (row, query) keys, since only one query's corners share
 // a grad_out vector. FUSED and the hit-counted mode take QW = QPW = 1.
+// SHARE as in the forward: lane i resolves point i of the warp's queries once
+// per round and the lane groups fetch it by shuffle (QW * L * K <= 32).
 template <typename T, typename A, int VEC, int LPR, int CPL, int WARPS, int NB, int MODE, bool FUSED = false,
-          int QW = 1, int QPW = 1>
+          int QW = 1, int QPW = 1, bool SHARE = false>
 __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNTED_MIN_BLOCKS : MSDA_BWD_MIN_BLOCKS) *
                                                   kBwdCapWarps / WARPS)
     msda_bwd_kernel(const OpParams p) {
@@ -335,6 +387,7 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
   constexpr int G = 32 / LPR;
   static_assert((QW == 1 || QW == 2) && G % QW == 0, "QW: 1 or 2 queries per warp");
   static_assert(QW == 1 || (!FUSED && MODE != kCounted), "one query per warp for FUSED / kCounted");
+  static_assert(!SHARE || (!FUSED && NB == 1), "SHARE: one point per group, no fused prologue");
   constexpr int GQ = G / QW;
   using Raw = typename Pack<T, VEC>::Raw;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -441,18 +494,40 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
     // every iteration then loads the next one's while its gathers are in flight.
     float2 pxy[NB];
     float pat[NB];
+    // SHARE: this lane's own point (query my_q of the warp, point my_s).
+    const int my_q = SHARE ? lane / LK : 0, my_s = SHARE ? lane - my_q * LK : 0;
+    const bool my_live = SHARE && my_q < QW && q - qsub + my_q < p.Q;
 #pragma unroll
     for (int n = 0; n < NB; ++n) {
       const int s = n * GQ + gq_;
       pxy[n] = make_float2(0.f, 0.f);
       pat[n] = 0.f;
-      if (live && s < LK) {
+      if constexpr (SHARE) {
+        if (my_live) {
+          const int64_t qm_mine = (b * p.Q + (q - qsub + my_q)) * p.M + m;
+          pxy[n] = load_pair(reinterpret_cast<const T*>(p.loc) + qm_mine * (2 * LK) + 2 * my_s);
+          pat[n] = to_f32(reinterpret_cast<const T*>(p.attn)[qm_mine * LK + my_s]);
+        }
+      } else if (live && s < LK) {
         pxy[n] = load_pair(lp + 2 * s);
         pat[n] = to_f32(ap[s]);
       }
     }
     if (round == 0) load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);  // syncs the block
     if (!__any_sync(kFullMask, live)) break;  // warp-uniform: past the last query
+    int sh_p00 = 0, sh_p10 = 0;
+    unsigned sh_valid = 0u;
+    float sh_lx = 0.f, sh_ly = 0.f;
+    if constexpr (SHARE) {
+      if (my_live) {
+        const Bilinear bm = resolve(pxy[0].x, pxy[0].y, lv[level_of(my_s, p.K, p.kshift)]);
+        sh_p00 = bm.pix[0];
+        sh_p10 = bm.pix[2];
+        sh_lx = bm.lx;
+        sh_ly = bm.ly;
+        sh_valid = bm.valid;
+      }
+    }
     // Fused prologue: this query's reference point and its head's softmax;
     // sdot accumulates sum_s a_s * dL/da_s for the softmax backward.
     float2 refp = make_float2(0.f, 0.f);
@@ -467,27 +542,53 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
       float at[NB];
       float fw[NB], fh[NB];
       bool dense[NB];
+      if constexpr (SHARE) {
+        const int s = s0 + gq_;
+        const bool ok = live && s < LK;
+        const int src = qsub * LK + (s < LK ? s : 0);
+        const int p00 = __shfl_sync(kFullMask, sh_p00, src), p10 = __shfl_sync(kFullMask, sh_p10, src);
+        const float lx = __shfl_sync(kFullMask, sh_lx, src), ly = __shfl_sync(kFullMask, sh_ly, src);
+        const float a = __shfl_sync(kFullMask, pat[0], src);
+        const unsigned v = __shfl_sync(kFullMask, sh_valid, src);
+        bl[0].pix[0] = p00;
+        bl[0].pix[1] = p00 + 1;
+        bl[0].pix[2] = p10;
+        bl[0].pix[3] = p10 + 1;
+        bl[0].lx = lx;
+        bl[0].ly = ly;
+        bl[0].w[0] = (1.0f - lx) * (1.0f - ly);
+        bl[0].w[1] = lx * (1.0f - ly);
+        bl[0].w[2] = (1.0f - lx) * ly;
+        bl[0].w[3] = lx * ly;
+        bl[0].valid = ok ? v : 0u;
+        at[0] = ok ? a : 0.f;
+        const LevelInfo& L = lv[level_of(ok ? s : 0, p.K, p.kshift)];
+        fw[0] = ok ? L.fW : 0.f;
+        fh[0] = ok ? L.fH : 0.f;
+        dense[0] = ok && L.dense;
+      } else {
 #pragma unroll
-      for (int n = 0; n < NB; ++n) {
-        const int s = s0 + n * GQ + gq_;
-        if (live && s < LK) {
-          const float2 xy = pxy[n];  // loaded one iteration ahead
-          const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
-          if constexpr (FUSED) {
-            at[n] = expf(pat[n] - smx) * sinv;
-            bl[n] = resolve_fused(refp, xy, L);
+        for (int n = 0; n < NB; ++n) {
+          const int s = s0 + n * GQ + gq_;
+          if (live && s < LK) {
+            const float2 xy = pxy[n];  // loaded one iteration ahead
+            const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
+            if constexpr (FUSED) {
+              at[n] = expf(pat[n] - smx) * sinv;
+              bl[n] = resolve_fused(refp, xy, L);
+            } else {
+              at[n] = pat[n];
+              bl[n] = resolve(xy.x, xy.y, L);
+            }
+            fw[n] = L.fW;
+            fh[n] = L.fH;
+            dense[n] = L.dense;
           } else {
-            at[n] = pat[n];
-            bl[n] = resolve(xy.x, xy.y, L);
+            at[n] = 0.f;
+            fw[n] = fh[n] = 0.f;
+            bl[n] = empty_slot();
+            dense[n] = false;
           }
-          fw[n] = L.fW;
-          fh[n] = L.fH;
-          dense[n] = L.dense;
-        } else {
-          at[n] = 0.f;
-          fw[n] = fh[n] = 0.f;
-          bl[n] = empty_slot();
-          dense[n] = false;
         }
       }
       Raw raw[NB][4][CPL];
@@ -515,7 +616,7 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
 #pragma unroll
       for (int n = 0; n < NB; ++n) {
         const int sn = s0 + GQ * NB + n * GQ + gq_;
-        if (live && sn < LK) {
+        if (!SHARE && live && sn < LK) {
           pxy[n] = load_pair(lp + 2 * sn);
           pat[n] = to_f32(ap[sn]);
         }

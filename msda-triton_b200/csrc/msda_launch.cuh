@@ -130,6 +130,16 @@ static cudaError_t fwd_launch(const OpParams& p, bool short_grid, cudaStream_t s
   constexpr int NBL = FUSED ? NB : 1;
   constexpr int per_cta = kLongWarps * QW * kLongRounds;
   const dim3 grid((unsigned)((p.Q + per_cta - 1) / per_cta), (unsigned)p.M, (unsigned)p.B);
+  // When the warp's queries have at most 32 points between them, each lane
+  // resolves one point per round and the lane groups fetch it by shuffle
+  // (measured: encoder forward 351 -> 299 us, Mask2Former 150 -> 129 us).
+  if constexpr (!FUSED) {
+    if (QW * p.L * p.K <= 32) {
+      msda_fwd_kernel<T, VEC, LPR, CPL, kLongWarps, 1, 0, false, QW, kLongRounds, true>
+          <<<grid, kLongWarps * 32, 0, st>>>(p);
+      return cudaGetLastError();
+    }
+  }
   msda_fwd_kernel<T, VEC, LPR, CPL, kLongWarps, NBL, 0, FUSED, QW, kLongRounds><<<grid, kLongWarps * 32, 0, st>>>(p);
   return cudaGetLastError();
 }
@@ -156,6 +166,11 @@ static cudaError_t bwd_launch(const OpParams& p, bool short_grid, bool pdl, cuda
     if (!short_grid) {
       constexpr int per_cta = kLongWarps * 2 * kLongRounds;
       const dim3 grid((unsigned)((p.Q + per_cta - 1) / per_cta), (unsigned)p.M, (unsigned)p.B);
+      // Points shared by lane when the warp's 2 queries have at most 32
+      // (encoder fp32 backward 851 -> 836 us, native 828 -> 800 us).
+      if (2 * p.L * p.K <= 32)
+        return launch_ex(msda_bwd_kernel<T, A, VEC, LPR, CPL, kLongWarps, 1, MODE, false, 2, kLongRounds, true>,
+                         grid, dim3(kLongWarps * 32), 0, st, pdl, p);
       return launch_ex(msda_bwd_kernel<T, A, VEC, LPR, CPL, kLongWarps, 1, MODE, false, 2, kLongRounds>, grid,
                        dim3(kLongWarps * 32), 0, st, pdl, p);
     }

@@ -535,13 +535,18 @@ def test_backward_algorithms(name, kw, lo, hi, dtype, algo):
 # ---------------------------------------------------------------------------
 # Long grids (more query-heads than a few waves of one-query warps) take the
 # multi-query launch shapes: 2 queries per warp, rounds of consecutive
-# queries per CTA. Ragged query counts leave partially live warps and CTAs.
+# queries per CTA, and -- when the warp's queries have at most 32 points --
+# one point resolved per lane and shared with the lane groups. Ragged query
+# counts leave partially live warps and CTAs.
 # ---------------------------------------------------------------------------
 LONG_CASES = [
     ("dense_l2k4", dict(B=1, Q=3001, M=8, D=32, K=4, shapes=[(30, 40), (15, 20)]), 0.3, 0.7),
     ("dense_l3k4_oob", dict(B=1, Q=2999, M=8, D=32, K=4, shapes=[(32, 32), (16, 16), (8, 8)]), -0.1, 1.1),
     ("d64_k3", dict(B=2, Q=1203, M=8, D=64, K=3, shapes=[(20, 30), (10, 15)]), 0.0, 1.0),
     ("sparse", dict(B=1, Q=3001, M=8, D=32, K=4, shapes=[(100, 200)]), 0.0, 1.0),
+    # 24 points per query: 2 queries exceed a warp's 32 lanes, so the long
+    # shape resolves points per lane group instead of sharing them.
+    ("many_points", dict(B=1, Q=2501, M=8, D=32, K=8, shapes=[(30, 40), (15, 20), (8, 10)]), -0.05, 1.05),
 ]
 _LONG_CACHE: dict = {}
 
