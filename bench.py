@@ -379,10 +379,12 @@ def kernel_breakdown(one, steps=5):
     return {k: (statistics.fmean(v), len(v) / steps) for k, v in agg.items()}
 
 
-def backward_algorithm(kernels):
+def backward_algorithm(kernels, deterministic=False):
     if "msda_absmax_kernel" in kernels:
         kind = "counted" if "msda_count_kernel" in kernels else "scatter"
         return f"deterministic {kind} (64-bit fixed-point rows)"
+    if deterministic and "msda_count_kernel" in kernels:
+        return "deterministic counted (exact integer-valued fp32 rows; 64-bit rows past 32 hits)"
     if "msda_count_kernel" in kernels:
         return "counted (fp32 rows for multi-hit pixels)"
     if "msda_cast_kernel" in kernels:
@@ -917,7 +919,7 @@ def main(argv=None) -> int:
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (bwd_mean / 1e3) / 1e9
     step_achieved = (fwd_b + bwd_b) / ((fwd_mean + bwd_mean) / 1e3) / 1e9
-    algo = backward_algorithm(kernels) if kernels else "automatic (not inspected)"
+    algo = backward_algorithm(kernels, args.deterministic) if kernels else "automatic (not inspected)"
     roofline = {"kernel": "msda_backward call (" + " + ".join(
                     k for k in kernels if k != "msda_fwd_kernel") + "), CUDA-event time",
                 "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

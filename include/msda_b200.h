@@ -96,6 +96,16 @@ typedef enum msda_status {
  * claim then). Takes the hit-counted algorithm for sparse sampling
  * (Q*L*K <= 2*S), else the scatter; MSDA_BWD_FORCE_SCATTER / _COUNTED pick
  * one. MSDA_BWD_FP32_ACCUM is implied.
+ * fp16 / bf16 values in the hit-counted algorithm need no absmax pass and
+ * reduce most rows in 4-byte words: the count pass also records, per
+ * grad_value row, a bound on its contributions (max |attention weight| *
+ * max |grad_output row| over the points hitting it). A row with 2 to 32
+ * hits gets every contribution rounded once to an integer multiple of 2^-F,
+ * 2^F chosen from that bound and the hit count so that every partial sum is
+ * an integer below 2^24: exact in fp32, hence order-independent, on a grid of
+ * at most 2^-19 of the bound; the reductions move the bytes of fp32
+ * accumulation. Busier rows take 64-bit integers on a per-row scale from the
+ * same bound (a grid of 2^-51 of it).
  * Needs a workspace (msda_backward_workspace_size with this flag). */
 #define MSDA_BWD_DETERMINISTIC 16u
 /* Sibling gathers only (msda_grid_sample_backward, msda_roi_align_backward;

@@ -68,16 +68,19 @@ constexpr double kMergeMinPointsPerRow = 2.0;
 constexpr uint32_t kKnownBwdFlags = MSDA_BWD_FP32_ACCUM | MSDA_BWD_FORCE_SCATTER | MSDA_BWD_FORCE_COUNTED |
                                     MSDA_BWD_DETERMINISTIC;
 
-enum class Algo { kScatterNative, kScatterF32, kCounted, kScatterFixed, kCountedFixed };
+enum class Algo { kScatterNative, kScatterF32, kCounted, kScatterFixed, kCountedFixed, kCountedExact };
 
 Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags) {
   const bool fp32_ws = (flags & MSDA_BWD_FP32_ACCUM) && dtype != MSDA_DTYPE_F32;
   const bool fp32_semantics = (flags & MSDA_BWD_FP32_ACCUM) || dtype == MSDA_DTYPE_F32;
   const double density = (double)s.Q * s.L * s.K / (double)s.S;
-  if (flags & MSDA_BWD_DETERMINISTIC) {  // 64-bit fixed-point accumulation
+  if (flags & MSDA_BWD_DETERMINISTIC) {
+    // Hit-counted: exact integer-valued fp32 rows for fp16 / bf16, 64-bit
+    // fixed point for fp32 values; the scatter: 64-bit fixed point.
+    const Algo counted = dtype == MSDA_DTYPE_F32 ? Algo::kCountedFixed : Algo::kCountedExact;
     if (flags & MSDA_BWD_FORCE_SCATTER) return Algo::kScatterFixed;
-    if (flags & MSDA_BWD_FORCE_COUNTED) return Algo::kCountedFixed;
-    return density <= kCountedMaxPointsPerRow ? Algo::kCountedFixed : Algo::kScatterFixed;
+    if (flags & MSDA_BWD_FORCE_COUNTED) return counted;
+    return density <= kCountedMaxPointsPerRow ? counted : Algo::kScatterFixed;
   }
   const Algo scatter = fp32_ws ? Algo::kScatterF32 : Algo::kScatterNative;
   if (flags & MSDA_BWD_FORCE_SCATTER) return scatter;
@@ -93,17 +96,17 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags) {
 constexpr size_t kFixedHeaderBytes = 256;
 
 // Workspace of the hit-counted scatter: [absmax header (fixed point only)]
-// per-row hit counts, then one accumulator row per grad_value row -- fp32
-// (fp16/bf16 only; fp32 values accumulate in grad_value itself) or 64-bit
-// fixed point (every dtype).
-size_t counted_ws_bytes(const Shape& s, int32_t dtype, bool fixed, size_t* counts_offset,
+// per-row hit counts, [per-row bounds (exact rows only)], then one
+// accumulator row per grad_value row -- fp32 (fp16/bf16 only; fp32 values
+// accumulate in grad_value itself) or 64-bit fixed point (every dtype).
+size_t counted_ws_bytes(const Shape& s, int32_t dtype, bool fixed, bool exact, size_t* counts_offset,
                         size_t* acc_offset) {
   const size_t rows = (size_t)s.B * s.S * s.M;
   const size_t head = fixed ? kFixedHeaderBytes : 0;
-  const size_t counts = align256(rows * sizeof(unsigned));
+  const size_t counts = align256(rows * sizeof(unsigned)) * (exact ? 2 : 1);
   *counts_offset = head;
   *acc_offset = head + counts;
-  if (fixed) return head + counts + rows * (size_t)s.D * sizeof(long long);
+  if (fixed || exact) return head + counts + rows * (size_t)s.D * sizeof(long long);
   if (dtype == MSDA_DTYPE_F32) return counts;
   return counts + rows * (size_t)s.D * sizeof(float);
 }
@@ -212,9 +215,9 @@ size_t msda_backward_workspace_size(int64_t batch, int64_t num_values, int64_t n
     return 0;
   if (flags & ~kKnownBwdFlags) return 0;
   const Algo a = choose_algo(s, dtype, flags);
-  if (a == Algo::kCounted || a == Algo::kCountedFixed) {
+  if (a == Algo::kCounted || a == Algo::kCountedFixed || a == Algo::kCountedExact) {
     size_t coff, aoff;
-    return counted_ws_bytes(s, dtype, a == Algo::kCountedFixed, &coff, &aoff);
+    return counted_ws_bytes(s, dtype, a == Algo::kCountedFixed, a == Algo::kCountedExact, &coff, &aoff);
   }
   const size_t elems = (size_t)batch * (size_t)num_values * (size_t)num_heads * (size_t)head_dim;
   if (a == Algo::kScatterFixed) return kFixedHeaderBytes + elems * sizeof(long long);
@@ -257,12 +260,13 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   const Algo algo = choose_algo(s, dtype, flags);
   const bool fixed = algo == Algo::kScatterFixed || algo == Algo::kCountedFixed;
   const bool fp32_ws = algo == Algo::kScatterF32;
-  const bool counted = algo == Algo::kCounted || algo == Algo::kCountedFixed;
+  const bool exact = algo == Algo::kCountedExact;
+  const bool counted = algo == Algo::kCounted || algo == Algo::kCountedFixed || exact;
   const bool ws_target = fp32_ws || algo == Algo::kScatterFixed;  // reductions into the workspace
   const size_t ws_need = msda_backward_workspace_size(s.B, s.S, s.Q, s.M, s.D, s.L, s.K, dtype, flags);
   if (fp32_ws || counted || fixed) {
     if (!workspace || workspace_bytes < ws_need)
-      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: %s accumulation needs a workspace of %zu bytes (got %zu)", fn, fixed ? "deterministic" : "fp32", ws_need, workspace_bytes);
+      return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: %s accumulation needs a workspace of %zu bytes (got %zu)", fn, (fixed || exact) ? "deterministic" : "fp32", ws_need, workspace_bytes);
     if (!aligned(workspace, 16))
       return fail(MSDA_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
   }
@@ -281,10 +285,11 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
 
   cudaError_t e;
   size_t counts_off = 0, acc_off = 0;
+  const size_t rows = (size_t)s.B * s.S * s.M;
   if (counted) {
-    counted_ws_bytes(s, dtype, fixed, &counts_off, &acc_off);
-    // Counts (and the absmax header before them).
-    e = cudaMemsetAsync(workspace, 0, counts_off + (size_t)s.B * s.S * s.M * sizeof(unsigned), st);
+    counted_ws_bytes(s, dtype, fixed, exact, &counts_off, &acc_off);
+    // Counts (and the absmax header before them, the row bounds after them).
+    e = cudaMemsetAsync(workspace, 0, exact ? acc_off : counts_off + rows * sizeof(unsigned), st);
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count zero-fill");
   }
   // The backward may overlap the tail of the kernel before it when that
@@ -328,7 +333,8 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.fused = fused ? 1 : 0;
   p.grad_out = grad_output;
   p.grad_value = counted ? grad_value : target;
-  p.acc_words = fixed ? 2 : 1;
+  p.acc_words = (fixed || exact) ? 2 : 1;
+  if (exact) p.rowmax = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + counts_off + align256(rows * sizeof(unsigned)));
   p.fixed_hdr = fixed_hdr;
   p.fixed_log2n = ceil_log2(s.Q * s.K);
   p.grad_loc = grad_sampling_locations;
@@ -344,9 +350,9 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.BQM = s.B * s.Q * s.M;
   if (counted) {
     switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, sm_count(), st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, sm_count(), st); break;
-      default: e = msda::launch_count<__nv_bfloat16>(p, sm_count(), st); break;
+      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, sm_count(), exact, st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, sm_count(), exact, st); break;
+      default: e = msda::launch_count<__nv_bfloat16>(p, sm_count(), exact, st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count launch");
   }
@@ -355,7 +361,10 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   // them before the reductions. Sparse sampling rarely does.
   const bool merge = (double)s.Q * s.L * s.K > kMergeMinPointsPerRow * (double)s.S;
   const int mode = counted ? msda::kCounted : merge ? msda::kScatterMerge : msda::kScatter;
-  const int acc = fixed ? msda::kAccFixed : (fp32_ws || dtype == MSDA_DTYPE_F32) ? msda::kAccF32 : msda::kAccNative;
+  const int acc = fixed   ? msda::kAccFixed
+                  : exact ? msda::kAccExact
+                  : (fp32_ws || dtype == MSDA_DTYPE_F32) ? msda::kAccF32
+                                                         : msda::kAccNative;
   switch (dtype) {
     case MSDA_DTYPE_F32: e = msda::launch_backward<float>(p, cfg, mode, acc, bwd_pdl, st); break;
     case MSDA_DTYPE_F16: e = msda::launch_backward<__half>(p, cfg, mode, acc, bwd_pdl, st); break;
@@ -365,9 +374,9 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   if (counted) {
     const bool fvec = aligned(grad_value, 16);
     switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_finalize<float>(p, fvec, fixed, sm_count(), st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_finalize<__half>(p, fvec, fixed, sm_count(), st); break;
-      default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, fixed, sm_count(), st); break;
+      case MSDA_DTYPE_F32: e = msda::launch_finalize<float>(p, fvec, fixed, exact, sm_count(), st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_finalize<__half>(p, fvec, fixed, exact, sm_count(), st); break;
+      default: e = msda::launch_finalize<__nv_bfloat16>(p, fvec, fixed, exact, sm_count(), st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward finalize launch");
   }

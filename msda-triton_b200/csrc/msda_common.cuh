@@ -89,6 +89,12 @@ __device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
   *reinterpret_cast<typename Pack<T, VEC>::Raw*>(p) = pk.raw;
 }
 
+// max(m, |x|) that keeps a NaN (fmaxf would drop it).
+__device__ __forceinline__ float max_abs_nan(float m, float x) {
+  const float ax = fabsf(x);
+  return (ax > m || ax != ax) ? ax : m;
+}
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch. A kernel launched with programmatic stream
 // serialization may start while the kernel before it still runs; pdl_wait()
@@ -353,6 +359,77 @@ template <>
 struct IsFixed<long long> {
   static constexpr bool value = true;
 };
+
+// Deterministic grad_value of fp16 / bf16 data in the hit-counted algorithm:
+// the accumulator rows stay fp32, and every contribution to a row with three
+// or more hits is made an integer-valued float (exact_scale), so the row's
+// partial sums are exact integers below 2^24 and do not depend on the order
+// the reductions land in.
+struct ExactF32 {
+  float v;
+};
+template <typename A>
+struct IsExact {
+  static constexpr bool value = false;
+};
+template <>
+struct IsExact<ExactF32> {
+  static constexpr bool value = true;
+};
+
+// 2^k as a float, k in [-126, 127].
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((k + 127) << 23); }
+
+// Rounds x (|x| < 2^22) to an integer-valued float: the FMA with 1.5 * 2^23
+// leaves round(x) in the low mantissa bits, the subtraction is exact.
+constexpr float kExactMagic = 12582912.0f;  // 1.5 * 2^23
+
+// Scale 2^F of an exact row: n >= 2 hits whose products |a w_c g| are below
+// the bound rowmax (the bits of max |a| * max|grad_out row| over the row's
+// points) < 2^E. Each contribution fl(a w_c g) * 2^F is below 2^(E + F) =
+// 2^(24 - max(ceil(log2 n), 2)) <= 2^22 before rounding, so every partial sum
+// of the n rounded terms is an integer of magnitude <= 2^24: exact in fp32
+// (and never a denormal, which fp32 `red` would flush). F lies in [-126, 147]
+// and is applied as 2^F1 on the weight before the product
+// (F1 = max(F - 64, 0): the products of tiny rows stay normal floats) and
+// 2^F2 on the product. Returns false for the fp32 fallback: a non-finite
+// bound, one so large that F < -126, or rowmax == 0 (then every contribution
+// is zero).
+struct ExactScale {
+  float s1, s2;      // 2^F1, 2^F2
+  float inv1, inv2;  // 2^-F1, 2^-F2
+};
+
+__device__ __forceinline__ bool exact_scale(unsigned rowmax, unsigned n, ExactScale& xs) {
+  const int E = max((int)(rowmax >> 23), 1) - 126;  // rowmax < 2^E (denormals: 2^-125)
+  const int l2n = max(32 - __clz(n - 1u), 2);       // ceil(log2 n), at least 2
+  const int F = 24 - E - l2n;
+  const bool ok = rowmax - 1u < 0x7f7fffffu && F >= -126;
+  const int F2 = ok ? min(F, 64) : 0, F1 = ok ? F - F2 : 0;
+  xs.s1 = pow2f(F1);
+  xs.s2 = pow2f(F2);
+  xs.inv1 = pow2f(-F1);
+  xs.inv2 = pow2f(-F2);
+  return ok;
+}
+
+// Rows of the exact hit-counted algorithm with more hits than this use
+// 64-bit integers instead (wide_scale): the integer-valued fp32 grid is
+// 2^(ceil(log2 hits) - 24) of the row's bound, at most 2^-19 of it up to here.
+constexpr unsigned kExactMaxHits = 32;
+
+// Scale 2^F of a 64-bit exact row (more than kExactMaxHits hits, bound
+// rowmax < 2^E): contributions a w_c g (exact in fp64) times 2^F stay below
+// 2^51 (rounded to an integer by one fp64 FMA) and n of them below 2^62.
+// Returns false (fp32 fallback) for a zero or non-finite bound.
+__device__ __forceinline__ bool wide_scale(unsigned rowmax, unsigned n, double& scale, double& inv) {
+  const int E = max((int)(rowmax >> 23), 1) - 126;
+  const int l2n = 32 - __clz(n - 1u);
+  const int F = min(51 - E, 62 - E - l2n);  // in [-98, 176]
+  scale = __longlong_as_double((long long)(1023 + F) << 52);
+  inv = __longlong_as_double((long long)(1023 - F) << 52);
+  return rowmax - 1u < 0x7f7fffffu;
+}
 
 constexpr double kFixedMagic = 6755399441055744.0;  // 1.5 * 2^52
 constexpr long long kFixedMagicBits = 0x4338000000000000ll;

@@ -38,6 +38,7 @@ struct OpParams {
   void* grad_attn;
   unsigned* counts;   // counted scatter: bilinear hits per (b, pixel, m) row
   void* acc;          // counted scatter: accumulator rows of the multi-hit rows
+  unsigned* rowmax;   // exact counted scatter: per-row bound of |a| * max|grad_out row|
   int acc_words;      // 32-bit words per accumulator element: 1 (fp32), 2 (64-bit fixed point)
   // Deterministic grad_value (64-bit fixed point): the absmax header and
   // ceil(log2(Q*K)), the bound on contributions per row.
@@ -380,6 +381,11 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
   // fixed_scale); the scatter target (kScatter*) or the multi-hit rows
   // (kCounted) hold fixed-point elements.
   constexpr bool FIXED = IsFixed<A>::value;
+  // A = ExactF32: deterministic fp16 / bf16 in the hit-counted mode -- rows
+  // with three or more hits receive integer-valued contributions on the
+  // row's scale (exact_scale) in their fp32 accumulator rows.
+  constexpr bool EXACT = IsExact<A>::value;
+  static_assert(!EXACT || (MODE == kCounted && sizeof(T) == 2), "exact rows: hit-counted fp16 / bf16");
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
   __shared__ float fused_ga[FUSED ? WARPS : 1][FUSED ? kFusedMaxLK : 1];  // fused: dL/da per point
@@ -404,6 +410,7 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
   float* accb = reinterpret_cast<float*>(p.acc) + head_base;  // kCounted, fp32 rows
   long long* faccb = reinterpret_cast<long long*>(p.acc) + head_base;  // kCounted, fixed point
   const unsigned* cnb = p.counts + (b * p.S * p.M + m);  // kCounted: row pix at cnb[pix * M]
+  const unsigned* rmb = p.rowmax + (b * p.S * p.M + m);  // EXACT: row pix's bound at rmb[pix * M]
   const int LK = p.L * p.K;
   // Scatter: keep the reduction target in L2, let the gathered value rows go first.
   uint64_t pol_keep = 0, pol_stream = 0;
@@ -593,6 +600,7 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
       }
       Raw raw[NB][4][CPL];
       unsigned hits[NB][4];
+      unsigned rmx[EXACT ? NB : 1][4];  // EXACT: the rows' bounds
 #pragma unroll
       for (int n = 0; n < NB; ++n)
 #pragma unroll
@@ -632,10 +640,18 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           hits[n][c] = 0u;
+          if constexpr (EXACT) rmx[n][c] = 0u;
           // Dense-level rows are always reduced in fp32: no count to read.
+          // Counts and bounds come from the kernel before this one, which may
+          // still run when this kernel starts (programmatic dependent
+          // launch): L2-coherent loads, not the read-only path, which would
+          // serve lines that were cached before it finished.
           if constexpr (MODE == kCounted && !COMBINE)
-            if ((bl[n].valid >> c) & 1u)
-              hits[n][c] = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)bl[n].pix[c] * p.M);
+            if ((bl[n].valid >> c) & 1u) {
+              // (EXACT reads them too: the scale needs the count below the flag)
+              hits[n][c] = dense[n] && !EXACT ? kDenseRow : __ldcg(cnb + (int64_t)bl[n].pix[c] * p.M);
+              if constexpr (EXACT) rmx[n][c] = __ldcg(rmb + (int64_t)bl[n].pix[c] * p.M);
+            }
         }
 #pragma unroll
       for (int n = 0; n < NB; ++n) {
@@ -729,7 +745,35 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
         if constexpr (SCATTER) {
           // Writes this lane's channels of a * w * grad_out into row `pix`
           // (weight wc; `hits` is the row's count in the counted mode).
-          auto scatter_row = [&](int pix, float wc, unsigned hits) {
+          auto scatter_row = [&](int pix, float wc, unsigned hits, unsigned rmax) {
+            // EXACT (rows of 64-bit words; fp32 rows in their first half): a
+            // row with 2 .. kExactMaxHits hits gets each contribution fl(wc g)
+            // as an integer-valued float on the row's scale, a row with
+            // more hits wc g * 2^F rounded to a 64-bit integer (wide); nothing
+            // when the bound is zero (every contribution is zero), plain fp32
+            // when the scale falls back.
+            bool exact_row = false, wide = false;
+            ExactScale xs{1.f, 1.f, 1.f, 1.f};
+            double wd = 0.0;
+            if constexpr (EXACT) {
+              if (hits > 1u) {  // a dense-level row (flagged) whatever its count
+                if (rmax == 0u) return;
+                const unsigned nh = hits & ~kDenseRow;
+                if (nh > kExactMaxHits) {
+                  double inv;
+                  wide = wide_scale(rmax, nh, wd, inv);
+                  wd *= (double)wc;  // exact: a power-of-two scale
+                } else {
+                  exact_row = exact_scale(rmax, nh, xs);
+                }
+              }
+            }
+            // exact rows: fl(wc 2^F1 g) (the weight's scale is exact), then
+            // the FMA applies 2^F2 and rounds to an integer
+            const float wcs = wc * xs.s1;
+            auto term = [&](float gv) {
+              return exact_row ? fmaf(__fmul_rn(wcs, gv), xs.s2, kExactMagic) - kExactMagic : __fmul_rn(wc, gv);
+            };
 #pragma unroll
             for (int j = 0; j < CPL; ++j) {
               const int ch = (j * LPR + sub) * VEC;
@@ -762,13 +806,28 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
                 // fp32 reduction in interleaved quads (see gq); a counted
                 // one-hit row is stored in the natural layout.
                 if (MODE != kCounted || hits != 1u) {
-                  float* row = (MODE == kCounted ? accb : reinterpret_cast<float*>(gvb)) + pix * rs;
+                  if constexpr (EXACT) {
+                    if (wide) {  // a lane's 4 channels fill one 32-byte sector
+#pragma unroll
+                      for (int k = 0; k < 2; ++k) {
+                        const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
+                        if (cq < D)
+#pragma unroll
+                          for (int e = 0; e < 4; ++e)
+                            red_fixed(faccb + pix * rs + cq + e, wd, (double)gq[j][k][e], pol_keep);
+                      }
+                      continue;
+                    }
+                  }
+                  float* row = MODE != kCounted ? reinterpret_cast<float*>(gvb) + pix * rs
+                               : EXACT          ? reinterpret_cast<float*>(faccb + pix * rs)
+                                                : accb + pix * rs;
 #pragma unroll
                   for (int k = 0; k < 2; ++k) {
                     const int cq = j * LPR * VEC + (k * LPR + sub) * 4;
                     if (cq < D)
-                      red_add_f32x4_hint(row + cq, wc * gq[j][k][0], wc * gq[j][k][1], wc * gq[j][k][2],
-                                         wc * gq[j][k][3], pol_keep);
+                      red_add_f32x4_hint(row + cq, term(gq[j][k][0]), term(gq[j][k][1]), term(gq[j][k][2]),
+                                         term(gq[j][k][3]), pol_keep);
                   }
                   continue;
                 }
@@ -784,13 +843,26 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
 #pragma unroll
                   for (int e = 0; e < VEC; ++e) contrib[e] = wc * g[j][e];
                 }
+                if constexpr (EXACT) {
+                  if (exact_row) {
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) contrib[e] = term(g[j][e]);
+                  }
+                }
                 if constexpr (MODE == kCounted) {
                   // A row with one hit gets its only contribution stored
                   // (rounded once, as fp32 accumulation would); rows with
                   // more hits accumulate in fp32.
-                  if (hits == 1u)
+                  if (hits == 1u) {
                     store_vec<T, VEC>(gvt + pix * rs + ch, contrib);
-                  else if constexpr (!FIXED)
+                  } else if constexpr (EXACT) {
+                    if (wide) {
+#pragma unroll
+                      for (int e = 0; e < VEC; ++e) red_fixed(faccb + pix * rs + ch + e, wd, (double)g[j][e], pol_keep);
+                    } else {
+                      red_add_vec_hint<float, VEC>(reinterpret_cast<float*>(faccb + pix * rs) + ch, contrib, pol_keep);
+                    }
+                  } else if constexpr (!FIXED)
                     red_add_vec_hint<float, VEC>(accb + pix * rs + ch, contrib, pol_keep);
                   else  // two hits: fp32 in the first half of the 64-bit row
                     red_add_vec_hint<float, VEC>(reinterpret_cast<float*>(faccb + pix * rs) + ch, contrib,
@@ -836,7 +908,7 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
             const int lead = have && __ffs(same) - 1 == lane;
             unsigned hits_me = 0u;
             if constexpr (MODE == kCounted)
-              if (lead) hits_me = dense[n] ? kDenseRow : __ldg(cnb + (int64_t)(key / QW) * p.M);
+              if (lead) hits_me = dense[n] ? kDenseRow : __ldcg(cnb + (int64_t)(key / QW) * p.M);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               const int src = grp * LPR + c;
@@ -845,12 +917,13 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
               const float w_c = __shfl_sync(kFullMask, wsum, src);
               unsigned hits_c = 0u;
               if constexpr (MODE == kCounted) hits_c = __shfl_sync(kFullMask, hits_me, src);
-              if (lead_c) scatter_row(pix_c / QW, w_c, hits_c);
+              if (lead_c) scatter_row(pix_c / QW, w_c, hits_c, 0u);
             }
           } else if (live && s < LK) {
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              if ((bl[n].valid >> c) & 1u) scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c]);
+              if ((bl[n].valid >> c) & 1u)
+                scatter_row(bl[n].pix[c], at[n] * bl[n].w[c], hits[n][c], EXACT ? rmx[EXACT ? n : 0][c] : 0u);
           }
         }
       }
@@ -930,16 +1003,83 @@ __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelI
   }
 }
 
-template <typename T, bool FUSED = false>
+// Query-heads a block of 256 points can touch (256 / (L*K) + 2).
+constexpr int kCountMaxQm = 258;
+
+// EXACT (deterministic fp16 / bf16): the dense levels are counted too, with
+// fire-and-forget `red.add`s below the dense blocks' flag (the exact scale
+// needs every row's count), and each valid corner raises its row's bound
+// p.rowmax to the bits of |a| * max|grad_out[qm, :]| (|a| <= 1 for the fused
+// softmax weights) with a `red.max`; the point blocks compute max|grad_out|
+// of their query-heads first.
+template <typename T, bool FUSED = false, bool EXACT = false>
 __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsigned point_blocks) {
   pdl_trigger();
   __shared__ LevelInfo lv[kMaxLevels];
+  __shared__ unsigned s_gmax[EXACT ? kCountMaxQm : 1];
   const int LK = p.L * p.K;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool point = blockIdx.x < point_blocks && i < p.BQM * LK;
   float2 xy = make_float2(0.f, 0.f);
   if (point) xy = load_pair(reinterpret_cast<const T*>(p.loc) + 2 * i);  // in flight across the sync
-  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);
+  float amag = 1.f;
+  int64_t qm0 = 0;
+  int nq = 0;
+  // EXACT: max |grad_out| (NaN kept) of the block's query-heads, whose rows
+  // are consecutive (nq * D elements from row qm0); the first kCountPreload
+  // 16-byte vectors of each thread are in flight across the level-table sync.
+  constexpr int V = 16 / (int)sizeof(T);
+  constexpr int kCountPreload = 2;
+  const T* g = reinterpret_cast<const T*>(p.grad_out);
+  int64_t ne = 0;
+  bool gvec = false;
+  float pmx[EXACT ? kCountPreload : 1];
+  int pq[EXACT ? kCountPreload : 1];
+  if constexpr (EXACT) {
+    if (!FUSED && point) amag = fabsf(to_f32(reinterpret_cast<const T*>(p.attn)[i]));
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x;
+    const int64_t last = min(first + (int64_t)blockDim.x, p.BQM * LK) - 1;
+    qm0 = first / LK;
+    nq = first <= last ? (int)(last / LK - qm0 + 1) : 0;
+    for (int k = threadIdx.x; k < nq; k += blockDim.x) s_gmax[k] = 0u;
+    g += qm0 * p.D;
+    ne = (int64_t)nq * p.D;
+    gvec = (reinterpret_cast<uintptr_t>(g) & 15) == 0 && p.D % V == 0;
+#pragma unroll
+    for (int k = 0; k < kCountPreload; ++k) {
+      const int64_t e = ((int64_t)k * blockDim.x + threadIdx.x) * V;
+      pq[k] = -1;
+      pmx[k] = 0.f;
+      if (gvec && e < ne) {
+        float v[V];
+        load_vec<T, V>(g + e, v);
+#pragma unroll
+        for (int q = 0; q < V; ++q) pmx[k] = max_abs_nan(pmx[k], v[q]);
+        pq[k] = (int)(e / p.D);
+      }
+    }
+  }
+  load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);  // syncs the block
+  if constexpr (EXACT) {
+#pragma unroll
+    for (int k = 0; k < kCountPreload; ++k)
+      if (pq[k] >= 0) atomicMax(s_gmax + pq[k], __float_as_uint(pmx[k]) & 0x7fffffffu);
+    if (gvec) {
+      for (int64_t e = ((int64_t)kCountPreload * blockDim.x + threadIdx.x) * V; e < ne;
+           e += (int64_t)blockDim.x * V) {
+        float v[V];
+        load_vec<T, V>(g + e, v);
+        float mx = 0.f;
+#pragma unroll
+        for (int q = 0; q < V; ++q) mx = max_abs_nan(mx, v[q]);
+        atomicMax(s_gmax + e / p.D, __float_as_uint(mx) & 0x7fffffffu);
+      }
+    } else {
+      for (int64_t e = threadIdx.x; e < ne; e += blockDim.x)
+        atomicMax(s_gmax + e / p.D, __float_as_uint(max_abs_nan(0.f, to_f32(g[e]))) & 0x7fffffffu);
+    }
+    __syncthreads();
+  }
   if (blockIdx.x >= point_blocks) {
     const int wpb = blockDim.x >> 5;
     count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * wpb + (threadIdx.x >> 5),
@@ -962,7 +1102,7 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
     m = (int)(qm % p.M);
   }
   const LevelInfo& L = lv[level_of(s, p.K, p.kshift)];
-  if (L.dense) return;
+  if (!EXACT && L.dense) return;
   Bilinear bl;
   if constexpr (FUSED) {  // offsets around the query's reference point
     const int64_t bq = qm / p.M;  // b * Q + q
@@ -976,14 +1116,33 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   for (int c = 0; c < 4; ++c) {
     old[c] = 0u;
     row[c] = (b * p.S + bl.pix[c]) * p.M + m;
-    if ((bl.valid >> c) & 1u) old[c] = atomicAdd(p.counts + row[c], 1u);
+    if ((bl.valid >> c) & 1u) {
+      if (EXACT && L.dense)  // counted below the flag; the dense blocks zero the row
+        asm volatile("red.global.add.u32 [%0], 1;" ::"l"(p.counts + row[c]) : "memory");
+      else
+        old[c] = atomicAdd(p.counts + row[c], 1u);
+    }
+  }
+  if constexpr (EXACT) {
+    // |a| * gmax: non-negative float bits order as unsigned, NaN / Inf above
+    // every finite bound
+    const unsigned bound = __float_as_uint(amag * __uint_as_float(s_gmax[qm - qm0])) & 0x7fffffffu;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if ((bl.valid >> c) & 1u)
+        asm volatile("red.global.max.u32 [%0], %1;" ::"l"(p.rowmax + row[c]), "r"(bound) : "memory");
   }
   // old == 1 only on unflagged rows: a flagged (dense) row is zeroed by the
-  // dense blocks.
+  // dense blocks. EXACT: the second hit zeroes the fp32 half of the 64-bit
+  // row, the hit that makes the row busy (old == kExactMaxHits) all of it.
+  if (L.dense) return;
 #pragma unroll
   for (int c = 0; c < 4; ++c)
-    if (((bl.valid >> c) & 1u) && old[c] == 1u)
-      zero_row(reinterpret_cast<float*>(p.acc) + row[c] * p.D * p.acc_words, p.D * p.acc_words);
+    if ((bl.valid >> c) & 1u) {
+      float* a = reinterpret_cast<float*>(p.acc) + row[c] * p.D * p.acc_words;
+      if (old[c] == 1u) zero_row(a, EXACT ? p.D : p.D * p.acc_words);
+      if (EXACT && old[c] == kExactMaxHits) zero_row(a, p.D * p.acc_words);
+    }
 }
 
 // Hit-counted scatter, pass 3: rows nothing hit become zeros; multi-hit and
@@ -992,8 +1151,12 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
 // grad_value itself is the fp32 accumulator); one-hit rows were already
 // stored by the backward.
 // One thread per 4 consecutive rows x VEC elements (one 16-byte count load).
-template <typename T, int VEC, bool FIXED = false>
-__global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p) {
+// EXACT: the accumulator rows are 64-bit; rows with 2 .. kExactMaxHits hits
+// hold integer-valued fp32 sums on the row's scale 2^F (exact_scale) in their
+// first half and are multiplied by 2^-F (exact), busier rows a 64-bit
+// integer sum (wide_scale), before the one rounding to the value dtype.
+template <typename T, int VEC, bool FIXED = false, bool EXACT = false>
+__global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const OpParams p) {
   const int D = p.D;
   const int per_row = D / VEC;
   const int64_t rows = p.B * p.S * p.M;
@@ -1001,19 +1164,28 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
   const bool in_place = !FIXED && reinterpret_cast<const void*>(p.acc) == p.grad_value;
   const bool quad_loads = (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0;
   pdl_wait();  // counts and accumulator rows come from the count pass and the backward
+  // (read with L2-coherent loads: the read-only path may hold lines cached
+  // before the kernels that wrote them finished)
   FixedScale fx{1.0, 1.f, 1.f, true};
   if constexpr (FIXED) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < quads * per_row;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t quad = t / per_row;  // rows 4*quad .. 4*quad+3
     const int chunk = (int)(t - quad * per_row);
-    unsigned cnt[4];
+    unsigned cnt[4], rmq[4];
     if (quad * 4 + 3 < rows && quad_loads) {
-      const uint4 c4 = __ldg(reinterpret_cast<const uint4*>(p.counts) + quad);
+      const uint4 c4 = __ldcg(reinterpret_cast<const uint4*>(p.counts) + quad);
       cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
+      if constexpr (EXACT) {  // the bounds sit 256-byte aligned like the counts
+        const uint4 m4 = __ldcg(reinterpret_cast<const uint4*>(p.rowmax) + quad);
+        rmq[0] = m4.x; rmq[1] = m4.y; rmq[2] = m4.z; rmq[3] = m4.w;
+      }
     } else {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) cnt[r] = quad * 4 + r < rows ? __ldg(p.counts + quad * 4 + r) : 1u;
+      for (int r = 0; r < 4; ++r) {
+        cnt[r] = quad * 4 + r < rows ? __ldcg(p.counts + quad * 4 + r) : 1u;
+        if constexpr (EXACT) rmq[r] = quad * 4 + r < rows ? __ldcg(p.rowmax + quad * 4 + r) : 0u;
+      }
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
@@ -1023,27 +1195,48 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
       if (cnt[r] == 0u) {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) v[k] = 0.f;
+      } else if constexpr (EXACT) {
+        // 64-bit rows: busy rows hold a 64-bit integer sum, the others an
+        // fp32 sum in the row's first half, integer-valued on the row's scale
+        // (plain fp32 when the scale falls back)
+        const long long* a = reinterpret_cast<const long long*>(p.acc) + e;
+        const float* f = reinterpret_cast<const float*>(a - chunk * VEC) + chunk * VEC;
+        const unsigned rm = rmq[r];
+        const unsigned nh = cnt[r] & ~kDenseRow;
+        double sc, inv;
+        if (nh > kExactMaxHits && wide_scale(rm, nh, sc, inv)) {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[k] = (float)((double)__ldcg(a + k) * inv);
+        } else {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
+          ExactScale xs;
+          if (nh <= kExactMaxHits && exact_scale(rm, nh, xs)) {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) v[k] = v[k] * xs.inv2 * xs.inv1;  // exact, but for denormal results
+          }
+        }
       } else if constexpr (FIXED) {
         const long long* a = reinterpret_cast<const long long*>(p.acc) + e;
         if (cnt[r] == 2u) {  // two hits: an fp32 row at the start of the 64-bit row
           const float* f = reinterpret_cast<const float*>(a - chunk * VEC) + chunk * VEC;
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = __ldcs(f + k);
+          for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
         } else if constexpr (VEC % 2 == 0) {
 #pragma unroll
           for (int k = 0; k < VEC; k += 2) {
-            const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(a + k));
+            const longlong2 f = __ldcg(reinterpret_cast<const longlong2*>(a + k));
             v[k] = fixed_to_f32(f.x, fx);
             v[k + 1] = fixed_to_f32(f.y, fx);
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(a + k), fx);
+          for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcg(a + k), fx);
         }
       } else if constexpr (VEC % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < VEC; k += 4) {
-          const float4 f = __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.acc) + e + k));
+          const float4 f = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.acc) + e + k));
           v[k] = f.x;
           v[k + 1] = f.y;
           v[k + 2] = f.z;
@@ -1051,7 +1244,7 @@ __global__ void __launch_bounds__(256, 8) msda_finalize_kernel(const OpParams p)
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) v[k] = __ldcs(reinterpret_cast<const float*>(p.acc) + e + k);
+        for (int k = 0; k < VEC; ++k) v[k] = __ldcg(reinterpret_cast<const float*>(p.acc) + e + k);
       }
       store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
     }
@@ -1081,7 +1274,7 @@ __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict_
     if constexpr (VEC % 4 == 0) {
 #pragma unroll
       for (int k = 0; k < VEC; k += 4) {
-        const float4 f = __ldcs(reinterpret_cast<const float4*>(src + i * VEC + k));
+        const float4 f = __ldcg(reinterpret_cast<const float4*>(src + i * VEC + k));
         v[k] = f.x;
         v[k + 1] = f.y;
         v[k + 2] = f.z;
@@ -1089,7 +1282,7 @@ __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict_
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = __ldcs(src + i * VEC + k);
+      for (int k = 0; k < VEC; ++k) v[k] = __ldcg(src + i * VEC + k);
     }
     store_vec<T, VEC>(dst + i * VEC, v);
   }
@@ -1122,7 +1315,7 @@ __device__ __forceinline__ unsigned absmax_share(const T* __restrict__ p, int64_
     for (int64_t i = tid; i < nv; i += 4 * stride) {
       uint4 r[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) r[u] = i + u * stride < nv ? __ldcs(pv + i + u * stride) : make_uint4(0, 0, 0, 0);
+      for (int u = 0; u < 4; ++u) r[u] = i + u * stride < nv ? __ldcg(pv + i + u * stride) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const T* e = reinterpret_cast<const T*>(&r[u]);
@@ -1165,13 +1358,13 @@ __global__ void __launch_bounds__(256) msda_cast_fixed_kernel(const long long* _
     if constexpr (VEC % 2 == 0) {
 #pragma unroll
       for (int k = 0; k < VEC; k += 2) {
-        const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(src + i * VEC + k));
+        const longlong2 f = __ldcg(reinterpret_cast<const longlong2*>(src + i * VEC + k));
         v[k] = fixed_to_f32(f.x, fx);
         v[k + 1] = fixed_to_f32(f.y, fx);
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(src + i * VEC + k), fx);
+      for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcg(src + i * VEC + k), fx);
     }
     store_vec<T, VEC>(dst + i * VEC, v);
   }

@@ -49,6 +49,7 @@ enum AccKind : int {
   kAccNative = 0,  // the value dtype (packed f16x2 / bf16x2 `red`)
   kAccF32 = 1,     // fp32
   kAccFixed = 2,   // 64-bit fixed point (deterministic; needs p.fixed_hdr)
+  kAccExact = 3,   // fp16 / bf16, hit-counted: fp32 rows of exact integer-valued sums (deterministic; needs p.rowmax)
 };
 
 // Backward over sampling points: grad_loc / grad_attn, plus the grad_value
@@ -66,10 +67,12 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
 // Hit-counted scatter passes 1 (count hits, zero the accumulators that will
 // be reduced into) and 3 (zeros / downcast). p.counts must be zeroed before
 // launch_count.
+// `exact`: the kAccExact counting (every level, row bounds into p.rowmax,
+// which must be zeroed too).
 template <typename T>
-cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st);
+cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, cudaStream_t st);
 template <typename T>
-cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, int num_sms, cudaStream_t st);
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, bool exact, int num_sms, cudaStream_t st);
 // Deterministic grad_value: the absmax header (pass 0; `pdl` when the kernel
 // before it is our zero-fill) and the fixed-point -> dtype pass of the
 // deterministic scatter.
@@ -204,6 +207,17 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
                             cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
   const bool fp32_scatter = acc == kAccF32;
+  if (acc == kAccExact) {
+    if constexpr (sizeof(T) == 2) {
+      if (mode != kCounted) return cudaErrorNotSupported;
+      if (p.fused)
+        return c.vec == V16 ? bwd_by_shape<T, ExactF32, V16, kCounted, true>(p, c, pdl, st) : cudaErrorNotSupported;
+      if (c.vec == V16) return bwd_by_shape<T, ExactF32, V16, kCounted>(p, c, pdl, st);
+      if (c.vec == 1) return bwd_by_shape<T, ExactF32, 1, kCounted>(p, c, pdl, st);
+      return cudaErrorInvalidConfiguration;
+    }
+    return cudaErrorNotSupported;
+  }
   if (acc == kAccFixed) {
     using F = long long;
     if (mode == kNoScatter) return cudaErrorNotSupported;
@@ -249,7 +263,7 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
 }
 
 template <typename T>
-cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
+cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, cudaStream_t st) {
   const int64_t n = p.BQM * p.L * p.K;
   const int64_t point_blocks = (n + 255) / 256;
   // The dense rows are not known on the host (the level table is on the
@@ -261,13 +275,21 @@ cudaError_t launch_count(const OpParams& p, int num_sms, cudaStream_t st) {
   const int64_t dense_blocks = std::max<int64_t>(num_sms, (int64_t)per_sm * num_sms - point_blocks);
   if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   const dim3 grid((unsigned)(point_blocks + dense_blocks));
+  if (exact) {
+    if constexpr (sizeof(T) == 2) {
+      if (p.fused) msda_count_kernel<T, true, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
+      else msda_count_kernel<T, false, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
+      return cudaGetLastError();
+    }
+    return cudaErrorNotSupported;
+  }
   if (p.fused) msda_count_kernel<T, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
   else msda_count_kernel<T><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, int num_sms, cudaStream_t st) {
+cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, bool exact, int num_sms, cudaStream_t st) {
   constexpr int V16 = 16 / (int)sizeof(T);
   const int64_t rows = p.B * p.S * p.M;
   const int vec = (vec_ok && p.D % V16 == 0 && p.D % 4 == 0) ? V16 : 1;
@@ -281,6 +303,13 @@ cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, int num_
   if (fixed) {
     if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16, true>, grid, dim3(256), 0, st, true, p);
     return launch_ex(msda_finalize_kernel<T, 1, true>, grid, dim3(256), 0, st, true, p);
+  }
+  if (exact) {
+    if constexpr (sizeof(T) == 2) {
+      if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16, false, true>, grid, dim3(256), 0, st, true, p);
+      return launch_ex(msda_finalize_kernel<T, 1, false, true>, grid, dim3(256), 0, st, true, p);
+    }
+    return cudaErrorNotSupported;
   }
   if (vec == V16) return launch_ex(msda_finalize_kernel<T, V16>, grid, dim3(256), 0, st, true, p);
   return launch_ex(msda_finalize_kernel<T, 1>, grid, dim3(256), 0, st, true, p);
@@ -346,8 +375,8 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
   template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, int, bool, cudaStream_t); \
-  template cudaError_t launch_count<T>(const OpParams&, int, cudaStream_t);                         \
-  template cudaError_t launch_finalize<T>(const OpParams&, bool, bool, int, cudaStream_t);        \
+  template cudaError_t launch_count<T>(const OpParams&, int, bool, cudaStream_t);                   \
+  template cudaError_t launch_finalize<T>(const OpParams&, bool, bool, bool, int, cudaStream_t);  \
   template cudaError_t launch_absmax<T>(const void*, int64_t, bool, const void*, int64_t, unsigned*, int, bool, cudaStream_t); \
   template cudaError_t launch_cast_fixed<T>(const long long*, T*, int64_t, bool, const unsigned*, int, int, cudaStream_t); \
   template cudaError_t launch_cast<T>(const float*, T*, int64_t, bool, int, cudaStream_t);

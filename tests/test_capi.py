@@ -106,17 +106,18 @@ def test_abi_workspace_size():
 
 
 def test_abi_workspace_size_deterministic():
-    """Deterministic grad_value: a 256-byte absmax header, then 64-bit
-    fixed-point rows -- for every grad_value element (scatter, dense
-    sampling) or behind the per-row counts (hit-counted, sparse sampling),
-    whatever the dtype and fp32_grad_accum."""
+    """Deterministic grad_value: the scatter (dense sampling) takes a 256-byte
+    absmax header, then a 64-bit fixed-point element per grad_value element;
+    the hit-counted algorithm (sparse sampling) takes per-row counts and
+    64-bit rows, with the header before the counts (fp32 values) or per-row
+    bounds after them (fp16 / bf16); whatever fp32_grad_accum says."""
     lib = _lib.load()
     d = _lib.MSDA_BWD_DETERMINISTIC
     ws = lambda Q, dt, fl: lib.msda_backward_workspace_size(2, 10, Q, 3, 8, 1, 4, dt, fl)  # noqa: E731
     elems = 2 * 10 * 3 * 8
     scatter = 256 + elems * 8
-    counted = 256 + 256 + elems * 8
     for dt in (_lib.MSDA_DTYPE_F32, _lib.MSDA_DTYPE_F16, _lib.MSDA_DTYPE_BF16):
+        counted = 256 + 256 + elems * 8  # absmax header (fp32) or row bounds (fp16 / bf16)
         for f in (0, _lib.MSDA_BWD_FP32_ACCUM):
             assert ws(50, dt, d | f) == scatter
             assert ws(2, dt, d | f) == counted
