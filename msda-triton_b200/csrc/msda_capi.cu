@@ -96,14 +96,14 @@ Algo choose_algo(const Shape& s, int32_t dtype, uint32_t flags) {
 constexpr size_t kFixedHeaderBytes = 256;
 
 // Workspace of the hit-counted scatter: [absmax header (fixed point only)]
-// per-row hit counts, [per-row bounds (exact rows only)], then one
+// per-row hit counts (exact rows: (count, bound) pairs), then one
 // accumulator row per grad_value row -- fp32 (fp16/bf16 only; fp32 values
 // accumulate in grad_value itself) or 64-bit fixed point (every dtype).
 size_t counted_ws_bytes(const Shape& s, int32_t dtype, bool fixed, bool exact, size_t* counts_offset,
                         size_t* acc_offset) {
   const size_t rows = (size_t)s.B * s.S * s.M;
   const size_t head = fixed ? kFixedHeaderBytes : 0;
-  const size_t counts = align256(rows * sizeof(unsigned)) * (exact ? 2 : 1);
+  const size_t counts = align256(rows * sizeof(unsigned) * (exact ? 2 : 1));
   *counts_offset = head;
   *acc_offset = head + counts;
   if (fixed || exact) return head + counts + rows * (size_t)s.D * sizeof(long long);
@@ -334,7 +334,7 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.grad_out = grad_output;
   p.grad_value = counted ? grad_value : target;
   p.acc_words = (fixed || exact) ? 2 : 1;
-  if (exact) p.rowmax = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + counts_off + align256(rows * sizeof(unsigned)));
+  if (exact) p.rowmax = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + counts_off) + 1;
   p.fixed_hdr = fixed_hdr;
   p.fixed_log2n = ceil_log2(s.Q * s.K);
   p.grad_loc = grad_sampling_locations;

@@ -38,7 +38,10 @@ struct OpParams {
   void* grad_attn;
   unsigned* counts;   // counted scatter: bilinear hits per (b, pixel, m) row
   void* acc;          // counted scatter: accumulator rows of the multi-hit rows
-  unsigned* rowmax;   // exact counted scatter: per-row bound of |a| * max|grad_out row|
+  // Exact counted scatter: per-row bound of |a| * max|grad_out row|, packed
+  // with the count -- (count, bound) word pairs, p.rowmax = p.counts + 1 --
+  // so one 8-byte load reads both.
+  unsigned* rowmax;
   int acc_words;      // 32-bit words per accumulator element: 1 (fp32), 2 (64-bit fixed point)
   // Deterministic grad_value (64-bit fixed point): the absmax header and
   // ceil(log2(Q*K)), the bound on contributions per row.
@@ -410,7 +413,8 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
   float* accb = reinterpret_cast<float*>(p.acc) + head_base;  // kCounted, fp32 rows
   long long* faccb = reinterpret_cast<long long*>(p.acc) + head_base;  // kCounted, fixed point
   const unsigned* cnb = p.counts + (b * p.S * p.M + m);  // kCounted: row pix at cnb[pix * M]
-  const unsigned* rmb = p.rowmax + (b * p.S * p.M + m);  // EXACT: row pix's bound at rmb[pix * M]
+  // EXACT: (count, bound) of row pix at cpb[pix * M]
+  const uint2* cpb = reinterpret_cast<const uint2*>(p.counts) + (b * p.S * p.M + m);
   const int LK = p.L * p.K;
   // Scatter: keep the reduction target in L2, let the gathered value rows go first.
   uint64_t pol_keep = 0, pol_stream = 0;
@@ -649,8 +653,13 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
           if constexpr (MODE == kCounted && !COMBINE)
             if ((bl[n].valid >> c) & 1u) {
               // (EXACT reads them too: the scale needs the count below the flag)
-              hits[n][c] = dense[n] && !EXACT ? kDenseRow : __ldcg(cnb + (int64_t)bl[n].pix[c] * p.M);
-              if constexpr (EXACT) rmx[n][c] = __ldcg(rmb + (int64_t)bl[n].pix[c] * p.M);
+              if constexpr (EXACT) {
+                const uint2 cb = __ldcg(cpb + (int64_t)bl[n].pix[c] * p.M);
+                hits[n][c] = cb.x;
+                rmx[n][c] = cb.y;
+              } else {
+                hits[n][c] = dense[n] ? kDenseRow : __ldcg(cnb + (int64_t)bl[n].pix[c] * p.M);
+              }
             }
         }
 #pragma unroll
@@ -768,11 +777,14 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
                 }
               }
             }
-            // exact rows: fl(wc 2^F1 g) (the weight's scale is exact), then
-            // the FMA applies 2^F2 and rounds to an integer
-            const float wcs = wc * xs.s1;
+            // exact rows: one FMA rounds the exact product wc 2^F g to an
+            // integer (wc 2^F is exact); a weight that 2^F would push past
+            // 2^100 (its grad_out row is tiny) is split as (wc 2^F1)(g 2^F2)
+            const float wx = wc * xs.s1 * xs.s2;
+            const bool split = !(fabsf(wx) < 0x1p100f);
+            const float wa = split ? wc * xs.s1 : wx, gb = split ? xs.s2 : 1.f;
             auto term = [&](float gv) {
-              return exact_row ? fmaf(__fmul_rn(wcs, gv), xs.s2, kExactMagic) - kExactMagic : __fmul_rn(wc, gv);
+              return exact_row ? fmaf(wa, split ? gv * gb : gv, kExactMagic) - kExactMagic : __fmul_rn(wc, gv);
             };
 #pragma unroll
             for (int j = 0; j < CPL; ++j) {
@@ -980,7 +992,7 @@ __device__ __forceinline__ int64_t dense_pixel(const LevelInfo* lv, int L, int64
 // One warp per dense pixel row (the M*D accumulator elements of all heads of
 // one pixel): flag its M counts and zero its accumulator.
 __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelInfo* lv, int64_t warp,
-                                                 int64_t nwarps) {
+                                                 int64_t nwarps, int cstride) {
   int64_t per_batch = 0;
   for (int l = 0; l < p.L; ++l)
     if (lv[l].dense) per_batch += (int64_t)lv[l].H * lv[l].W;
@@ -992,7 +1004,7 @@ __device__ __forceinline__ void count_dense_rows(const OpParams& p, const LevelI
     const int64_t b = px / per_batch;
     const int64_t pix = dense_pixel(lv, p.L, px - b * per_batch);
     const int64_t row0 = (b * p.S + pix) * p.M;  // first (b, pix, m) row
-    for (int m = lane; m < p.M; m += 32) atomicOr(p.counts + row0 + m, kDenseRow);
+    for (int m = lane; m < p.M; m += 32) atomicOr(p.counts + (row0 + m) * cstride, kDenseRow);
     float* a = reinterpret_cast<float*>(p.acc) + row0 * p.D * p.acc_words;
     if (vec) {
       for (int64_t k = lane; k < row_floats / 4; k += 32)
@@ -1061,9 +1073,21 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   }
   load_levels(p.shapes, p.starts, p.L, p.S, lv, p.Q, p.K);  // syncs the block
   if constexpr (EXACT) {
+    // A row's D / V vectors sit in consecutive lanes when D / V is a power of
+    // two up to 32 (the warp's vectors start at a multiple of 32 * V): their
+    // maxima combine by shuffles and one lane writes the row's entry.
+    const int vr = p.D / V;
+    const bool lanes = gvec && vr <= 32 && (vr & (vr - 1)) == 0;
 #pragma unroll
-    for (int k = 0; k < kCountPreload; ++k)
-      if (pq[k] >= 0) atomicMax(s_gmax + pq[k], __float_as_uint(pmx[k]) & 0x7fffffffu);
+    for (int k = 0; k < kCountPreload; ++k) {
+      if (lanes) {
+        float mx = pmx[k];
+        for (int off = 1; off < vr; off <<= 1) mx = max_abs_nan(mx, __shfl_xor_sync(kFullMask, mx, off));
+        if (pq[k] >= 0 && (threadIdx.x & (vr - 1)) == 0) s_gmax[pq[k]] = __float_as_uint(mx) & 0x7fffffffu;
+      } else if (pq[k] >= 0) {
+        atomicMax(s_gmax + pq[k], __float_as_uint(pmx[k]) & 0x7fffffffu);
+      }
+    }
     if (gvec) {
       for (int64_t e = ((int64_t)kCountPreload * blockDim.x + threadIdx.x) * V; e < ne;
            e += (int64_t)blockDim.x * V) {
@@ -1083,7 +1107,7 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
   if (blockIdx.x >= point_blocks) {
     const int wpb = blockDim.x >> 5;
     count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * wpb + (threadIdx.x >> 5),
-                     (int64_t)(gridDim.x - point_blocks) * wpb);
+                     (int64_t)(gridDim.x - point_blocks) * wpb, EXACT ? 2 : 1);
     return;
   }
   if (!point) return;
@@ -1118,9 +1142,9 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
     row[c] = (b * p.S + bl.pix[c]) * p.M + m;
     if ((bl.valid >> c) & 1u) {
       if (EXACT && L.dense)  // counted below the flag; the dense blocks zero the row
-        asm volatile("red.global.add.u32 [%0], 1;" ::"l"(p.counts + row[c]) : "memory");
+        asm volatile("red.global.add.u32 [%0], 1;" ::"l"(p.counts + 2 * row[c]) : "memory");
       else
-        old[c] = atomicAdd(p.counts + row[c], 1u);
+        old[c] = atomicAdd(p.counts + (EXACT ? 2 : 1) * row[c], 1u);
     }
   }
   if constexpr (EXACT) {
@@ -1130,7 +1154,7 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       if ((bl.valid >> c) & 1u)
-        asm volatile("red.global.max.u32 [%0], %1;" ::"l"(p.rowmax + row[c]), "r"(bound) : "memory");
+        asm volatile("red.global.max.u32 [%0], %1;" ::"l"(p.rowmax + 2 * row[c]), "r"(bound) : "memory");
   }
   // old == 1 only on unflagged rows: a flagged (dense) row is zeroed by the
   // dense blocks. EXACT: the second hit zeroes the fp32 half of the 64-bit
@@ -1174,17 +1198,21 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
     const int chunk = (int)(t - quad * per_row);
     unsigned cnt[4], rmq[4];
     if (quad * 4 + 3 < rows && quad_loads) {
-      const uint4 c4 = __ldcg(reinterpret_cast<const uint4*>(p.counts) + quad);
-      cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
-      if constexpr (EXACT) {  // the bounds sit 256-byte aligned like the counts
-        const uint4 m4 = __ldcg(reinterpret_cast<const uint4*>(p.rowmax) + quad);
-        rmq[0] = m4.x; rmq[1] = m4.y; rmq[2] = m4.z; rmq[3] = m4.w;
+      if constexpr (EXACT) {  // (count, bound) pairs
+        const uint4 a4 = __ldcg(reinterpret_cast<const uint4*>(p.counts) + 2 * quad);
+        const uint4 b4 = __ldcg(reinterpret_cast<const uint4*>(p.counts) + 2 * quad + 1);
+        cnt[0] = a4.x; rmq[0] = a4.y; cnt[1] = a4.z; rmq[1] = a4.w;
+        cnt[2] = b4.x; rmq[2] = b4.y; cnt[3] = b4.z; rmq[3] = b4.w;
+      } else {
+        const uint4 c4 = __ldcg(reinterpret_cast<const uint4*>(p.counts) + quad);
+        cnt[0] = c4.x; cnt[1] = c4.y; cnt[2] = c4.z; cnt[3] = c4.w;
       }
     } else {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        cnt[r] = quad * 4 + r < rows ? __ldcg(p.counts + quad * 4 + r) : 1u;
-        if constexpr (EXACT) rmq[r] = quad * 4 + r < rows ? __ldcg(p.rowmax + quad * 4 + r) : 0u;
+        const int64_t row = quad * 4 + r;
+        cnt[r] = row < rows ? __ldcg(p.counts + (EXACT ? 2 : 1) * row) : 1u;
+        if constexpr (EXACT) rmq[r] = row < rows ? __ldcg(p.rowmax + 2 * row) : 0u;
       }
     }
 #pragma unroll
@@ -1205,11 +1233,31 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
         const unsigned nh = cnt[r] & ~kDenseRow;
         double sc, inv;
         if (nh > kExactMaxHits && wide_scale(rm, nh, sc, inv)) {
+          if constexpr (VEC % 2 == 0) {
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = (float)((double)__ldcg(a + k) * inv);
+            for (int k = 0; k < VEC; k += 2) {
+              const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(a + k));
+              v[k] = (float)((double)w.x * inv);
+              v[k + 1] = (float)((double)w.y * inv);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) v[k] = (float)((double)__ldcg(a + k) * inv);
+          }
         } else {
+          if constexpr (VEC % 4 == 0) {
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
+            for (int k = 0; k < VEC; k += 4) {
+              const float4 w = __ldcg(reinterpret_cast<const float4*>(f + k));
+              v[k] = w.x;
+              v[k + 1] = w.y;
+              v[k + 2] = w.z;
+              v[k + 3] = w.w;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
+          }
           ExactScale xs;
           if (nh <= kExactMaxHits && exact_scale(rm, nh, xs)) {
 #pragma unroll

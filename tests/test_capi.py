@@ -117,7 +117,7 @@ def test_abi_workspace_size_deterministic():
     elems = 2 * 10 * 3 * 8
     scatter = 256 + elems * 8
     for dt in (_lib.MSDA_DTYPE_F32, _lib.MSDA_DTYPE_F16, _lib.MSDA_DTYPE_BF16):
-        counted = 256 + 256 + elems * 8  # absmax header (fp32) or row bounds (fp16 / bf16)
+        counted = 256 + 256 + elems * 8  # header + counts (fp32) or (count, bound) pairs (fp16 / bf16)
         for f in (0, _lib.MSDA_BWD_FP32_ACCUM):
             assert ws(50, dt, d | f) == scatter
             assert ws(2, dt, d | f) == counted
