@@ -46,8 +46,8 @@ def _use_fp32_grad_accum(value: torch.Tensor) -> bool:
 def _use_deterministic(deterministic: bool | None) -> bool:
     """``deterministic=None`` follows ``torch.use_deterministic_algorithms``:
     when PyTorch is asked for deterministic algorithms the backward takes the
-    library's 64-bit fixed-point grad_value accumulation (bitwise
-    reproducible) instead of raising or silently using atomics."""
+    library's order-independent grad_value accumulation (integer sums:
+    bitwise reproducible) instead of raising or silently using atomics."""
     if deterministic is None:
         return torch.are_deterministic_algorithms_enabled()
     return bool(deterministic)
@@ -225,8 +225,9 @@ def multi_scale_deformable_attention(
             (``False``). ``None`` picks fp32 for fp16/bf16 (see
             :func:`_use_fp32_grad_accum`); fp32 inputs always accumulate in
             fp32.
-        deterministic: accumulate ``grad_value`` in 64-bit fixed point so
-            the backward is bitwise reproducible (no counterpart in the
+        deterministic: accumulate ``grad_value`` as exact integer sums
+            (integer-valued fp32 rows, or 64-bit fixed point) so the backward
+            is bitwise reproducible (no counterpart in the
             reference; ``fp32_grad_accum`` is then moot). ``None`` follows
             ``torch.are_deterministic_algorithms_enabled()``.
 
