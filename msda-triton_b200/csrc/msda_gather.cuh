@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(256) transpose4_kernel(const T* __restrict__ s
     const int r = r0 + hi + k, c = c0 + 4 * lo;
     if (r < R && c < C) {
       union { V4 v; T e[4]; } u;
-      u.v = __ldcg(reinterpret_cast<const V4*>(s + r * C + c));
+      u.v = __ldcs(reinterpret_cast<const V4*>(s + r * C + c));
 #pragma unroll
       for (int e = 0; e < 4; ++e) tile[hi + k][4 * lo + e] = u.e[e];
     }
@@ -635,15 +635,15 @@ __global__ void __launch_bounds__(256) convert_transpose_kernel(const S* __restr
         const S* p = s + r * Ci + c;
         float v[4];
         if constexpr (sizeof(S) == 8) {
-          const longlong2 a = __ldcg(reinterpret_cast<const longlong2*>(p));
-          const longlong2 b = __ldcg(reinterpret_cast<const longlong2*>(p) + 1);
+          const longlong2 a = __ldcs(reinterpret_cast<const longlong2*>(p));
+          const longlong2 b = __ldcs(reinterpret_cast<const longlong2*>(p) + 1);
           v[0] = cvt(a.x); v[1] = cvt(a.y); v[2] = cvt(b.x); v[3] = cvt(b.y);
         } else if constexpr (sizeof(S) == 4) {
-          const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+          const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
           v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
         } else {
           union { uint2 u; S e[4]; } a;
-          a.u = __ldcg(reinterpret_cast<const uint2*>(p));
+          a.u = __ldcs(reinterpret_cast<const uint2*>(p));
 #pragma unroll
           for (int e = 0; e < 4; ++e) v[e] = cvt(a.e[e]);
         }
@@ -667,7 +667,7 @@ __global__ void __launch_bounds__(256) convert_transpose_kernel(const S* __restr
 #pragma unroll
     for (int k = 0; k < TL; k += 4) {
       const int64_t r = r0 + ty + k, c = c0 + tx;
-      if (r < R && c < C) tile[ty + k][tx] = cvt(__ldcg(s + r * C + c));
+      if (r < R && c < C) tile[ty + k][tx] = cvt(__ldcs(s + r * C + c));
     }
     __syncthreads();
 #pragma unroll

@@ -648,8 +648,9 @@ __global__ void __launch_bounds__(WARPS * 32, (MODE == kCounted ? MSDA_BWD_COUNT
           // Dense-level rows are always reduced in fp32: no count to read.
           // Counts and bounds come from the kernel before this one, which may
           // still run when this kernel starts (programmatic dependent
-          // launch): L2-coherent loads, not the read-only path, which would
-          // serve lines that were cached before it finished.
+          // launch): ordinary (L2) loads, never the read-only `__ldg` path,
+          // whose loads the compiler treats as invariant and may issue before
+          // pdl_wait().
           if constexpr (MODE == kCounted && !COMBINE)
             if ((bl[n].valid >> c) & 1u) {
               // (EXACT reads them too: the scale needs the count below the flag)
@@ -1188,8 +1189,8 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
   const bool in_place = !FIXED && reinterpret_cast<const void*>(p.acc) == p.grad_value;
   const bool quad_loads = (reinterpret_cast<uintptr_t>(p.counts) & 15) == 0;
   pdl_wait();  // counts and accumulator rows come from the count pass and the backward
-  // (read with L2-coherent loads: the read-only path may hold lines cached
-  // before the kernels that wrote them finished)
+  // (ordinary loads, never the read-only `__ldg` path: the compiler treats
+  // those as invariant and may issue them before the wait)
   FixedScale fx{1.0, 1.f, 1.f, true};
   if constexpr (FIXED) fx = fixed_scale(p.fixed_hdr, p.fixed_log2n);
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < quads * per_row;
@@ -1236,19 +1237,19 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
           if constexpr (VEC % 2 == 0) {
 #pragma unroll
             for (int k = 0; k < VEC; k += 2) {
-              const longlong2 w = __ldcg(reinterpret_cast<const longlong2*>(a + k));
+              const longlong2 w = __ldcs(reinterpret_cast<const longlong2*>(a + k));
               v[k] = (float)((double)w.x * inv);
               v[k + 1] = (float)((double)w.y * inv);
             }
           } else {
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) v[k] = (float)((double)__ldcg(a + k) * inv);
+            for (int k = 0; k < VEC; ++k) v[k] = (float)((double)__ldcs(a + k) * inv);
           }
         } else {
           if constexpr (VEC % 4 == 0) {
 #pragma unroll
             for (int k = 0; k < VEC; k += 4) {
-              const float4 w = __ldcg(reinterpret_cast<const float4*>(f + k));
+              const float4 w = __ldcs(reinterpret_cast<const float4*>(f + k));
               v[k] = w.x;
               v[k + 1] = w.y;
               v[k + 2] = w.z;
@@ -1256,7 +1257,7 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
             }
           } else {
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
+            for (int k = 0; k < VEC; ++k) v[k] = __ldcs(f + k);
           }
           ExactScale xs;
           if (nh <= kExactMaxHits && exact_scale(rm, nh, xs)) {
@@ -1269,22 +1270,22 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
         if (cnt[r] == 2u) {  // two hits: an fp32 row at the start of the 64-bit row
           const float* f = reinterpret_cast<const float*>(a - chunk * VEC) + chunk * VEC;
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = __ldcg(f + k);
+          for (int k = 0; k < VEC; ++k) v[k] = __ldcs(f + k);
         } else if constexpr (VEC % 2 == 0) {
 #pragma unroll
           for (int k = 0; k < VEC; k += 2) {
-            const longlong2 f = __ldcg(reinterpret_cast<const longlong2*>(a + k));
+            const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(a + k));
             v[k] = fixed_to_f32(f.x, fx);
             v[k + 1] = fixed_to_f32(f.y, fx);
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcg(a + k), fx);
+          for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(a + k), fx);
         }
       } else if constexpr (VEC % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < VEC; k += 4) {
-          const float4 f = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.acc) + e + k));
+          const float4 f = __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.acc) + e + k));
           v[k] = f.x;
           v[k + 1] = f.y;
           v[k + 2] = f.z;
@@ -1292,7 +1293,7 @@ __global__ void __launch_bounds__(256, EXACT ? 6 : 8) msda_finalize_kernel(const
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) v[k] = __ldcg(reinterpret_cast<const float*>(p.acc) + e + k);
+        for (int k = 0; k < VEC; ++k) v[k] = __ldcs(reinterpret_cast<const float*>(p.acc) + e + k);
       }
       store_vec<T, VEC>(reinterpret_cast<T*>(p.grad_value) + e, v);
     }
@@ -1322,7 +1323,7 @@ __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict_
     if constexpr (VEC % 4 == 0) {
 #pragma unroll
       for (int k = 0; k < VEC; k += 4) {
-        const float4 f = __ldcg(reinterpret_cast<const float4*>(src + i * VEC + k));
+        const float4 f = __ldcs(reinterpret_cast<const float4*>(src + i * VEC + k));
         v[k] = f.x;
         v[k + 1] = f.y;
         v[k + 2] = f.z;
@@ -1330,7 +1331,7 @@ __global__ void __launch_bounds__(256) msda_cast_kernel(const float* __restrict_
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = __ldcg(src + i * VEC + k);
+      for (int k = 0; k < VEC; ++k) v[k] = __ldcs(src + i * VEC + k);
     }
     store_vec<T, VEC>(dst + i * VEC, v);
   }
@@ -1363,7 +1364,7 @@ __device__ __forceinline__ unsigned absmax_share(const T* __restrict__ p, int64_
     for (int64_t i = tid; i < nv; i += 4 * stride) {
       uint4 r[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) r[u] = i + u * stride < nv ? __ldcg(pv + i + u * stride) : make_uint4(0, 0, 0, 0);
+      for (int u = 0; u < 4; ++u) r[u] = i + u * stride < nv ? __ldcs(pv + i + u * stride) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const T* e = reinterpret_cast<const T*>(&r[u]);
@@ -1406,13 +1407,13 @@ __global__ void __launch_bounds__(256) msda_cast_fixed_kernel(const long long* _
     if constexpr (VEC % 2 == 0) {
 #pragma unroll
       for (int k = 0; k < VEC; k += 2) {
-        const longlong2 f = __ldcg(reinterpret_cast<const longlong2*>(src + i * VEC + k));
+        const longlong2 f = __ldcs(reinterpret_cast<const longlong2*>(src + i * VEC + k));
         v[k] = fixed_to_f32(f.x, fx);
         v[k + 1] = fixed_to_f32(f.y, fx);
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcg(src + i * VEC + k), fx);
+      for (int k = 0; k < VEC; ++k) v[k] = fixed_to_f32(__ldcs(src + i * VEC + k), fx);
     }
     store_vec<T, VEC>(dst + i * VEC, v);
   }

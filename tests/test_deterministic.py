@@ -107,6 +107,20 @@ def test_deterministic_at_the_decoder_operating_point(dtype):
     assert _bitwise_equal(got[0], gvp)
 
 
+@pytest.mark.parametrize("name,kw,lo,hi", ALGO_CASES[:1] + [c for c in ALGO_CASES if c[0] == "dense_local_d64"],
+                         ids=["decoder_case", "dense_local_d64"])
+def test_deterministic_repeated_calls(name, kw, lo, hi):
+    """Many back-to-back calls on one stream: every kernel of a call starts
+    while the one before it still runs (programmatic dependent launch), so
+    each must read what its predecessors wrote through coherent loads. A
+    stale read shows as an occasional run with different bits (it did, about
+    one run in ten, before the counts and row bounds were read that way)."""
+    value, shapes, starts, loc, attn, g = _inputs(kw, lo, hi, torch.bfloat16, seed=3)
+    first = _ops._backward(value, shapes, starts, loc, attn, g, True, DET)[0]
+    for _ in range(24):
+        assert _bitwise_equal(first, _ops._backward(value, shapes, starts, loc, attn, g, True, DET)[0])
+
+
 def test_deterministic_at_the_encoder_operating_point():
     """Full-size encoder (Q = S = 22223 per item, dense local sampling; the
     merged fixed-point scatter): bitwise equal across runs and under a query

@@ -610,6 +610,24 @@ def test_counted_scatter_matches_fp32_accumulation(dtype):
     torch.testing.assert_close(got[2], ref[2])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=str)
+def test_counted_backward_repeated_calls(dtype):
+    """The hit-counted backward's passes (count, backward, finalize) overlap
+    their predecessors' tails; each reads the counts and accumulator rows
+    that the passes before it wrote. Many back-to-back calls must all stay
+    at the strict bar (a stale count would store a row instead of reducing
+    it, or skip a zero fill)."""
+    kw, lo, hi = ALGO_CASES[0][1], ALGO_CASES[0][2], ALGO_CASES[0][3]
+    value, shapes, starts, loc, attn = cases.make_inputs(**kw, dtype=dtype, device=DEV, loc_lo=lo, loc_hi=hi)
+    B, Q, M, D = value.shape[0], loc.shape[1], value.shape[2], value.shape[3]
+    g = cases.grad_output_like(torch.empty(B, Q, M, D, device=DEV, dtype=dtype))
+    _, ref = oracle64(value, shapes, starts, loc, attn, g)
+    runs = [_ops._backward(value, shapes, starts, loc, attn, g, True, _clib.MSDA_BWD_FORCE_COUNTED)
+            for _ in range(16)]
+    for got in runs:
+        cases.assert_grads_close(got, ref, loc, shapes, STRICT_TOL[dtype], what="counted/repeated")
+
+
 # ---------------------------------------------------------------------------
 # Fused prologue: reference points + offsets (level pixels), attention logits
 # ---------------------------------------------------------------------------
