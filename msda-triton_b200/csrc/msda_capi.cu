@@ -288,15 +288,18 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   const size_t rows = (size_t)s.B * s.S * s.M;
   if (counted) {
     counted_ws_bytes(s, dtype, fixed, exact, &counts_off, &acc_off);
-    // Counts (and the absmax header before them, the row bounds after them).
-    e = cudaMemsetAsync(workspace, 0, exact ? acc_off : counts_off + rows * sizeof(unsigned), st);
+    // Counts (and the absmax header before them, the row bounds after them),
+    // zeroed by our kernel (padded to 16 bytes inside the 256-byte-aligned
+    // count region) so the passes behind it can start under its tail.
+    const size_t zbytes = ((exact ? acc_off : counts_off + rows * sizeof(unsigned)) + 15) / 16 * 16;
+    e = msda::launch_zero(workspace, zbytes, sm_count(), st);
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count zero-fill");
   }
   // The backward may overlap the tail of the kernel before it when that
   // kernel is ours (the hit count, the zero-fill kernel or the absmax pass;
   // not a memset).
   bool bwd_pdl = counted;
-  bool zero_kernel = false;
+  bool zero_kernel = counted;
   if (!counted) {
     // The deterministic scatter zeroes the header with the accumulator.
     void* zdst = algo == Algo::kScatterFixed ? workspace : target;
@@ -350,9 +353,10 @@ static int backward_impl(const char* fn, const void* value, const int64_t* spati
   p.BQM = s.B * s.Q * s.M;
   if (counted) {
     switch (dtype) {
-      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, sm_count(), exact, st); break;
-      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, sm_count(), exact, st); break;
-      default: e = msda::launch_count<__nv_bfloat16>(p, sm_count(), exact, st); break;
+      // behind the zero-fill, or behind the absmax pass that follows it
+      case MSDA_DTYPE_F32: e = msda::launch_count<float>(p, sm_count(), exact, true, st); break;
+      case MSDA_DTYPE_F16: e = msda::launch_count<__half>(p, sm_count(), exact, true, st); break;
+      default: e = msda::launch_count<__nv_bfloat16>(p, sm_count(), exact, true, st); break;
     }
     if (e != cudaSuccess) return cuda_fail(e, "msda_backward hit-count launch");
   }

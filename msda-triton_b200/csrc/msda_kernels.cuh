@@ -1105,6 +1105,9 @@ __global__ void __launch_bounds__(256) msda_count_kernel(const OpParams p, unsig
     }
     __syncthreads();
   }
+  // Counts (and the absmax header) are zeroed by the kernel before this one:
+  // everything above ran under its tail; nothing below may precede it.
+  pdl_wait();
   if (blockIdx.x >= point_blocks) {
     const int wpb = blockDim.x >> 5;
     count_dense_rows(p, lv, (int64_t)(blockIdx.x - point_blocks) * wpb + (threadIdx.x >> 5),

@@ -69,8 +69,11 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
 // launch_count.
 // `exact`: the kAccExact counting (every level, row bounds into p.rowmax,
 // which must be zeroed too).
+// `pdl`: the kernel before it is ours (the zero-fill of the counts or the
+// absmax pass): the count pass loads and resolves its points under that
+// kernel's tail and waits before its first count or accumulator write.
 template <typename T>
-cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, cudaStream_t st);
+cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, bool pdl, cudaStream_t st);
 template <typename T>
 cudaError_t launch_finalize(const OpParams& p, bool vec_ok, bool fixed, bool exact, int num_sms, cudaStream_t st);
 // Deterministic grad_value: the absmax header (pass 0; `pdl` when the kernel
@@ -263,7 +266,7 @@ cudaError_t launch_backward(const OpParams& p, const Cfg& c, int mode, int acc, 
 }
 
 template <typename T>
-cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, cudaStream_t st) {
+cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, bool pdl, cudaStream_t st) {
   const int64_t n = p.BQM * p.L * p.K;
   const int64_t point_blocks = (n + 255) / 256;
   // The dense rows are not known on the host (the level table is on the
@@ -275,17 +278,16 @@ cudaError_t launch_count(const OpParams& p, int num_sms, bool exact, cudaStream_
   const int64_t dense_blocks = std::max<int64_t>(num_sms, (int64_t)per_sm * num_sms - point_blocks);
   if (point_blocks + dense_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   const dim3 grid((unsigned)(point_blocks + dense_blocks));
+  const unsigned pb = (unsigned)point_blocks;
   if (exact) {
     if constexpr (sizeof(T) == 2) {
-      if (p.fused) msda_count_kernel<T, true, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
-      else msda_count_kernel<T, false, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
-      return cudaGetLastError();
+      if (p.fused) return launch_ex(msda_count_kernel<T, true, true>, grid, dim3(256), 0, st, pdl, p, pb);
+      return launch_ex(msda_count_kernel<T, false, true>, grid, dim3(256), 0, st, pdl, p, pb);
     }
     return cudaErrorNotSupported;
   }
-  if (p.fused) msda_count_kernel<T, true><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
-  else msda_count_kernel<T><<<grid, 256, 0, st>>>(p, (unsigned)point_blocks);
-  return cudaGetLastError();
+  if (p.fused) return launch_ex(msda_count_kernel<T, true>, grid, dim3(256), 0, st, pdl, p, pb);
+  return launch_ex(msda_count_kernel<T>, grid, dim3(256), 0, st, pdl, p, pb);
 }
 
 template <typename T>
@@ -375,7 +377,7 @@ cudaError_t launch_zero(void* dst, size_t bytes, int num_sms, cudaStream_t st) {
 #define MSDA_INSTANTIATE(T)                                                                       \
   template cudaError_t launch_forward<T>(const OpParams&, const Cfg&, cudaStream_t);              \
   template cudaError_t launch_backward<T>(const OpParams&, const Cfg&, int, int, bool, cudaStream_t); \
-  template cudaError_t launch_count<T>(const OpParams&, int, bool, cudaStream_t);                   \
+  template cudaError_t launch_count<T>(const OpParams&, int, bool, bool, cudaStream_t);             \
   template cudaError_t launch_finalize<T>(const OpParams&, bool, bool, bool, int, cudaStream_t);  \
   template cudaError_t launch_absmax<T>(const void*, int64_t, bool, const void*, int64_t, unsigned*, int, bool, cudaStream_t); \
   template cudaError_t launch_cast_fixed<T>(const long long*, T*, int64_t, bool, const unsigned*, int, int, cudaStream_t); \
